@@ -1,0 +1,784 @@
+"""Benchmark of the CUDA provider on BASELINE.json's configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+    python bench.py --impl reference ...      # the reference CPU provider
+
+Default workload: configs[1] of BASELINE.json, softmax + row max/argmax
+(TOP_K k=1) over F32 [32768,1024], logits N(0,3^2) with 1% set to +20, as
+one m3 graph (SOFTMAX and TOP_K of one input).  One step = one session run
+over one batch.  Multi-GPU runs shard by independent batches (rows) with no
+data-path collective: every rank runs a full batch ("weak" scaling) and
+`value` is the whole-job throughput.  --config c1..c5 select the other
+configurations (c5 all-reduces its abs-max across ranks with NCCL).
+
+Metric: achieved HBM GB/s = algorithmic bytes (each input read once, each
+graph output written once) / device time.  Inputs are generated on the device
+from the reference's seeded PCG32 streams and are resident in HBM before the
+timed region; a 256 MiB buffer is overwritten between timed steps so no step
+starts from a warm L2.  `e2e` repeats the measurement through the public C
+API with host buffers: pinned host -> device input writes, the run, and
+device -> pinned host output reads inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _module(name: str, path: str):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    module = importlib.util.module_from_spec(spec)
+    sys.modules[name] = module
+    spec.loader.exec_module(module)
+    return module
+
+
+def m3mod():
+    return _module("m3cuda", os.path.join(ROOT, "m3.c_b200", "m3cuda.py"))
+
+
+def oraclemod():
+    return _module("m3_oracle_py", os.path.join(ROOT, "oracle", "oracle.py"))
+
+
+METRIC = ("achieved HBM GB/s (fraction of B200 peak) per op; "
+          "elems/s at 1/2/4/8 GPUs vs CPU")
+
+
+# ---------------------------------------------------------------- configs
+
+class Config:
+    """One benchmark graph: builder, seeded inputs, algorithmic bytes."""
+
+    name = ""
+    workload = ""
+    dtype = "f32"
+    runs_per_step = 1
+
+    def build(self, m3, g, scale: float = 1.0):  # -> (inputs {name: vid}, outputs [vid])
+        raise NotImplementedError
+
+    def inputs_host(self, m3, oracle, scale: float = 1.0):  # -> {name: ndarray}
+        raise NotImplementedError
+
+    def algorithmic_bytes(self, scale: float = 1.0) -> int:
+        raise NotImplementedError
+
+    def elements(self, scale: float = 1.0) -> int:
+        raise NotImplementedError
+
+
+class C2(Config):
+    name = "c2"
+    workload = ("softmax + row max/argmax (TOP_K k=1) F32 [32768,1024], "
+                "N(0,3^2) logits with 1% = +20, seed 1")
+    rows, width = 32768, 1024
+
+    def shape(self, scale):
+        return (max(1, int(self.rows * scale)), self.width)
+
+    def build(self, m3, g, scale=1.0):
+        shape = self.shape(scale)
+        x = g.value(m3.INPUT, m3.F32, shape)
+        p = g.inferred("SOFTMAX", [x], m3.OUTPUT, m3.F32)
+        g.node("SOFTMAX", [x], [p])
+        v = g.inferred("TOP_K", [x], m3.OUTPUT, m3.F32, 0, k=1)
+        i = g.inferred("TOP_K", [x], m3.OUTPUT, m3.I32, 1, k=1)
+        g.node("TOP_K", [x], [v, i], k=1)
+        return {"x": x}, [p, v, i]
+
+    def inputs_host(self, m3, oracle, scale=1.0):
+        shape = self.shape(scale)
+        n = shape[0] * shape[1]
+        x = m3.fill_normal(1, 0, 0.0, 3.0, n)
+        spikes = m3.fill_uniform(1, 1, 0.0, 1.0, n) < 0.01
+        x[spikes] = 20.0
+        return {"x": x.reshape(shape)}
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        shape = self.shape(scale)
+        n = shape[0] * shape[1]
+        x = torch.empty(n, dtype=torch.float32, device=device)
+        u = torch.empty(n, dtype=torch.float32, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        fill(m3, "normal", 1, 0, 0.0, 3.0, x, stream)
+        fill(m3, "uniform", 1, 1, 0.0, 1.0, u, stream)
+        x[u < 0.01] = 20.0
+        return {"x": x.view(shape)}
+
+    def algorithmic_bytes(self, scale=1.0):
+        rows, width = self.shape(scale)
+        return rows * width * 4 * 2 + rows * 4 * 2
+
+    def elements(self, scale=1.0):
+        rows, width = self.shape(scale)
+        return rows * width
+
+
+class C1(Config):
+    name = "c1"
+    workload = "y = (x * c) + b F32 [1024,4096], c [4096] / b [1,4096] constants, seed 0"
+    rows, width = 1024, 4096
+
+    def build(self, m3, g, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        c = m3.fill_uniform(0, 1, 0.5, 2.0, self.width)
+        b = m3.fill_normal(0, 2, 0.0, 1.0, self.width).reshape(1, self.width)
+        x = g.value(m3.INPUT, m3.F32, (rows, self.width))
+        vc = g.constant(m3.F32, c)
+        vb = g.constant(m3.F32, b)
+        t = g.inferred("MUL", [x, vc], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [x, vc], [t])
+        y = g.inferred("ADD", [t, vb], m3.OUTPUT, m3.F32)
+        g.node("ADD", [t, vb], [y])
+        return {"x": x}, [y]
+
+    def inputs_host(self, m3, oracle, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        return {"x": m3.fill_uniform(0, 0, -1.0, 1.0, rows * self.width).reshape(rows, self.width)}
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        x = torch.empty(rows * self.width, dtype=torch.float32, device=device)
+        fill(m3, "uniform", 0, 0, -1.0, 1.0, x, torch.cuda.current_stream(device).cuda_stream)
+        return {"x": x.view(rows, self.width)}
+
+    def algorithmic_bytes(self, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        return rows * self.width * 8 + 2 * self.width * 4
+
+    def elements(self, scale=1.0):
+        return max(1, int(self.rows * scale)) * self.width
+
+
+class C3(Config):
+    name = "c3"
+    dtype = "f16"
+    workload = ("F16 residual add + RMSNorm [8192,2048] (eps 1e-6, w N(1,0.05)) "
+                "and SiLU(gate)*up [8192,5632], seed 2")
+    rows, width, ffn = 8192, 2048, 5632
+
+    def build(self, m3, g, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        w = f16_bits(m3.fill_normal(2, 2, 1.0, 0.05, self.width))
+        h = g.value(m3.INPUT, m3.F16, (rows, self.width))
+        r = g.value(m3.INPUT, m3.F16, (rows, self.width))
+        vw = g.constant(m3.F16, w)
+        gate = g.value(m3.INPUT, m3.F16, (rows, self.ffn))
+        up = g.value(m3.INPUT, m3.F16, (rows, self.ffn))
+        s = g.inferred("ADD", [h, r], m3.OUTPUT, m3.F16)
+        g.node("ADD", [h, r], [s])
+        n = g.inferred("RMS_NORM", [s, vw], m3.OUTPUT, m3.F16, epsilon=1e-6)
+        g.node("RMS_NORM", [s, vw], [n], epsilon=1e-6)
+        y = g.inferred("GATED_SILU", [gate, up], m3.OUTPUT, m3.F16)
+        g.node("GATED_SILU", [gate, up], [y])
+        return {"h": h, "r": r, "gate": gate, "up": up}, [s, n, y]
+
+    def _sizes(self, scale):
+        rows = max(1, int(self.rows * scale))
+        return {"h": (rows, self.width, 0), "r": (rows, self.width, 1),
+                "gate": (rows, self.ffn, 3), "up": (rows, self.ffn, 4)}
+
+    def inputs_host(self, m3, oracle, scale=1.0):
+        out = {}
+        for name, (rows, cols, seq) in self._sizes(scale).items():
+            out[name] = f16_bits(m3.fill_normal(2, seq, 0.0, 1.0, rows * cols)).reshape(rows, cols)
+        return out
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        out = {}
+        stream = torch.cuda.current_stream(device).cuda_stream
+        for name, (rows, cols, seq) in self._sizes(scale).items():
+            tmp = torch.empty(rows * cols, dtype=torch.float32, device=device)
+            fill(m3, "normal", 2, seq, 0.0, 1.0, tmp, stream)
+            out[name] = device_cast_f16(m3, tmp, device).view(rows, cols)
+            del tmp
+        return out
+
+    def algorithmic_bytes(self, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        return (rows * self.width * 2 * 4 + self.width * 2 + rows * self.ffn * 2 * 3)
+
+    def elements(self, scale=1.0):
+        rows = max(1, int(self.rows * scale))
+        return rows * (self.width + self.ffn)
+
+
+class C4(Config):
+    name = "c4"
+    workload = ("flow-matching CFG + Euler step, F32 [2,64,8192], g = 4, dt = 1/30, "
+                "then BF16 cast; 30 steps carried on device; seed 3")
+    shape3 = (2, 64, 8192)
+    runs_per_step = 30
+
+    def build(self, m3, g, scale=1.0):
+        shape = self.shape3
+        x = g.value(m3.INPUT, m3.F32, shape)
+        vc = g.value(m3.INPUT, m3.F32, shape)
+        vu = g.value(m3.INPUT, m3.F32, shape)
+        k1 = g.constant(m3.F32, np.array([-1.0], np.float32))
+        kg = g.constant(m3.F32, np.array([4.0], np.float32))
+        kd = g.constant(m3.F32, np.array([np.float32(1.0) / np.float32(30.0)], np.float32))
+        a = g.inferred("MUL", [vu, k1], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [vu, k1], [a])
+        a2 = g.inferred("ADD", [vc, a], m3.TEMPORARY, m3.F32)
+        g.node("ADD", [vc, a], [a2])
+        a3 = g.inferred("MUL", [a2, kg], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [a2, kg], [a3])
+        v = g.inferred("ADD", [vu, a3], m3.TEMPORARY, m3.F32)
+        g.node("ADD", [vu, a3], [v])
+        t = g.inferred("MUL", [v, kd], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [v, kd], [t])
+        xn = g.inferred("ADD", [x, t], m3.OUTPUT, m3.F32)
+        g.node("ADD", [x, t], [xn])
+        xb = g.inferred("CAST", [xn], m3.OUTPUT, m3.BF16)
+        g.node("CAST", [xn], [xb])
+        self.carry = (x, xn)
+        return {"x": x, "vc": vc, "vu": vu}, [xn, xb]
+
+    def inputs_host(self, m3, oracle, scale=1.0):
+        n = int(np.prod(self.shape3))
+        return {name: m3.fill_normal(3, seq, 0.0, 1.0, n).reshape(self.shape3)
+                for seq, name in enumerate(("x", "vc", "vu"))}
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        n = int(np.prod(self.shape3))
+        stream = torch.cuda.current_stream(device).cuda_stream
+        out = {}
+        for seq, name in enumerate(("x", "vc", "vu")):
+            t = torch.empty(n, dtype=torch.float32, device=device)
+            fill(m3, "normal", 3, seq, 0.0, 1.0, t, stream)
+            out[name] = t.view(self.shape3)
+        return out
+
+    def algorithmic_bytes(self, scale=1.0):
+        n = int(np.prod(self.shape3))
+        return 30 * (n * 4 * 3 + n * 4 + n * 2)
+
+    def elements(self, scale=1.0):
+        return 30 * int(np.prod(self.shape3))
+
+
+class C5(Config):
+    name = "c5"
+    workload = ("snake x + sin^2(a x)/a on stereo F32 [2,512,1572864], a U[0.2,2], "
+                "x N(0,0.5); global abs-max (NCCL all-reduce across ranks) and clamp "
+                "to [-1,1]; seed 4")
+    batch, channels, length = 2, 512, 1572864
+
+    def build(self, m3, g, scale=1.0):
+        length = max(4, int(self.length * scale) // 4 * 4)
+        alpha = m3.fill_uniform(4, 1, 0.2, 2.0, self.channels).reshape(1, self.channels, 1)
+        x = g.value(m3.INPUT, m3.F32, (self.batch, self.channels, length))
+        va = g.constant(m3.F32, alpha)
+        z = g.inferred("SNAKE1D", [x, va], m3.TEMPORARY, m3.F32)
+        g.node("SNAKE1D", [x, va], [z])
+        m = g.inferred("ABS_MAX", [z], m3.OUTPUT, m3.F32)
+        g.node("ABS_MAX", [z], [m])
+        y = g.inferred("CLAMP_UNIT", [z], m3.OUTPUT, m3.F32)
+        g.node("CLAMP_UNIT", [z], [y])
+        return {"x": x}, [m, y]
+
+    def _length(self, scale):
+        return max(4, int(self.length * scale) // 4 * 4)
+
+    def inputs_host(self, m3, oracle, scale=1.0):
+        n = self.batch * self.channels * self._length(scale)
+        return {"x": m3.fill_normal(4, 0, 0.0, 0.5, n).reshape(
+            self.batch, self.channels, self._length(scale))}
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        n = self.batch * self.channels * self._length(scale)
+        x = torch.empty(n, dtype=torch.float32, device=device)
+        fill(m3, "normal", 4, 0, 0.0, 0.5, x, torch.cuda.current_stream(device).cuda_stream)
+        return {"x": x.view(self.batch, self.channels, self._length(scale))}
+
+    def algorithmic_bytes(self, scale=1.0):
+        n = self.batch * self.channels * self._length(scale)
+        return n * 8 + self.channels * 4 + 4
+
+    def elements(self, scale=1.0):
+        return self.batch * self.channels * self._length(scale)
+
+
+CONFIGS = {c.name: c for c in (C1(), C2(), C3(), C4(), C5())}
+
+
+# ------------------------------------------------------------- helpers
+
+def f16_bits(values: np.ndarray) -> np.ndarray:
+    """F32 -> F16 bits with the reference's RN-even encoder (exact integer
+    restatement; vectorised in numpy for input preparation)."""
+    b = np.ascontiguousarray(values, np.float32).view(np.uint32).astype(np.uint64)
+    sign = ((b >> 16) & 0x8000).astype(np.uint64)
+    exp = ((b >> 23) & 0xFF).astype(np.int64)
+    frac = (b & 0x7FFFFF).astype(np.uint64)
+    e = exp - 127
+    out = np.zeros(b.shape, np.uint64)
+    normal = (e >= -14) & (e <= 15)
+    half = ((np.clip(e + 15, 0, 31).astype(np.uint64)) << 10) | (frac >> 13)
+    rest = frac & 0x1FFF
+    up = (rest > 0x1000) | ((rest == 0x1000) & ((half & 1) == 1))
+    half = half + up.astype(np.uint64)
+    half = np.where(half >= 0x7C00, 0x7C00, half)
+    out = np.where(normal, half, out)
+    sub = (e >= -25) & (e < -14)
+    shift = np.clip(-e - 1, 1, 63).astype(np.uint64)
+    sig = 0x800000 | frac
+    kept = sig >> shift
+    remainder = sig & ((np.uint64(1) << shift) - 1)
+    halfway = np.uint64(1) << (shift - 1)
+    kept = kept + ((remainder > halfway) | ((remainder == halfway) & ((kept & 1) == 1))).astype(np.uint64)
+    out = np.where(sub, kept, out)
+    out = np.where(e > 15, 0x7C00, out)
+    nan = (exp == 0xFF) & (frac != 0)
+    payload = frac >> 13
+    out = np.where(nan, 0x7E00 | payload | (payload == 0).astype(np.uint64), out)
+    out = np.where((exp == 0xFF) & (frac == 0), 0x7C00, out)
+    return (out | sign).astype(np.uint16)
+
+
+def fill(m3, kind, seed, sequence, a, b, tensor, stream):
+    lib = m3.load()
+    err = m3.M3Error()
+    fn = lib.m3_cuda_fill_normal_device if kind == "normal" else lib.m3_cuda_fill_uniform_device
+    m3.check(fn(seed, sequence, a, b, ctypes.c_void_p(tensor.data_ptr()), tensor.numel(),
+                ctypes.c_void_p(stream), ctypes.byref(err)), err)
+
+
+def device_cast_f16(m3, tensor, device):
+    """F32 -> F16 on the device with the library's CAST (reference codec)."""
+    import torch
+    n = tensor.numel()
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (n,))
+    y = g.inferred("CAST", [x], m3.OUTPUT, m3.F16)
+    g.node("CAST", [x], [y])
+    s = m3.Session(g, device=device.index,
+                   stream=torch.cuda.current_stream(device).cuda_stream)
+    s.write_device(x, tensor.data_ptr(), n * 4)
+    s.run()
+    out = torch.empty(n, dtype=torch.int16, device=device)
+    s.read_device(y, out.data_ptr(), n * 2)
+    s.close()
+    return out
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        data = json.load(open(path))
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(config_name: str):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(path):
+        return None
+    data = json.load(open(path))
+    entry = data.get(config_name)
+    return None if entry is None else entry.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.index = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------- reference arm
+
+def reference_seconds_per_run(m3, oracle, config, scale, threads):
+    """Run the reference CPU provider on `threads` independent row shards in
+    parallel threads (ctypes releases the GIL); returns seconds per run of
+    the scaled workload."""
+    lib = m3.bind(oracle.reference(), cuda=False)
+    sessions = []
+    per = scale / threads
+    for t in range(threads):
+        g = m3.Graph(lib=lib)
+        handles, outputs = config.build(m3, g, per)
+        s = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
+        data = config.inputs_host(m3, oracle, per)
+        for name, vid in handles.items():
+            s.write(vid, data[name])
+        sessions.append(s)
+
+    def run(s, repeat):
+        for _ in range(repeat):
+            s.run()
+
+    run(sessions[0], 1)  # warm
+    start = time.perf_counter()
+    workers = [threading.Thread(target=run, args=(s, config.runs_per_step)) for s in sessions]
+    for w in workers:
+        w.start()
+    for w in workers:
+        w.join()
+    return (time.perf_counter() - start)
+
+
+def cpu_baseline(m3, oracle, config, budget_seconds):
+    """Single-core reference CPU provider on a bounded sample (rank 0, N=1)."""
+    if not oracle.reference_available():
+        return None
+    probe = 1.0 / 64
+    t = reference_seconds_per_run(m3, oracle, config, probe, 1)
+    scale = min(1.0, max(probe, probe * budget_seconds / max(t, 1e-6) / 3))
+    times = [reference_seconds_per_run(m3, oracle, config, scale, 1) for _ in range(3)]
+    sec = statistics.median(times)
+    value = config.algorithmic_bytes(scale) / sec / 1e9
+    return {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
+            "sample": f"{config.name} at {scale:.4g} of full size (median of 3 runs, "
+                      f"{sec:.2f} s each), reference CPU-only m3_session_run, 1 thread",
+            "elems_per_s": config.elements(scale) / sec}
+
+
+def run_reference_arm(args, config):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    m3 = m3mod()
+    oracle = oraclemod()
+    if not oracle.reference_available():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "reference CPU library oracle/_ref/libm3ref.so not built"}))
+        return 0
+    threads = max(1, os.cpu_count() or 1)
+    # size each step to a few seconds of CPU time
+    probe = 1.0 / 64
+    t = reference_seconds_per_run(m3, oracle, config, probe, 1)
+    scale = min(1.0, max(probe, probe * 3.0 * threads / max(t, 1e-6)))
+    scale = max(scale, threads * probe / 8)
+    for _ in range(args.warmup):
+        reference_seconds_per_run(m3, oracle, config, scale, threads)
+    times = [reference_seconds_per_run(m3, oracle, config, scale, threads)
+             for _ in range(args.steps)]
+    sec = statistics.mean(times)
+    value = config.algorithmic_bytes(scale) / sec / 1e9
+    sample = (f"{config.name} at {scale:.4g} of full size per step, split into {threads} row "
+              f"shards run by {threads} threads, each its own reference CPU-only session")
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": config.dtype, "data": "synthetic (seeded PCG32, reference RNG)",
+            "impl": "reference",
+            "config": {"workload": config.workload, "sample_scale": scale},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "elems_per_s": config.elements(scale) / sec}
+    print(json.dumps(line))
+    return 0
+
+
+# ------------------------------------------------------------- CUDA arm
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    parser.add_argument("--cpu-seconds", type=float, default=12.0,
+                        help="CPU work budget of the cpu_baseline sample")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    args = parser.parse_args()
+    config = CONFIGS[args.config]
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args, config)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=device)
+    m3 = m3mod()
+    lib = m3.load()
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+
+    g = m3.Graph()
+    handles, outputs = config.build(m3, g)
+    session = m3.Session(g, device=local, stream=stream.cuda_stream)
+    report, plan_text = session.plan_report()
+    data = config.inputs_device(m3, torch, device)
+    host_in = {}
+    for name, vid in handles.items():
+        t = data[name]
+        session.write_device(vid, t.data_ptr(), t.numel() * t.element_size())
+        if not args.no_e2e:
+            pinned = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            pinned.copy_(t)
+            host_in[vid] = pinned
+    del data
+    torch.cuda.synchronize(device)
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    collective = None
+    if config.name == "c5" and world > 1:
+        collective = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def one_step():
+        for r in range(config.runs_per_step):
+            session.run_async()
+            if config.name == "c4" and r + 1 < config.runs_per_step:
+                session.swap(*config.carry)
+        if collective is not None:
+            session.read_device(outputs[0], collective.data_ptr(), 4)
+            dist.all_reduce(collective, op=dist.ReduceOp.MAX)
+
+    for _ in range(args.warmup):
+        one_step()
+    session.synchronize()
+    torch.cuda.synchronize(device)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    time.sleep(0.3)
+    for k in range(args.steps):
+        flush.zero_()
+        starts[k].record(stream)
+        one_step()
+        ends[k].record(stream)
+    session.synchronize()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(per_step)
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    bytes_step = config.algorithmic_bytes()
+    value = bytes_step * world / (ms_per_step / 1e3) / 1e9
+
+    # dominant kernel: one launch per run for c1/c2/c4/c5; c3's two launches
+    # are timed separately on their own sub-graphs
+    peak, peak_kind = measured_peaks()
+    kernel_ms = ms_per_step / config.runs_per_step
+    kernel_bytes = bytes_step / config.runs_per_step
+    kernel_name = plan_text
+    if config.name == "c3":
+        kernel_ms, kernel_bytes, kernel_name = time_c3_gsilu(m3, torch, device, stream, flush,
+                                                            args.steps)
+    achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": ncu_traffic(config.name),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
+                "kernel": kernel_name, "algorithmic_bytes_per_launch": kernel_bytes}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(m3, torch, device, stream, config, session, handles, outputs,
+                          flush, args, world, host_in)
+
+    baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        baseline = cpu_baseline(m3, oraclemod(), config, args.cpu_seconds)
+
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": config.dtype,
+            "data": "synthetic: seeded PCG32 streams of the reference RNG, generated on device",
+            "config": {"workload": config.workload, "per_gpu": "one full batch per rank",
+                       "l2": "256 MiB buffer overwritten between timed steps",
+                       "parallelism": f"dp{world}" + (" + NCCL all-reduce(max) of abs-max"
+                                                       if collective is not None else
+                                                       " (independent batches, no collective)"),
+                       "plan": plan_text},
+            "roofline": roofline, "cpu_baseline": baseline, "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": report.launch_count * config.runs_per_step * args.steps,
+            "elems_per_s": config.elements() * world / (ms_per_step / 1e3)}
+    session.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
+def time_c3_gsilu(m3, torch, device, stream, flush, steps):
+    """C3's dominant kernel (the gated-SiLU launch), timed alone."""
+    c = CONFIGS["c3"]
+    g = m3.Graph()
+    gate = g.value(m3.INPUT, m3.F16, (c.rows, c.ffn))
+    up = g.value(m3.INPUT, m3.F16, (c.rows, c.ffn))
+    y = g.inferred("GATED_SILU", [gate, up], m3.OUTPUT, m3.F16)
+    g.node("GATED_SILU", [gate, up], [y])
+    s = m3.Session(g, device=device.index, stream=stream.cuda_stream)
+    _, text = s.plan_report()
+    for _ in range(3):
+        s.run_async()
+    s.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        s.run_async()
+        b.record(stream)
+        times.append((a, b))
+    s.synchronize()
+    torch.cuda.synchronize(device)
+    ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+    s.close()
+    return ms, c.rows * c.ffn * 2 * 3, text
+
+
+def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, flush, args,
+                world, host_in):
+    """The same metric through the public C API with pinned host buffers:
+    m3_session_write_input (H2D), m3_session_run, m3_session_read_output
+    (D2H) inside the timed region."""
+    import torch.distributed as dist
+    host_out = {}
+    for vid in outputs:
+        dtype, shape, _ = session.values[vid]
+        nbytes = int(np.prod(shape)) * m3.ITEMSIZE[dtype]
+        host_out[vid] = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    err = m3.M3Error()
+    lib = m3.load()
+
+    def call(fn, *a):
+        m3.check(fn(session.handle, *a, ctypes.byref(err)), err)
+
+    def one():
+        for vid, buf in host_in.items():
+            call(lib.m3_session_write_input, vid, ctypes.c_void_p(buf.data_ptr()), buf.nbytes)
+        for r in range(config.runs_per_step):
+            call(lib.m3_session_run)
+            if config.name == "c4" and r + 1 < config.runs_per_step:
+                # the reference's host-side carry: read x', write it as x
+                x_in, x_out = config.carry
+                buf = host_in[x_in]
+                call(lib.m3_session_read_output, x_out, ctypes.c_void_p(buf.data_ptr()),
+                     buf.nbytes)
+                call(lib.m3_session_write_input, x_in, ctypes.c_void_p(buf.data_ptr()),
+                     buf.nbytes)
+        for vid, buf in host_out.items():
+            call(lib.m3_session_read_output, vid, ctypes.c_void_p(buf.data_ptr()), buf.nbytes)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    times = []
+    for _ in range(max(3, args.steps // 2)):
+        flush.zero_()
+        torch.cuda.synchronize(device)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        one()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    ms = statistics.mean(times)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    h2d = sum(b.nbytes for b in host_in.values())
+    d2h = sum(b.nbytes for b in host_out.values())
+    if config.name == "c4":
+        carried = host_in[config.carry[0]].nbytes * (config.runs_per_step - 1)
+        h2d += carried
+        d2h += carried
+    return {"value": config.algorithmic_bytes() * world / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,603 @@
+/* m3_cuda.h -- the C ABI of libm3cuda.so, a B200 (sm_100a) CUDA provider for
+ * m3.c's tensor hot path: element-wise, broadcast, cast, activation and
+ * row-reduction operators.
+ *
+ * Three layers are exported, all plain C, plain pointers and sizes:
+ *
+ *  1. The graph/session API of the reference's include/m3.h:197-259, same
+ *     names, same argument meaning, same status codes and same failure
+ *     atomicity.  A program written against m3.h that builds graphs from the
+ *     operators below links against this library unchanged; its regular nodes
+ *     run on the GPU, planned into liveness slots of one device arena and
+ *     fused into few kernels.
+ *
+ *  2. The reference's backend plug-in interface (m3_backend_vtable,
+ *     reference src/m3_backend_internal.h:9-17) as free functions with the
+ *     exact vtable signatures, so the reference's own provider scheduler
+ *     (src/m3_provider.c) can register this library as one more provider.
+ *
+ *  3. CUDA-only extensions: device and stream selection, asynchronous runs,
+ *     device pointers of session values, a host-only planner for tests, and
+ *     the seeded input generators of the reference's m3_rng.
+ *
+ * ABI compatibility.  The reference types that cross this boundary are
+ * restated below with identical layout.  Each block is guarded by the
+ * reference header's own include guard, so a translation unit that already
+ * included the reference headers uses their definitions; include this header
+ * after the reference headers when both are used.
+ *
+ * Operators executed on the GPU: COPY, CAST, ADD, MUL, GATED_SILU, SOFTMAX,
+ * TOP_K, RMS_NORM, LAYER_NORM, SNAKE1D, TANH, and the extensions
+ * M3_OP_ABS_MAX and M3_OP_CLAMP_UNIT.  Other m3.h kinds (contractions,
+ * attention, convolutions, embedding, RoPE, categorical) are rejected with
+ * M3_STATUS_UNSUPPORTED at session creation; there is no CPU fallback inside
+ * this library.
+ *
+ * Threading: as in the reference (include/m3.h:270-273) a session is neither
+ * reentrant nor thread-safe; distinct sessions are independent. */
+
+#ifndef M3_CUDA_H
+#define M3_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * Reference ABI (include/m3.h)
+ * ------------------------------------------------------------------------ */
+#ifndef M3_H
+#define M3_TENSOR_MAX_RANK 8U
+#define M3_GRAPH_NODE_INPUT_CAPACITY 5U
+#define M3_GRAPH_NODE_OUTPUT_CAPACITY 2U
+#define M3_GRAPH_VALUE_NONE UINT32_MAX
+
+/* include/m3.h:20-31 */
+typedef enum {
+    M3_STATUS_OK = 0,
+    M3_STATUS_INVALID_ARGUMENT = 1,
+    M3_STATUS_OUT_OF_RANGE = 2,
+    M3_STATUS_OVERFLOW = 3,
+    M3_STATUS_OUT_OF_MEMORY = 4,
+    M3_STATUS_IO = 5,
+    M3_STATUS_INVALID_FORMAT = 6,
+    M3_STATUS_UNSUPPORTED = 7,
+    M3_STATUS_CANCELLED = 8,
+    M3_STATUS_INTERNAL = 9
+} m3_status;
+
+#define M3_ERROR_MESSAGE_CAPACITY 256U
+
+/* include/m3.h:35-38 */
+typedef struct {
+    m3_status status;
+    char message[M3_ERROR_MESSAGE_CAPACITY];
+} m3_error;
+
+/* include/m3.h:45-50 */
+typedef enum {
+    M3_DTYPE_F32 = 0,
+    M3_DTYPE_F16,
+    M3_DTYPE_BF16,
+    M3_DTYPE_I32
+} m3_dtype;
+
+/* include/m3.h:52-73 */
+typedef enum {
+    M3_OP_COPY = 0,
+    M3_OP_CAST,
+    M3_OP_ADD,
+    M3_OP_MUL,
+    M3_OP_EMBEDDING,
+    M3_OP_MATMUL,
+    M3_OP_LINEAR,
+    M3_OP_RMS_NORM,
+    M3_OP_LAYER_NORM,
+    M3_OP_ROPE,
+    M3_OP_ATTENTION,
+    M3_OP_GATED_SILU,
+    M3_OP_SOFTMAX,
+    M3_OP_TOP_K,
+    M3_OP_CATEGORICAL,
+    M3_OP_CONV1D,
+    M3_OP_CONV_TRANSPOSE1D,
+    M3_OP_NEAREST_RESIZE1D,
+    M3_OP_SNAKE1D,
+    M3_OP_TANH
+} m3_op_kind;
+
+/* include/m3.h:75-78 */
+typedef enum {
+    M3_ROPE_HALF_SPLIT = 0,
+    M3_ROPE_INTERLEAVED
+} m3_rope_mode;
+
+/* include/m3.h:80-84 */
+typedef enum {
+    M3_PROVIDER_NEURAL_ENGINE = 0,
+    M3_PROVIDER_METAL,
+    M3_PROVIDER_CPU
+} m3_provider_kind;
+
+/* include/m3.h:86-91 */
+typedef enum {
+    M3_GRAPH_INPUT = 0,
+    M3_GRAPH_CONSTANT,
+    M3_GRAPH_TEMPORARY,
+    M3_GRAPH_OUTPUT
+} m3_graph_value_role;
+
+typedef uint32_t m3_graph_value_id;
+
+/* include/m3.h:95-100 */
+typedef struct {
+    m3_dtype dtype;
+    uint8_t rank;
+    uint64_t shape[M3_TENSOR_MAX_RANK];
+    m3_graph_value_role role;
+} m3_graph_value_desc;
+
+/* include/m3.h:102-135 */
+typedef struct {
+    m3_op_kind kind;
+    m3_graph_value_id inputs[M3_GRAPH_NODE_INPUT_CAPACITY];
+    m3_graph_value_id outputs[M3_GRAPH_NODE_OUTPUT_CAPACITY];
+    union {
+        struct {
+            float epsilon;
+        } norm;
+        struct {
+            uint64_t position_offset;
+            uint32_t rotary_dimension;
+            m3_rope_mode mode;
+        } rope;
+        struct {
+            float scale;
+            int64_t causal_offset;
+            bool causal;
+        } attention;
+        struct {
+            uint64_t k;
+        } top_k;
+        struct {
+            uint64_t groups;
+            uint64_t stride;
+            uint64_t dilation;
+            uint64_t pad_left;
+            uint64_t pad_right;
+            uint64_t output_padding;
+        } convolution;
+        struct {
+            uint64_t output_length;
+        } resize;
+    } parameters;
+} m3_graph_node_desc;
+
+/* include/m3.h:147-151 */
+typedef struct {
+    bool allow_neural_engine;
+    bool allow_metal;
+    bool allow_cpu;
+} m3_session_options;
+
+/* include/m3.h:153-158 */
+typedef struct {
+    size_t value_count;
+    size_t node_count;
+    size_t storage_slot_count;
+    size_t allocated_bytes;
+} m3_session_plan_info;
+
+typedef struct m3_graph m3_graph;
+typedef struct m3_session m3_session;
+
+/* include/m3.h:197-259 (the graph/session subset; Music3 and Core ML
+ * partitions are not part of this library). */
+const char *m3_version(void);
+const char *m3_status_string(m3_status status);
+void m3_error_reset(m3_error *error);
+const char *m3_error_message(const m3_error *error);
+void m3_graph_value_desc_init(m3_graph_value_desc *description,
+                              m3_graph_value_role role, m3_dtype dtype,
+                              uint8_t rank, const uint64_t *shape);
+void m3_graph_node_desc_init(m3_graph_node_desc *description,
+                             m3_op_kind kind);
+void m3_session_options_init(m3_session_options *options);
+m3_status m3_graph_create(m3_graph **graph, m3_error *error);
+void m3_graph_free(m3_graph *graph);
+m3_status m3_graph_add_value(m3_graph *graph,
+                             const m3_graph_value_desc *description,
+                             m3_graph_value_id *value, m3_error *error);
+m3_status m3_graph_set_constant(m3_graph *graph, m3_graph_value_id value,
+                                const void *data, size_t byte_count,
+                                m3_error *error);
+m3_status m3_graph_add_inferred_value(
+    m3_graph *graph, const m3_graph_node_desc *node, size_t output_index,
+    m3_graph_value_role role, m3_dtype dtype, m3_graph_value_id *value,
+    m3_error *error);
+m3_status m3_graph_add_node(m3_graph *graph,
+                            const m3_graph_node_desc *description,
+                            m3_error *error);
+m3_status m3_session_create(m3_session **session, const m3_graph *graph,
+                             const m3_session_options *options,
+                             m3_error *error);
+void m3_session_free(m3_session *session);
+m3_status m3_session_write_input(m3_session *session, m3_graph_value_id value,
+                                  const void *data, size_t byte_count,
+                                  m3_error *error);
+m3_status m3_session_read_output(const m3_session *session,
+                                  m3_graph_value_id value, void *data,
+                                  size_t byte_count, m3_error *error);
+m3_status m3_session_run(m3_session *session, m3_error *error);
+m3_status m3_session_get_plan_info(const m3_session *session,
+                                    m3_session_plan_info *info,
+                                    m3_error *error);
+m3_status m3_session_get_node_provider(const m3_session *session,
+                                        size_t node_index,
+                                        m3_provider_kind *provider,
+                                        m3_error *error);
+#endif /* M3_H */
+
+/* ------------------------------------------------------------------------
+ * Reference ABI (src/m3_tensor.h, src/m3_scratch.h, src/m3_op.h)
+ * ------------------------------------------------------------------------ */
+#ifndef M3_TENSOR_H
+/* src/m3_tensor.h:12-18 */
+typedef struct {
+    m3_dtype dtype;
+    uint8_t rank;
+    uint64_t shape[M3_TENSOR_MAX_RANK];
+    size_t element_count;
+    size_t byte_count;
+} m3_tensor_metadata;
+
+/* Opaque storage of the host library (src/m3_backend.c:9-16). */
+typedef struct m3_storage m3_storage;
+
+/* src/m3_tensor.h:22-27 */
+typedef struct {
+    m3_tensor_metadata metadata;
+    size_t byte_offset;
+    size_t byte_strides[M3_TENSOR_MAX_RANK];
+    m3_storage *storage;
+} m3_tensor_view;
+#endif /* M3_TENSOR_H */
+
+#ifndef M3_SCRATCH_H
+/* src/m3_scratch.h:11-15 */
+typedef struct {
+    uint8_t *data;
+    size_t capacity;
+    size_t offset;
+} m3_scratch_arena;
+#endif /* M3_SCRATCH_H */
+
+#ifndef M3_OP_H
+/* src/m3_op.h:14-148 */
+typedef struct {
+    const m3_tensor_view *input;
+    m3_tensor_view *output;
+} m3_op_unary;
+
+typedef struct {
+    const m3_tensor_view *left;
+    const m3_tensor_view *right;
+    m3_tensor_view *output;
+} m3_op_binary;
+
+typedef struct {
+    const m3_tensor_view *ids;
+    const m3_tensor_view *table;
+    m3_tensor_view *output;
+} m3_op_embedding;
+
+typedef struct {
+    const m3_tensor_view *left;
+    const m3_tensor_view *right;
+    m3_tensor_view *output;
+} m3_op_matmul;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *weight;
+    const m3_tensor_view *bias;
+    m3_tensor_view *output;
+} m3_op_linear;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *scale;
+    m3_tensor_view *output;
+    float epsilon;
+} m3_op_rms_norm;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *scale;
+    const m3_tensor_view *bias;
+    m3_tensor_view *output;
+    float epsilon;
+} m3_op_layer_norm;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *cosines;
+    const m3_tensor_view *sines;
+    m3_tensor_view *output;
+    uint64_t position_offset;
+    uint32_t rotary_dimension;
+    m3_rope_mode mode;
+} m3_op_rope;
+
+typedef struct {
+    const m3_tensor_view *query;
+    const m3_tensor_view *key;
+    const m3_tensor_view *value;
+    const m3_tensor_view *mask;
+    m3_tensor_view *output;
+    float scale;
+    int64_t causal_offset;
+    bool causal;
+} m3_op_attention;
+
+typedef struct {
+    const m3_tensor_view *logits;
+    m3_tensor_view *values;
+    m3_tensor_view *indices;
+    uint64_t k;
+} m3_op_top_k;
+
+typedef struct {
+    const m3_tensor_view *probabilities;
+    const m3_tensor_view *uniforms;
+    m3_tensor_view *output;
+} m3_op_categorical;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *weight;
+    const m3_tensor_view *bias;
+    m3_tensor_view *output;
+    uint64_t groups;
+    uint64_t stride;
+    uint64_t dilation;
+    uint64_t pad_left;
+    uint64_t pad_right;
+} m3_op_conv1d;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *weight;
+    const m3_tensor_view *bias;
+    m3_tensor_view *output;
+    uint64_t groups;
+    uint64_t stride;
+    uint64_t dilation;
+    uint64_t pad_left;
+    uint64_t pad_right;
+    uint64_t output_padding;
+} m3_op_conv_transpose1d;
+
+typedef struct {
+    const m3_tensor_view *input;
+    const m3_tensor_view *alpha;
+    m3_tensor_view *output;
+} m3_op_snake1d;
+
+typedef struct {
+    m3_op_kind kind;
+    union {
+        m3_op_unary copy;
+        m3_op_unary cast;
+        m3_op_binary add;
+        m3_op_binary mul;
+        m3_op_embedding embedding;
+        m3_op_matmul matmul;
+        m3_op_linear linear;
+        m3_op_rms_norm rms_norm;
+        m3_op_layer_norm layer_norm;
+        m3_op_rope rope;
+        m3_op_attention attention;
+        m3_op_binary gated_silu;
+        m3_op_unary softmax;
+        m3_op_top_k top_k;
+        m3_op_categorical categorical;
+        m3_op_conv1d conv1d;
+        m3_op_conv_transpose1d conv_transpose1d;
+        m3_op_unary nearest_resize1d;
+        m3_op_snake1d snake1d;
+        m3_op_unary tanh;
+    } descriptor;
+} m3_command;
+#endif /* M3_OP_H */
+
+/* ------------------------------------------------------------------------
+ * CUDA provider extensions
+ * ------------------------------------------------------------------------ */
+
+/* Provider reported by m3_session_get_node_provider for GPU-placed nodes.
+ * Appended after the reference's last value (include/m3.h:80-84). */
+#define M3_PROVIDER_CUDA ((m3_provider_kind)3)
+
+/* Extension operators (no reference counterpart).  Both are unary: graph
+ * nodes use inputs[0] / outputs[0]; commands use descriptor.copy.
+ *
+ * M3_OP_ABS_MAX: output is one F32 element holding max |x| over the whole
+ *   input (any float dtype), computed on bit patterns so the result is exact
+ *   and order-free; an empty input gives +0.  Any NaN fails the operator with
+ *   M3_STATUS_OUT_OF_RANGE and leaves the output untouched (the reference's
+ *   top-k NaN rule, src/m3_op_data_preflight.c:288-291).
+ * M3_OP_CLAMP_UNIT: same shape and dtype; values above +1 become +1, values
+ *   below -1 become -1, everything else (NaN payloads, signed zeros,
+ *   subnormals) is copied bit for bit (the waveform clamp of the reference,
+ *   src/m3_waveform.c:360-380). */
+#define M3_OP_ABS_MAX ((m3_op_kind)64)
+#define M3_OP_CLAMP_UNIT ((m3_op_kind)65)
+
+#define M3_CUDA_DEVICE_CURRENT (-1)
+
+typedef struct {
+    int device;            /* CUDA ordinal, or M3_CUDA_DEVICE_CURRENT */
+    void *stream;          /* cudaStream_t to run on; NULL: the session owns
+                              a non-blocking stream */
+    bool fuse;             /* fuse element-wise chains and row prologues
+                              (default true) */
+    bool cuda_graphs;      /* replay each run's launches as a CUDA graph
+                              (default true) */
+} m3_cuda_session_options;
+
+void m3_cuda_session_options_init(m3_cuda_session_options *options);
+
+/* m3_session_create with explicit CUDA options.  m3_session_create itself
+ * uses the defaults.  The accelerator is permitted when options->allow_metal
+ * or options->allow_neural_engine is set (the reference's GPU switches); a
+ * CPU-only request is M3_STATUS_UNSUPPORTED because this library holds no CPU
+ * provider. */
+m3_status m3_cuda_session_create(m3_session **session, const m3_graph *graph,
+                                  const m3_session_options *options,
+                                  const m3_cuda_session_options *cuda,
+                                  m3_error *error);
+
+/* Enqueue one run without waiting.  Failures of data checks (NaN, range) are
+ * recorded on the device; later runs enqueued before the next synchronise
+ * become no-ops after a failure, exactly as a failing m3_session_run stops.
+ * m3_cuda_session_synchronize waits and returns the first failure since the
+ * previous synchronise, with the reference's message. */
+m3_status m3_cuda_session_run_async(m3_session *session, m3_error *error);
+m3_status m3_cuda_session_synchronize(m3_session *session, m3_error *error);
+
+/* Device address and byte size of a value's current storage (valid until the
+ * next run, write or swap).  For zero-copy interoperation, e.g. handing an
+ * output to a collective. */
+m3_status m3_cuda_session_value_device_pointer(const m3_session *session,
+                                               m3_graph_value_id value,
+                                               void **device_pointer,
+                                               size_t *byte_count,
+                                               m3_error *error);
+
+/* Device-to-device input write / output read (no host staging). */
+m3_status m3_cuda_session_write_input_device(m3_session *session,
+                                             m3_graph_value_id value,
+                                             const void *device_source,
+                                             size_t byte_count,
+                                             m3_error *error);
+m3_status m3_cuda_session_read_output_device(const m3_session *session,
+                                             m3_graph_value_id value,
+                                             void *device_destination,
+                                             size_t byte_count,
+                                             m3_error *error);
+
+/* Exchange the storage of an INPUT and an OUTPUT value of equal byte size, in
+ * O(1) and without copying: the next run reads as input what the last run
+ * wrote as output.  Carries a solver state between runs (the flow solver's
+ * x' -> x, reference src/m3_flow_solver_math.c:102-135). */
+m3_status m3_cuda_session_swap_values(m3_session *session,
+                                      m3_graph_value_id input,
+                                      m3_graph_value_id output,
+                                      m3_error *error);
+
+/* The session's stream (cudaStream_t) and device ordinal. */
+void *m3_cuda_session_stream(const m3_session *session);
+int m3_cuda_session_device(const m3_session *session);
+
+/* Execution plan summary: kernel launches per run and a one-line description
+ * of each launch group ("ew[MUL,ADD] out=1", "row[SOFTMAX+TOP_K] ..."). */
+typedef struct {
+    size_t launch_count;
+    size_t fused_node_count;     /* nodes that share a launch with another */
+    size_t shadow_bytes;         /* extra arena bytes for atomic commit */
+    size_t arena_bytes;          /* total device arena bytes */
+} m3_cuda_plan_report;
+
+m3_status m3_cuda_session_get_plan_report(const m3_session *session,
+                                          m3_cuda_plan_report *report,
+                                          char *text, size_t text_capacity,
+                                          m3_error *error);
+
+/* The same compile steps as session creation (topology, liveness slots,
+ * binding, validation, placement, fusion) without touching a GPU: for tests
+ * and capacity planning on hosts without a device. */
+m3_status m3_cuda_graph_plan(const m3_graph *graph,
+                             const m3_cuda_session_options *cuda,
+                             m3_session_plan_info *info,
+                             m3_cuda_plan_report *report, char *text,
+                             size_t text_capacity, m3_error *error);
+
+/* ------------------------------------------------------------------------
+ * Backend plug-in (reference src/m3_backend_internal.h:9-17)
+ * ------------------------------------------------------------------------
+ * Free functions with the exact signatures of m3_backend_vtable's members,
+ * to be registered with the reference's m3_backend_create_internal
+ * (src/m3_backend.c:80-111).  The context is created here; the host library
+ * supplies its storage accessor so views can be resolved to device
+ * addresses. */
+typedef struct {
+    int device;                                    /* CUDA ordinal */
+    /* The host library's m3_storage_data (reference src/m3_backend.h:52). */
+    void *(*storage_data)(m3_storage *storage);
+    /* true: storages are cudaMallocManaged, so the reference's memcpy-based
+     * m3_storage_write/read (src/m3_backend.c:319-366) work unchanged and
+     * the backend reports unified memory; false: device memory, and the
+     * host library must route writes/reads to m3_cuda_backend_write/read. */
+    bool managed_memory;
+} m3_cuda_backend_options;
+
+m3_status m3_cuda_backend_context_create(
+    const m3_cuda_backend_options *options, void **context, m3_error *error);
+/* vtable.destroy_context */
+void m3_cuda_backend_destroy_context(void *context);
+/* vtable.allocate: 256-byte aligned device (or managed) memory. */
+m3_status m3_cuda_backend_allocate(void *context, size_t byte_count,
+                                   size_t alignment, void **handle,
+                                   void **data, m3_error *error);
+/* vtable.free_storage */
+void m3_cuda_backend_free_storage(void *context, void *handle, void *data);
+/* vtable.execute: runs the commands in order on the GPU and returns after the
+ * stream has finished, with the reference's all-or-nothing data checks. */
+m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
+                                  size_t command_count,
+                                  m3_scratch_arena *scratch, m3_error *error);
+/* The write/read hooks a non-unified backend needs (host <-> device). */
+m3_status m3_cuda_backend_write(void *context, void *data, size_t byte_offset,
+                                const void *source, size_t byte_count,
+                                m3_error *error);
+m3_status m3_cuda_backend_read(void *context, const void *data,
+                               size_t byte_offset, void *destination,
+                               size_t byte_count, m3_error *error);
+/* Placement table for m3_provider_select_regular (src/m3_provider.c:7-33). */
+bool m3_cuda_backend_supports_kind(m3_op_kind kind);
+
+/* ------------------------------------------------------------------------
+ * Seeded synthetic inputs (reference src/m3_rng.c:9-110)
+ * ------------------------------------------------------------------------
+ * PCG32 seeded as m3_rng_seed(seed, sequence).  Host fills produce exactly the
+ * reference's sequence; device fills produce the same sequence by jumping the
+ * generator ahead per element block (bit-identical for uniforms; normals use
+ * the GPU's double-precision log/sin/cos and agree to within 1 ulp of F32). */
+m3_status m3_cuda_fill_uniform_host(uint64_t seed, uint64_t sequence,
+                                    float low, float high, float *values,
+                                    size_t count, m3_error *error);
+m3_status m3_cuda_fill_normal_host(uint64_t seed, uint64_t sequence,
+                                   float mean, float deviation, float *values,
+                                   size_t count, m3_error *error);
+m3_status m3_cuda_fill_uniform_device(uint64_t seed, uint64_t sequence,
+                                      float low, float high,
+                                      float *device_values, size_t count,
+                                      void *stream, m3_error *error);
+m3_status m3_cuda_fill_normal_device(uint64_t seed, uint64_t sequence,
+                                     float mean, float deviation,
+                                     float *device_values, size_t count,
+                                     void *stream, m3_error *error);
+
+/* Number of CUDA devices visible (0 without a driver or GPU). */
+int m3_cuda_device_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3_CUDA_H */

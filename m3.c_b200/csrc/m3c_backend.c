@@ -1,0 +1,642 @@
+/* The backend plug-in of the reference (m3_backend_vtable,
+ * src/m3_backend_internal.h:9-17) backed by the CUDA kernels.
+ *
+ * The reference's scheduler hands this backend whole command lists
+ * (src/m3_backend.c:113-154 validates them first).  Commands run in order on
+ * one stream, one launch per command (no liveness information reaches a
+ * backend, so nothing is fused here).  Views may be strided: element-wise
+ * operands are addressed through their strides directly; row operators gather
+ * a non-contiguous input into a temporary first.  Data-checked operators
+ * (SOFTMAX/TOP_K NaN, float-to-I32 CAST range) run a scan kernel before the
+ * computing kernel; the computing kernel skips its writes when the scan (or
+ * any earlier command) failed, so a failing list leaves the failing command's
+ * outputs and everything after it untouched, as in the reference.
+ * `execute` returns after the stream is idle (the reference's Metal backend
+ * likewise waits for completion, src/m3_backend_metal.m:211-212). */
+
+#include "m3c_internal.h"
+
+#include <cuda_runtime_api.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct {
+    int device;
+    void *(*storage_data)(m3_storage *storage);
+    bool managed;
+    cudaStream_t stream;
+    m3c_status *status;
+    m3c_status *status_host;
+    m3c_reduce_scratch *reduce;
+} cuda_backend;
+
+static const m3c_status clean = {UINT32_MAX, 0U, 0U, 0U};
+
+static m3_status fail_cuda(m3_error *error, cudaError_t code, const char *what)
+{
+    (void)cudaGetLastError();
+    return m3c_error_set(error,
+                         code == cudaErrorMemoryAllocation
+                             ? M3_STATUS_OUT_OF_MEMORY
+                             : M3_STATUS_INTERNAL,
+                         "%s: %s", what, cudaGetErrorString(code));
+}
+
+bool m3_cuda_backend_supports_kind(m3_op_kind kind)
+{
+    return m3c_kind_supported(kind);
+}
+
+m3_status m3_cuda_backend_context_create(
+    const m3_cuda_backend_options *options, void **context, m3_error *error)
+{
+    cuda_backend *b;
+    cudaError_t code;
+    int devices = 0;
+
+    if (context == NULL || options == NULL || options->storage_data == NULL) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "backend options and storage accessor are required");
+    }
+    *context = NULL;
+    if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) {
+        (void)cudaGetLastError();
+        return m3c_error_set(error, M3_STATUS_UNSUPPORTED,
+                             "no CUDA device is available");
+    }
+    b = calloc(1U, sizeof(*b));
+    if (b == NULL) {
+        return m3c_error_set(error, M3_STATUS_OUT_OF_MEMORY,
+                             "cannot allocate CUDA backend context");
+    }
+    b->device = options->device < 0 ? 0 : options->device;
+    b->storage_data = options->storage_data;
+    b->managed = options->managed_memory;
+    code = cudaSetDevice(b->device);
+    if (code == cudaSuccess) {
+        code = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    }
+    if (code == cudaSuccess) {
+        code = cudaMalloc((void **)&b->status, sizeof(m3c_status));
+    }
+    if (code == cudaSuccess) {
+        code = cudaMalloc((void **)&b->reduce, sizeof(m3c_reduce_scratch));
+    }
+    if (code == cudaSuccess) {
+        code = cudaMallocHost((void **)&b->status_host, sizeof(m3c_status));
+    }
+    if (code == cudaSuccess) {
+        code = cudaMemset(b->reduce, 0, sizeof(m3c_reduce_scratch));
+    }
+    if (code == cudaSuccess) {
+        code = cudaMemcpy(b->status, &clean, sizeof(clean),
+                          cudaMemcpyHostToDevice);
+    }
+    if (code != cudaSuccess) {
+        m3_cuda_backend_destroy_context(b);
+        return fail_cuda(error, code, "cannot create CUDA backend");
+    }
+    *context = b;
+    m3_error_reset(error);
+    return M3_STATUS_OK;
+}
+
+void m3_cuda_backend_destroy_context(void *context)
+{
+    cuda_backend *b = context;
+
+    if (b == NULL) {
+        return;
+    }
+    (void)cudaSetDevice(b->device);
+    if (b->stream != NULL) {
+        (void)cudaStreamSynchronize(b->stream);
+        (void)cudaStreamDestroy(b->stream);
+    }
+    (void)cudaFree(b->status);
+    (void)cudaFree(b->reduce);
+    (void)cudaFreeHost(b->status_host);
+    (void)cudaGetLastError();
+    free(b);
+}
+
+m3_status m3_cuda_backend_allocate(void *context, size_t byte_count,
+                                   size_t alignment, void **handle,
+                                   void **data, m3_error *error)
+{
+    cuda_backend *b = context;
+    cudaError_t code;
+    void *memory = NULL;
+
+    *handle = NULL;
+    *data = NULL;
+    if (byte_count == 0U) {
+        return M3_STATUS_OK;
+    }
+    if (alignment > M3C_ARENA_ALIGNMENT) {
+        return m3c_error_set(error, M3_STATUS_UNSUPPORTED,
+                             "CUDA storage alignment above 256 bytes");
+    }
+    (void)cudaSetDevice(b->device);
+    code = b->managed ? cudaMallocManaged(&memory, byte_count,
+                                          cudaMemAttachGlobal)
+                      : cudaMalloc(&memory, byte_count);
+    if (code != cudaSuccess) {
+        return fail_cuda(error, code, "cannot allocate CUDA storage");
+    }
+    *handle = memory;
+    *data = memory;
+    return M3_STATUS_OK;
+}
+
+void m3_cuda_backend_free_storage(void *context, void *handle, void *data)
+{
+    cuda_backend *b = context;
+
+    (void)data;
+    if (handle != NULL) {
+        (void)cudaSetDevice(b->device);
+        (void)cudaFree(handle);
+        (void)cudaGetLastError();
+    }
+}
+
+m3_status m3_cuda_backend_write(void *context, void *data, size_t byte_offset,
+                                const void *source, size_t byte_count,
+                                m3_error *error)
+{
+    cuda_backend *b = context;
+    cudaError_t code;
+
+    if (byte_count == 0U) {
+        return M3_STATUS_OK;
+    }
+    (void)cudaSetDevice(b->device);
+    code = cudaMemcpyAsync((unsigned char *)data + byte_offset, source,
+                           byte_count, cudaMemcpyHostToDevice, b->stream);
+    if (code == cudaSuccess) {
+        code = cudaStreamSynchronize(b->stream);
+    }
+    return code == cudaSuccess ? M3_STATUS_OK
+                               : fail_cuda(error, code, "storage write failed");
+}
+
+m3_status m3_cuda_backend_read(void *context, const void *data,
+                               size_t byte_offset, void *destination,
+                               size_t byte_count, m3_error *error)
+{
+    cuda_backend *b = context;
+    cudaError_t code;
+
+    if (byte_count == 0U) {
+        return M3_STATUS_OK;
+    }
+    (void)cudaSetDevice(b->device);
+    code = cudaMemcpyAsync(destination, (const unsigned char *)data + byte_offset,
+                           byte_count, cudaMemcpyDeviceToHost, b->stream);
+    if (code == cudaSuccess) {
+        code = cudaStreamSynchronize(b->stream);
+    }
+    return code == cudaSuccess ? M3_STATUS_OK
+                               : fail_cuda(error, code, "storage read failed");
+}
+
+/* ------------------------------------------------------------ execution */
+
+static unsigned char *view_base(const cuda_backend *b, const m3_tensor_view *v)
+{
+    return (unsigned char *)b->storage_data(v->storage);
+}
+
+static void vview_of(const m3_tensor_view *view, m3c_vview *out)
+{
+    memset(out, 0, sizeof(*out));
+    if (view == NULL) {
+        return;
+    }
+    out->metadata = &view->metadata;
+    out->byte_offset = view->byte_offset;
+    out->byte_strides = view->byte_strides;
+    out->storage = view->storage;
+    out->present = true;
+}
+
+/* The reference command, in the validator's positional form. */
+static void to_vcommand(const m3_command *c, m3c_vcommand *v)
+{
+    memset(v, 0, sizeof(*v));
+    v->kind = c->kind;
+    switch ((int)c->kind) {
+    case M3_OP_ADD:
+    case M3_OP_MUL:
+    case M3_OP_GATED_SILU:
+        vview_of(c->descriptor.add.left, &v->in[0]);
+        vview_of(c->descriptor.add.right, &v->in[1]);
+        vview_of(c->descriptor.add.output, &v->out[0]);
+        break;
+    case M3_OP_RMS_NORM:
+        vview_of(c->descriptor.rms_norm.input, &v->in[0]);
+        vview_of(c->descriptor.rms_norm.scale, &v->in[1]);
+        vview_of(c->descriptor.rms_norm.output, &v->out[0]);
+        v->epsilon = c->descriptor.rms_norm.epsilon;
+        break;
+    case M3_OP_LAYER_NORM:
+        vview_of(c->descriptor.layer_norm.input, &v->in[0]);
+        vview_of(c->descriptor.layer_norm.scale, &v->in[1]);
+        vview_of(c->descriptor.layer_norm.bias, &v->in[2]);
+        vview_of(c->descriptor.layer_norm.output, &v->out[0]);
+        v->epsilon = c->descriptor.layer_norm.epsilon;
+        break;
+    case M3_OP_TOP_K:
+        vview_of(c->descriptor.top_k.logits, &v->in[0]);
+        vview_of(c->descriptor.top_k.values, &v->out[0]);
+        vview_of(c->descriptor.top_k.indices, &v->out[1]);
+        v->k = c->descriptor.top_k.k;
+        break;
+    case M3_OP_SNAKE1D:
+        vview_of(c->descriptor.snake1d.input, &v->in[0]);
+        vview_of(c->descriptor.snake1d.alpha, &v->in[1]);
+        vview_of(c->descriptor.snake1d.output, &v->out[0]);
+        break;
+    default: /* unary shapes: COPY, CAST, SOFTMAX, TANH, extensions */
+        vview_of(c->descriptor.copy.input, &v->in[0]);
+        vview_of(c->descriptor.copy.output, &v->out[0]);
+        break;
+    }
+}
+
+/* One element-wise op over views (single-op program). */
+static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
+                           const m3_tensor_view *a, const m3_tensor_view *x,
+                           const m3_tensor_view *out, int aux,
+                           const m3_tensor_metadata *space)
+{
+    m3c_ew_params p;
+    int reg = 0;
+
+    memset(&p, 0, sizeof(p));
+    p.count = space->element_count;
+    p.status = b->status;
+    p.first_of_run = 0;
+    p.n_operands = 0;
+    if (a != NULL) {
+        m3c_operand_setup(&p.operands[p.n_operands++], view_base(b, a),
+                          &a->metadata, a->byte_offset, a->byte_strides, space,
+                          a->metadata.dtype == M3_DTYPE_I32 ? M3C_LOAD_INT
+                                                            : M3C_LOAD_RAW);
+    }
+    if (x != NULL) {
+        m3c_operand_setup(&p.operands[p.n_operands++], view_base(b, x),
+                          &x->metadata, x->byte_offset, x->byte_strides, space,
+                          x->metadata.dtype == M3_DTYPE_I32 ? M3C_LOAD_INT
+                                                            : M3C_LOAD_RAW);
+    }
+    /* widen 16-bit operands explicitly (registers 0, 1 -> 2, 3) */
+    {
+        int k;
+        int regs[2] = {0, 1};
+
+        for (k = 0; k < p.n_operands; ++k) {
+            const m3_tensor_view *v = k == 0 ? a : x;
+            bool raw_copy = code == M3C_OP_MOV;
+
+            if (!raw_copy && (v->metadata.dtype == M3_DTYPE_F16 ||
+                              v->metadata.dtype == M3_DTYPE_BF16)) {
+                m3c_ew_op *op = &p.ops[p.n_ops++];
+
+                op->code = M3C_OP_WIDEN;
+                op->dst = (uint8_t)(2 + k);
+                op->a = (uint8_t)k;
+                op->b = (uint8_t)k;
+                op->rdtype = M3C_F32;
+                op->aux = (int8_t)v->metadata.dtype;
+                op->command = (uint16_t)command;
+                regs[k] = 2 + k;
+            }
+        }
+        {
+            m3c_ew_op *op = &p.ops[p.n_ops++];
+
+            op->code = code;
+            op->a = (uint8_t)regs[0];
+            op->b = (uint8_t)(p.n_operands > 1 ? regs[1] : regs[0]);
+            op->dst = code == M3C_OP_ABSMAX ? op->a : 4U;
+            op->rdtype = out != NULL ? (int8_t)out->metadata.dtype : M3C_F32;
+            op->aux = (int8_t)aux;
+            op->command = (uint16_t)command;
+            reg = 4;
+        }
+    }
+    if (code == M3C_OP_ABSMAX) {
+        p.reduce = b->reduce;
+        p.absmax_out = view_base(b, out) + out->byte_offset;
+        p.absmax_command = command;
+    } else {
+        p.n_outputs = 1;
+        p.outputs[0].base = view_base(b, out) + out->byte_offset;
+        p.outputs[0].dtype = (int32_t)out->metadata.dtype;
+        p.outputs[0].reg = (int16_t)reg;
+        p.outputs[0].raw = (code == M3C_OP_MOV &&
+                            m3c_dtype_size(out->metadata.dtype) == 2U)
+                               ? 1
+                               : 0;
+    }
+    return m3c_launch_ew(&p, b->stream);
+}
+
+/* Row operators need a dense row-major input: gather strided views into a
+ * temporary device buffer. */
+static int dense_input(cuda_backend *b, const m3_tensor_view *view,
+                       const void **data, void **temporary)
+{
+    m3_tensor_view dense;
+    size_t stride = m3c_dtype_size(view->metadata.dtype);
+    cudaError_t code;
+    int axis;
+    int result;
+
+    *temporary = NULL;
+    if (m3c_contiguous(&view->metadata, view->byte_strides)) {
+        *data = view_base(b, view) + view->byte_offset;
+        return 0;
+    }
+    code = cudaMallocAsync(temporary, view->metadata.byte_count, b->stream);
+    if (code != cudaSuccess) {
+        return (int)code;
+    }
+    dense = *view;
+    dense.byte_offset = 0U;
+    for (axis = (int)dense.metadata.rank - 1; axis >= 0; --axis) {
+        dense.byte_strides[axis] = stride;
+        stride *= (size_t)dense.metadata.shape[axis];
+    }
+    {
+        m3c_ew_params p;
+
+        memset(&p, 0, sizeof(p));
+        p.count = view->metadata.element_count;
+        p.status = b->status;
+        p.n_operands = 1;
+        m3c_operand_setup(&p.operands[0], view_base(b, view), &view->metadata,
+                          view->byte_offset, view->byte_strides,
+                          &view->metadata, M3C_LOAD_RAW);
+        p.n_ops = 1;
+        p.ops[0].code = M3C_OP_MOV;
+        p.ops[0].dst = 1;
+        p.n_outputs = 1;
+        p.outputs[0].base = *temporary;
+        p.outputs[0].dtype = (int32_t)view->metadata.dtype;
+        p.outputs[0].reg = 1;
+        p.outputs[0].raw = 1;
+        result = m3c_launch_ew(&p, b->stream);
+    }
+    *data = *temporary;
+    return result;
+}
+
+static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
+                       void **temporary)
+{
+    const m3_tensor_metadata *space;
+    int code = 0;
+
+    switch ((int)c->kind) {
+    case M3_OP_COPY:
+        space = &c->descriptor.copy.output->metadata;
+        return launch_unary_ew(b, index, M3C_OP_MOV, c->descriptor.copy.input,
+                               NULL, c->descriptor.copy.output, 0, space);
+    case M3_OP_CAST: {
+        const m3_tensor_view *in = c->descriptor.cast.input;
+        const m3_tensor_view *out = c->descriptor.cast.output;
+
+        space = &out->metadata;
+        if (in->metadata.dtype == out->metadata.dtype) {
+            return launch_unary_ew(b, index, M3C_OP_MOV, in, NULL, out, 0,
+                                   space);
+        }
+        if (in->metadata.dtype == M3_DTYPE_I32) {
+            return launch_unary_ew(b, index, M3C_OP_I2F, in, NULL, out, 0,
+                                   space);
+        }
+        if (out->metadata.dtype == M3_DTYPE_I32) {
+            const void *data;
+            code = dense_input(b, in, &data, temporary);
+            if (code == 0) {
+                code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
+                                       in->metadata.element_count, 1, index,
+                                       b->status, b->stream);
+            }
+            if (code == 0) {
+                code = launch_unary_ew(b, index, M3C_OP_F2I, in, NULL, out, 0,
+                                       space);
+            }
+            return code;
+        }
+        return launch_unary_ew(b, index, M3C_OP_ROUND, in, NULL, out, 0,
+                               space);
+    }
+    case M3_OP_ADD:
+    case M3_OP_MUL:
+    case M3_OP_GATED_SILU: {
+        const m3_op_binary *op = &c->descriptor.add;
+        uint8_t opcode = c->kind == M3_OP_ADD   ? M3C_OP_ADD
+                         : c->kind == M3_OP_MUL ? M3C_OP_MUL
+                                                : M3C_OP_GSILU;
+
+        return launch_unary_ew(b, index, opcode, op->left, op->right,
+                               op->output, (int)op->left->metadata.dtype,
+                               &op->output->metadata);
+    }
+    case M3_OP_SNAKE1D:
+        return launch_unary_ew(b, index, M3C_OP_SNAKE,
+                               c->descriptor.snake1d.input,
+                               c->descriptor.snake1d.alpha,
+                               c->descriptor.snake1d.output, 0,
+                               &c->descriptor.snake1d.output->metadata);
+    case M3_OP_TANH:
+        return launch_unary_ew(b, index, M3C_OP_TANH, c->descriptor.tanh.input,
+                               NULL, c->descriptor.tanh.output, 0,
+                               &c->descriptor.tanh.output->metadata);
+    case (int)M3_OP_CLAMP_UNIT:
+        return launch_unary_ew(b, index, M3C_OP_CLAMP, c->descriptor.copy.input,
+                               NULL, c->descriptor.copy.output, 0,
+                               &c->descriptor.copy.output->metadata);
+    case (int)M3_OP_ABS_MAX:
+        return launch_unary_ew(b, index, M3C_OP_ABSMAX, c->descriptor.copy.input,
+                               NULL, c->descriptor.copy.output, 0,
+                               &c->descriptor.copy.input->metadata);
+    case M3_OP_SOFTMAX:
+    case M3_OP_TOP_K: {
+        const m3_tensor_view *in = c->kind == M3_OP_SOFTMAX
+                                       ? c->descriptor.softmax.input
+                                       : c->descriptor.top_k.logits;
+        m3c_softmax_params p;
+        const void *data;
+
+        code = dense_input(b, in, &data, temporary);
+        if (code == 0) {
+            code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
+                                   in->metadata.element_count, 0, index,
+                                   b->status, b->stream);
+        }
+        if (code != 0) {
+            return code;
+        }
+        memset(&p, 0, sizeof(p));
+        p.input = data;
+        p.in_dtype = (int32_t)in->metadata.dtype;
+        p.width = in->metadata.shape[in->metadata.rank - 1U];
+        p.rows = p.width ? in->metadata.element_count / p.width : 0U;
+        p.status = b->status;
+        p.softmax_command = UINT32_MAX;
+        p.topk_command = UINT32_MAX;
+        if (c->kind == M3_OP_SOFTMAX) {
+            p.probs = view_base(b, c->descriptor.softmax.output) +
+                      c->descriptor.softmax.output->byte_offset;
+            p.probs_dtype = (int32_t)c->descriptor.softmax.output->metadata.dtype;
+            p.softmax_command = index;
+        } else {
+            p.top_values = (float *)(view_base(b, c->descriptor.top_k.values) +
+                                     c->descriptor.top_k.values->byte_offset);
+            p.top_indices =
+                (int32_t *)(view_base(b, c->descriptor.top_k.indices) +
+                            c->descriptor.top_k.indices->byte_offset);
+            p.k = c->descriptor.top_k.k;
+            p.topk_command = index;
+        }
+        return m3c_launch_softmax(&p, b->stream);
+    }
+    case M3_OP_RMS_NORM:
+    case M3_OP_LAYER_NORM: {
+        bool layer = c->kind == M3_OP_LAYER_NORM;
+        const m3_tensor_view *in = layer ? c->descriptor.layer_norm.input
+                                         : c->descriptor.rms_norm.input;
+        const m3_tensor_view *scale = layer ? c->descriptor.layer_norm.scale
+                                            : c->descriptor.rms_norm.scale;
+        const m3_tensor_view *bias = layer ? c->descriptor.layer_norm.bias : NULL;
+        const m3_tensor_view *out = layer ? c->descriptor.layer_norm.output
+                                          : c->descriptor.rms_norm.output;
+        m3c_norm_params p;
+        const void *data;
+
+        if ((scale->metadata.element_count > 1U &&
+             scale->byte_strides[0] != m3c_dtype_size(scale->metadata.dtype)) ||
+            (bias != NULL && bias->metadata.element_count > 1U &&
+             bias->byte_strides[0] != m3c_dtype_size(bias->metadata.dtype))) {
+            return -1;  /* strided norm vectors are not supported */
+        }
+        code = dense_input(b, in, &data, temporary);
+        if (code != 0) {
+            return code;
+        }
+        memset(&p, 0, sizeof(p));
+        p.x = data;
+        p.in_dtype = (int32_t)in->metadata.dtype;
+        p.scale = view_base(b, scale) + scale->byte_offset;
+        p.scale_dtype = (int32_t)scale->metadata.dtype;
+        if (bias != NULL) {
+            p.bias = view_base(b, bias) + bias->byte_offset;
+            p.bias_dtype = (int32_t)bias->metadata.dtype;
+        }
+        p.layer_norm = layer ? 1 : 0;
+        p.out = view_base(b, out) + out->byte_offset;
+        p.out_dtype = (int32_t)out->metadata.dtype;
+        p.width = in->metadata.shape[in->metadata.rank - 1U];
+        p.rows = p.width ? in->metadata.element_count / p.width : 0U;
+        p.epsilon = layer ? c->descriptor.layer_norm.epsilon
+                          : c->descriptor.rms_norm.epsilon;
+        p.status = b->status;
+        return m3c_launch_norm(&p, b->stream);
+    }
+    default:
+        return -1;
+    }
+}
+
+static const char *check_message(m3_op_kind kind)
+{
+    switch ((int)kind) {
+    case M3_OP_SOFTMAX:
+        return "softmax input contains NaN";
+    case M3_OP_TOP_K:
+        return "top-k logits contain NaN";
+    case M3_OP_CAST:
+        return "float-to-I32 cast value is invalid";
+    default:
+        return "abs-max input contains NaN";
+    }
+}
+
+m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
+                                  size_t command_count,
+                                  m3_scratch_arena *scratch, m3_error *error)
+{
+    cuda_backend *b = context;
+    void **temporaries;
+    size_t i;
+    m3_status status = M3_STATUS_OK;
+    cudaError_t code;
+
+    (void)scratch;
+    if (b == NULL || (command_count != 0U && commands == NULL)) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "backend and commands are required");
+    }
+    for (i = 0U; i < command_count; ++i) {
+        m3c_vcommand v;
+
+        to_vcommand(&commands[i], &v);
+        status = m3c_validate(&v, error);
+        if (status != M3_STATUS_OK) {
+            return status;
+        }
+    }
+    temporaries = calloc(command_count ? command_count : 1U, sizeof(void *));
+    if (temporaries == NULL) {
+        return m3c_error_set(error, M3_STATUS_OUT_OF_MEMORY,
+                             "cannot allocate execution state");
+    }
+    (void)cudaSetDevice(b->device);
+    for (i = 0U; i < command_count; ++i) {
+        int result = run_command(b, &commands[i], (uint32_t)i, &temporaries[i]);
+
+        if (result != 0) {
+            status = m3c_error_set(
+                error, result < 0 ? M3_STATUS_UNSUPPORTED : M3_STATUS_INTERNAL,
+                "CUDA execution of %s failed: %s",
+                m3c_kind_name(commands[i].kind),
+                result < 0 ? "unsupported view layout"
+                           : m3c_cuda_error_string(result));
+            break;
+        }
+    }
+    for (i = 0U; i < command_count; ++i) {
+        if (temporaries[i] != NULL) {
+            (void)cudaFreeAsync(temporaries[i], b->stream);
+        }
+    }
+    free(temporaries);
+    code = cudaMemcpyAsync(b->status_host, b->status, sizeof(m3c_status),
+                           cudaMemcpyDeviceToHost, b->stream);
+    if (code == cudaSuccess) {
+        code = cudaStreamSynchronize(b->stream);
+    }
+    if (code != cudaSuccess) {
+        return fail_cuda(error, code, "CUDA execution failed");
+    }
+    if (b->status_host->fail_command != UINT32_MAX) {
+        uint32_t failing = b->status_host->fail_command;
+
+        code = cudaMemcpy(b->status, &clean, sizeof(clean),
+                          cudaMemcpyHostToDevice);
+        if (code != cudaSuccess) {
+            return fail_cuda(error, code, "cannot reset backend status");
+        }
+        return m3c_error_set(error, M3_STATUS_OUT_OF_RANGE, "%s",
+                             check_message(commands[failing].kind));
+    }
+    if (status == M3_STATUS_OK) {
+        m3_error_reset(error);
+    }
+    return status;
+}

@@ -1,0 +1,143 @@
+// Device helpers shared by the kernels: the reference's storage codecs and
+// per-statement F32 rounding, restated for the GPU.
+//
+// F16/BF16 conversions are integer restatements of the reference encoders
+// (src/m3_op_numeric.c:27-130): round to nearest even, gradual underflow,
+// overflow to infinity, and the reference's NaN payload rules.  The hardware
+// conversion instructions quiet NaNs differently, so they are not used.
+#pragma once
+
+#include <cstdint>
+
+#include "m3c_kernels.h"
+
+namespace m3c {
+
+__device__ __forceinline__ float as_float(uint32_t bits) { return __uint_as_float(bits); }
+__device__ __forceinline__ uint32_t as_bits(float value) { return __float_as_uint(value); }
+
+// src/m3_op_numeric.c:27-53
+__device__ __forceinline__ float f16_to_f32(uint32_t half)
+{
+    const uint32_t sign = (half & 0x8000u) << 16;
+    const uint32_t exponent = (half >> 10) & 0x1fu;
+    const uint32_t fraction = half & 0x3ffu;
+    if (exponent == 0u) {
+        // zero or subnormal: fraction * 2^-24 is exact
+        return as_float(sign | as_bits(__fmul_rn(__uint2float_rn(fraction), 0x1p-24f)));
+    }
+    if (exponent == 0x1fu) {
+        return as_float(sign | 0x7f800000u | (fraction << 13));
+    }
+    return as_float(sign | ((exponent + 112u) << 23) | (fraction << 13));
+}
+
+// src/m3_op_numeric.c:55-112
+__device__ __forceinline__ uint32_t f32_to_f16(float value)
+{
+    const uint32_t bits = as_bits(value);
+    const uint32_t sign = (bits >> 16) & 0x8000u;
+    const uint32_t biased = (bits >> 23) & 0xffu;
+    const uint32_t fraction = bits & 0x7fffffu;
+    const int exponent = static_cast<int>(biased) - 127;
+    if (biased == 0xffu) {
+        if (fraction == 0u) {
+            return sign | 0x7c00u;
+        }
+        const uint32_t payload = fraction >> 13;
+        return sign | 0x7e00u | payload | (payload == 0u ? 1u : 0u);
+    }
+    if (exponent > 15) {
+        return sign | 0x7c00u;
+    }
+    if (exponent >= -14) {
+        uint32_t half = (static_cast<uint32_t>(exponent + 15) << 10) | (fraction >> 13);
+        const uint32_t rest = fraction & 0x1fffu;
+        if (rest > 0x1000u || (rest == 0x1000u && (half & 1u) != 0u)) {
+            half += 1u;  // carries into the exponent; may reach infinity
+        }
+        return half >= 0x7c00u ? (sign | 0x7c00u) : (sign | half);
+    }
+    if (exponent >= -25) {
+        const uint32_t significand = 0x800000u | fraction;
+        const uint32_t shift = static_cast<uint32_t>(-exponent - 1);
+        uint32_t kept = significand >> shift;
+        const uint32_t rest = significand & ((1u << shift) - 1u);
+        const uint32_t halfway = 1u << (shift - 1u);
+        if (rest > halfway || (rest == halfway && (kept & 1u) != 0u)) {
+            kept += 1u;
+        }
+        return sign | kept;
+    }
+    return sign;
+}
+
+// src/m3_op_numeric.c:114-130
+__device__ __forceinline__ float bf16_to_f32(uint32_t value) { return as_float(value << 16); }
+
+__device__ __forceinline__ uint32_t f32_to_bf16(float value)
+{
+    const uint32_t bits = as_bits(value);
+    if ((bits & 0x7f800000u) == 0x7f800000u && (bits & 0x7fffffu) != 0u) {
+        return (bits >> 16) | 0x40u;
+    }
+    return (bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16;
+}
+
+// src/m3_op_numeric.c:210-222: the value the reference reads back after
+// storing `value` in `dtype`.
+__device__ __forceinline__ float round_to(int dtype, float value)
+{
+    if (dtype == M3C_F16) {
+        return f16_to_f32(f32_to_f16(value));
+    }
+    if (dtype == M3C_BF16) {
+        return bf16_to_f32(f32_to_bf16(value));
+    }
+    return value;
+}
+
+// Widen raw storage bits of a float dtype to F32.
+__device__ __forceinline__ float widen(int dtype, uint32_t raw)
+{
+    if (dtype == M3C_F16) {
+        return f16_to_f32(raw & 0xffffu);
+    }
+    if (dtype == M3C_BF16) {
+        return bf16_to_f32(raw & 0xffffu);
+    }
+    return as_float(raw);
+}
+
+// Narrow an F32 value to the raw storage bits of `dtype`.
+__device__ __forceinline__ uint32_t narrow(int dtype, float value)
+{
+    if (dtype == M3C_F16) {
+        return f32_to_f16(value);
+    }
+    if (dtype == M3C_BF16) {
+        return f32_to_bf16(value);
+    }
+    return as_bits(value);
+}
+
+// Granlund-Montgomery division by an invariant 32-bit divisor.
+__device__ __forceinline__ uint32_t fastdiv(uint32_t n, const m3c_fastdiv &d)
+{
+    const uint64_t t = static_cast<uint64_t>(__umulhi(n, d.multiplier)) + n;
+    return static_cast<uint32_t>(t >> d.shift);
+}
+
+// Status of a session's run: has an earlier command failed?
+__device__ __forceinline__ bool run_failed(const m3c_status *status)
+{
+    return *reinterpret_cast<const volatile uint32_t *>(&status->fail_command) != 0xffffffffu;
+}
+
+__device__ __forceinline__ void record_failure(m3c_status *status, uint32_t command)
+{
+    atomicMin(&status->fail_command, command);
+    atomicExch(&status->fail_code, 2u);  // M3_STATUS_OUT_OF_RANGE
+}
+
+}  // namespace m3c

@@ -1,0 +1,185 @@
+/* Kernel parameter blocks shared by the C11 host planner and the sm_100a
+ * kernels.  Plain C structs of fixed size, passed by value as kernel
+ * parameters, so a launch needs no device-side descriptor memory. */
+
+#ifndef M3C_KERNELS_H
+#define M3C_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage dtypes: the reference numbering (include/m3.h:45-50). */
+#define M3C_F32 0
+#define M3C_F16 1
+#define M3C_BF16 2
+#define M3C_I32 3
+
+#define M3C_MAX_DIMS 8
+
+/* 32-bit division by an invariant divisor d > 0 as a multiply-high and a
+ * shift (Granlund and Montgomery, "Division by invariant integers using
+ * multiplication", PLDI 1994): q = (umulhi(n, m) + n) >> s for n < 2^32,
+ * with s = ceil(log2 d) and m = floor(2^32 * (2^s - d) / d) + 1. */
+typedef struct {
+    uint32_t divisor;
+    uint32_t multiplier;
+    uint32_t shift;
+    uint32_t reserved;
+} m3c_fastdiv;
+
+/* How an element-wise operand is addressed for a block of VEC consecutive
+ * output elements. */
+enum {
+    M3C_V_CONTIG = 0,   /* same order as the output: one vector load */
+    M3C_V_UNIFORM = 1,  /* the whole block reads one element */
+    M3C_V_GATHER = 2,   /* general strided/broadcast: per-element offsets */
+    M3C_V_IMM = 3,      /* folded scalar constant */
+    M3C_V_VECTOR = 4    /* adjacent input elements at a strided offset */
+};
+
+/* How a loaded element becomes a 32-bit register word. */
+enum {
+    M3C_LOAD_FLOAT = 0, /* widen F16/BF16/F32 to F32 */
+    M3C_LOAD_INT = 1,   /* I32 bits */
+    M3C_LOAD_RAW = 2    /* the raw storage bits (16 or 32), for exact copies */
+};
+
+/* A strided, broadcast operand addressed by the flat output index f: with the
+ * output dimensions coalesced for this operand, innermost first,
+ *   offset(f) = sum_d ((f / prod_{e<d} size_e) % size_d) * stride_d
+ * in bytes (stride 0 on broadcast dimensions). */
+typedef struct {
+    const void *base;
+    int32_t dtype;
+    int32_t load_as;
+    int32_t vclass;
+    int32_t ndim;
+    uint32_t imm_bits;
+    uint32_t reserved;
+    uint64_t size[M3C_MAX_DIMS];
+    int64_t stride[M3C_MAX_DIMS];
+    m3c_fastdiv fdiv[M3C_MAX_DIMS];
+} m3c_operand;
+
+/* Element-wise micro-operations on 32-bit register words.  Every float result
+ * is rounded to F32 and then to `rdtype` (the dtype the reference stores it
+ * in), which reproduces the reference's store-then-reload between commands. */
+enum {
+    M3C_OP_ADD = 0,     /* dst = a + b */
+    M3C_OP_MUL,         /* dst = a * b */
+    M3C_OP_GSILU,       /* dst = round_aux(a / (1 + expf(-a))) * b */
+    M3C_OP_SNAKE,       /* dst = snake1d(x = a, alpha = b) */
+    M3C_OP_TANH,        /* dst = tanhf(a) */
+    M3C_OP_ROUND,       /* dst = round_rdtype(a): float-to-float cast */
+    M3C_OP_F2I,         /* dst = (int32)trunc(a), range-checked */
+    M3C_OP_I2F,         /* dst = round_rdtype((float)(int32)a) */
+    M3C_OP_WIDEN,       /* dst = widen raw 16-bit word of dtype aux */
+    M3C_OP_CLAMP,       /* dst = bits-preserving clamp of F32 a to [-1,1] */
+    M3C_OP_MOV,         /* dst = a (raw word) */
+    M3C_OP_ABSMAX       /* reduce |a| (bits) into the group's max word */
+};
+
+typedef struct {
+    uint8_t code;
+    uint8_t dst;
+    uint8_t a;
+    uint8_t b;
+    int8_t rdtype;      /* dtype the result is rounded to */
+    int8_t aux;         /* GSILU: gate dtype; WIDEN: source dtype */
+    uint16_t command;   /* reference command (node) index, for failures */
+} m3c_ew_op;
+
+typedef struct {
+    void *base;
+    int32_t dtype;
+    int16_t reg;
+    int16_t raw;        /* register holds raw storage bits (exact copies) */
+} m3c_ew_out;
+
+#define M3C_EW_MAX_OPERANDS 8
+#define M3C_EW_MAX_OPS 16
+#define M3C_EW_MAX_OUTPUTS 4
+#define M3C_EW_MAX_REGS 8
+
+/* Device status of a session: the first failing command and its code, and the
+ * number of runs that started clean since the last synchronise. */
+typedef struct {
+    uint32_t fail_command;  /* UINT32_MAX when clean */
+    uint32_t fail_code;
+    uint32_t runs_started;
+    uint32_t reserved;
+} m3c_status;
+
+/* Reduction scratch of one launch: the running abs-max bit pattern and the
+ * count of finished CTAs (the last CTA publishes and resets both). */
+typedef struct {
+    uint32_t max_bits;
+    uint32_t done_ctas;
+} m3c_reduce_scratch;
+
+typedef struct {
+    uint64_t count;                 /* output elements */
+    int32_t n_operands;
+    int32_t n_ops;
+    int32_t n_outputs;
+    int32_t first_of_run;           /* count this run in status->runs_started */
+    m3c_status *status;
+    /* abs-max reduction (n_ops contains one M3C_OP_ABSMAX) */
+    m3c_reduce_scratch *reduce;
+    void *absmax_out;               /* one F32 element */
+    uint32_t absmax_command;
+    uint32_t reserved;
+    m3c_operand operands[M3C_EW_MAX_OPERANDS];
+    m3c_ew_op ops[M3C_EW_MAX_OPS];
+    m3c_ew_out outputs[M3C_EW_MAX_OUTPUTS];
+} m3c_ew_params;
+
+/* Row kernels over the last axis of a contiguous [rows, width] tensor. */
+typedef struct {
+    const void *input;          /* [rows, width] */
+    int32_t in_dtype;
+    int32_t first_of_run;
+    uint64_t rows;
+    uint64_t width;
+    m3c_status *status;
+    /* softmax output (NULL: none) */
+    void *probs;
+    int32_t probs_dtype;
+    uint32_t softmax_command;
+    /* top-k outputs (NULL: none) */
+    float *top_values;          /* [rows, k] F32 */
+    int32_t *top_indices;       /* [rows, k] I32 */
+    uint64_t k;
+    uint32_t topk_command;
+    uint32_t reserved;
+} m3c_softmax_params;
+
+typedef struct {
+    /* input = x, or x = round_in(resid_a + resid_b) when resid_b != NULL */
+    const void *x;
+    const void *resid_b;
+    void *sum_out;              /* write x (the residual sum) here if non-NULL */
+    int32_t in_dtype;
+    int32_t first_of_run;
+    const void *scale;          /* [width] */
+    int32_t scale_dtype;
+    int32_t out_dtype;
+    const void *bias;           /* [width] or NULL (LayerNorm only) */
+    int32_t bias_dtype;
+    int32_t layer_norm;         /* 0: RMSNorm, 1: LayerNorm */
+    void *out;
+    uint64_t rows;
+    uint64_t width;
+    float epsilon;
+    uint32_t reserved;
+    m3c_status *status;
+} m3c_norm_params;
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,162 @@
+// Utility kernels: seeded input generation and the standalone data scans used
+// by the backend plug-in path (where outputs cannot be double-buffered).
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "m3c_device.cuh"
+#include "m3c_kernels.h"
+
+namespace m3c {
+namespace {
+
+constexpr uint64_t PCG_MULTIPLIER = 6364136223846793005ull;
+
+struct Pcg {
+    uint64_t state;
+    uint64_t increment;
+};
+
+// PCG32 XSH-RR output of the reference (src/m3_rng.c:9-20).
+__device__ __forceinline__ uint32_t pcg_next(Pcg &rng)
+{
+    const uint64_t old = rng.state;
+    rng.state = old * PCG_MULTIPLIER + rng.increment;
+    const uint32_t shifted = static_cast<uint32_t>(((old >> 18u) ^ old) >> 27u);
+    const uint32_t rotation = static_cast<uint32_t>(old >> 59u);
+    return (shifted >> rotation) | (shifted << ((0u - rotation) & 31u));
+}
+
+// Seeding of src/m3_rng.c:22-39.
+__device__ __forceinline__ Pcg pcg_seed(uint64_t seed, uint64_t sequence)
+{
+    Pcg rng{0u, (sequence << 1u) | 1u};
+    (void)pcg_next(rng);
+    rng.state += seed;
+    (void)pcg_next(rng);
+    return rng;
+}
+
+// Advance an LCG by `delta` steps in O(log delta) (F. Brown, "Random number
+// generation with arbitrary strides", Trans. Am. Nucl. Soc. 71, 1994).
+__device__ __forceinline__ void pcg_advance(Pcg &rng, uint64_t delta)
+{
+    uint64_t acc_mult = 1u;
+    uint64_t acc_plus = 0u;
+    uint64_t cur_mult = PCG_MULTIPLIER;
+    uint64_t cur_plus = rng.increment;
+    while (delta > 0u) {
+        if (delta & 1u) {
+            acc_mult *= cur_mult;
+            acc_plus = acc_plus * cur_mult + cur_plus;
+        }
+        cur_plus = (cur_mult + 1u) * cur_plus;
+        cur_mult *= cur_mult;
+        delta >>= 1u;
+    }
+    rng.state = acc_mult * rng.state + acc_plus;
+}
+
+constexpr uint64_t CHUNK = 1024;  // values per thread
+
+__global__ void uniform_kernel(uint64_t seed, uint64_t sequence, float low, float high, float *out,
+                               uint64_t count)
+{
+    const uint64_t first = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * CHUNK;
+    if (first >= count) return;
+    Pcg rng = pcg_seed(seed, sequence);
+    pcg_advance(rng, first);
+    const float span = __fsub_rn(high, low);
+    const uint64_t end = first + CHUNK < count ? first + CHUNK : count;
+    for (uint64_t i = first; i < end; ++i) {
+        // src/m3_rng.c:53-66, then scaled: low + (high - low) * u
+        const float u = __fmul_rn(__uint2float_rn(pcg_next(rng) >> 8u), 0x1p-24f);
+        out[i] = __fadd_rn(low, __fmul_rn(span, u));
+    }
+}
+
+__global__ void normal_kernel(uint64_t seed, uint64_t sequence, float mean, float deviation,
+                              float *out, uint64_t count)
+{
+    // values come in pairs from two draws; CHUNK is even so pairs never split
+    const uint64_t first = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * CHUNK;
+    if (first >= count) return;
+    Pcg rng = pcg_seed(seed, sequence);
+    pcg_advance(rng, first);
+    const uint64_t end = first + CHUNK < count ? first + CHUNK : count;
+    for (uint64_t i = first; i < end; i += 2) {
+        // Box-Muller in double, src/m3_rng.c:68-110
+        const double radius_u = (static_cast<double>(pcg_next(rng)) + 0.5) * 0x1p-32;
+        const double angle_u = static_cast<double>(pcg_next(rng)) * 0x1p-32;
+        const double radius = sqrt(-2.0 * log(radius_u));
+        const double angle = 6.283185307179586476925286766559 * angle_u;
+        const float z0 = static_cast<float>(radius * cos(angle));
+        const float z1 = static_cast<float>(radius * sin(angle));
+        out[i] = __fadd_rn(mean, __fmul_rn(deviation, z0));
+        if (i + 1 < end) out[i + 1] = __fadd_rn(mean, __fmul_rn(deviation, z1));
+    }
+}
+
+// Whole-tensor data check for one command: NaN (mode 0) or a value that is
+// not a valid float-to-I32 cast source (mode 1).  Contiguous input.
+__global__ void scan_kernel(const void *data, int dtype, uint64_t count, int mode, uint32_t command,
+                            m3c_status *status)
+{
+    bool bad = false;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += stride) {
+        float v;
+        if (dtype == M3C_F16 || dtype == M3C_BF16) {
+            v = widen(dtype, static_cast<const uint16_t *>(data)[i]);
+        } else {
+            v = as_float(static_cast<const uint32_t *>(data)[i]);
+        }
+        bad |= mode == 0 ? (v != v) : !(v >= -2147483648.0f && v < 2147483648.0f);
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31u) == 0u) {
+        record_failure(status, command);
+    }
+}
+
+}  // namespace
+}  // namespace m3c
+
+extern "C" int m3c_launch_rng_uniform(uint64_t seed, uint64_t sequence, float low, float high,
+                                      float *out, uint64_t count, void *stream)
+{
+    if (count == 0) return 0;
+    const uint64_t threads = (count + m3c::CHUNK - 1) / m3c::CHUNK;
+    const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+    m3c::uniform_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(seed, sequence, low,
+                                                                               high, out, count);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int m3c_launch_rng_normal(uint64_t seed, uint64_t sequence, float mean, float deviation,
+                                     float *out, uint64_t count, void *stream)
+{
+    if (count == 0) return 0;
+    const uint64_t threads = (count + m3c::CHUNK - 1) / m3c::CHUNK;
+    const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+    m3c::normal_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(seed, sequence, mean,
+                                                                              deviation, out, count);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int m3c_launch_scan(const void *data, int32_t dtype, uint64_t count, int mode,
+                               uint32_t command, m3c_status *status, void *stream)
+{
+    if (count == 0) return 0;
+    uint64_t grid = (count + 255) / 256;
+    if (grid > 148u * 16u) grid = 148u * 16u;
+    m3c::scan_kernel<<<static_cast<unsigned>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        data, dtype, count, mode, command, status);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" const char *m3c_cuda_error_string(int code)
+{
+    return cudaGetErrorString(static_cast<cudaError_t>(code));
+}

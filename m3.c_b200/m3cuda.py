@@ -1,0 +1,619 @@
+"""ctypes binding of libm3cuda.so (include/m3_cuda.h).
+
+The library exports the graph/session API of m3.c's include/m3.h, the
+reference backend plug-in functions and the CUDA extensions.  This module
+mirrors those C types and wraps the graph/session API in two small classes.
+The wrappers only need the m3.h ABI, so `Graph(lib=...)`/`Session(lib=...)`
+also drive any other library exporting the same API.
+
+Loading fails loudly when libm3cuda.so is missing: there is no Python or CPU
+fallback for the provider.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Iterable, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(HERE, "libm3cuda.so")
+
+# include/m3.h:20-31
+OK, INVALID_ARGUMENT, OUT_OF_RANGE, OVERFLOW, OUT_OF_MEMORY = 0, 1, 2, 3, 4
+IO, INVALID_FORMAT, UNSUPPORTED, CANCELLED, INTERNAL = 5, 6, 7, 8, 9
+# include/m3.h:45-50
+F32, F16, BF16, I32 = 0, 1, 2, 3
+# include/m3.h:52-73 and the CUDA extensions
+OPS = dict(COPY=0, CAST=1, ADD=2, MUL=3, EMBEDDING=4, MATMUL=5, LINEAR=6,
+           RMS_NORM=7, LAYER_NORM=8, ROPE=9, ATTENTION=10, GATED_SILU=11,
+           SOFTMAX=12, TOP_K=13, CATEGORICAL=14, CONV1D=15,
+           CONV_TRANSPOSE1D=16, NEAREST_RESIZE1D=17, SNAKE1D=18, TANH=19,
+           ABS_MAX=64, CLAMP_UNIT=65)
+# include/m3.h:80-91
+PROVIDER_NEURAL_ENGINE, PROVIDER_METAL, PROVIDER_CPU, PROVIDER_CUDA = 0, 1, 2, 3
+INPUT, CONSTANT, TEMPORARY, OUTPUT = 0, 1, 2, 3
+VALUE_NONE = 0xFFFFFFFF
+MAX_RANK = 8
+
+NUMPY_OF = {F32: np.float32, F16: np.uint16, BF16: np.uint16, I32: np.int32}
+ITEMSIZE = {F32: 4, F16: 2, BF16: 2, I32: 4}
+
+
+class M3Error(ctypes.Structure):
+    _fields_ = [("status", ctypes.c_int), ("message", ctypes.c_char * 256)]
+
+
+class GraphValueDesc(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int), ("rank", ctypes.c_uint8),
+                ("shape", ctypes.c_uint64 * MAX_RANK), ("role", ctypes.c_int)]
+
+
+class _Norm(ctypes.Structure):
+    _fields_ = [("epsilon", ctypes.c_float)]
+
+
+class _Rope(ctypes.Structure):
+    _fields_ = [("position_offset", ctypes.c_uint64),
+                ("rotary_dimension", ctypes.c_uint32), ("mode", ctypes.c_int)]
+
+
+class _Attention(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_float), ("causal_offset", ctypes.c_int64),
+                ("causal", ctypes.c_bool)]
+
+
+class _TopK(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_uint64)]
+
+
+class _Convolution(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "groups", "stride", "dilation", "pad_left", "pad_right",
+        "output_padding")]
+
+
+class _Resize(ctypes.Structure):
+    _fields_ = [("output_length", ctypes.c_uint64)]
+
+
+class _Parameters(ctypes.Union):
+    _fields_ = [("norm", _Norm), ("rope", _Rope), ("attention", _Attention),
+                ("top_k", _TopK), ("convolution", _Convolution),
+                ("resize", _Resize)]
+
+
+class NodeDesc(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int), ("inputs", ctypes.c_uint32 * 5),
+                ("outputs", ctypes.c_uint32 * 2), ("parameters", _Parameters)]
+
+
+class SessionOptions(ctypes.Structure):
+    _fields_ = [("allow_neural_engine", ctypes.c_bool),
+                ("allow_metal", ctypes.c_bool), ("allow_cpu", ctypes.c_bool)]
+
+
+class PlanInfo(ctypes.Structure):
+    _fields_ = [("value_count", ctypes.c_size_t),
+                ("node_count", ctypes.c_size_t),
+                ("storage_slot_count", ctypes.c_size_t),
+                ("allocated_bytes", ctypes.c_size_t)]
+
+
+class CudaSessionOptions(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("stream", ctypes.c_void_p),
+                ("fuse", ctypes.c_bool), ("cuda_graphs", ctypes.c_bool)]
+
+
+class PlanReport(ctypes.Structure):
+    _fields_ = [("launch_count", ctypes.c_size_t),
+                ("fused_node_count", ctypes.c_size_t),
+                ("shadow_bytes", ctypes.c_size_t),
+                ("arena_bytes", ctypes.c_size_t)]
+
+
+# src/m3_tensor.h:12-27
+class TensorMetadata(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int), ("rank", ctypes.c_uint8),
+                ("shape", ctypes.c_uint64 * MAX_RANK),
+                ("element_count", ctypes.c_size_t),
+                ("byte_count", ctypes.c_size_t)]
+
+
+class TensorView(ctypes.Structure):
+    _fields_ = [("metadata", TensorMetadata), ("byte_offset", ctypes.c_size_t),
+                ("byte_strides", ctypes.c_size_t * MAX_RANK),
+                ("storage", ctypes.c_void_p)]
+
+
+_VP = ctypes.POINTER(TensorView)
+
+
+class _Unary(ctypes.Structure):
+    _fields_ = [("input", _VP), ("output", _VP)]
+
+
+class _Binary(ctypes.Structure):
+    _fields_ = [("left", _VP), ("right", _VP), ("output", _VP)]
+
+
+class _RmsNorm(ctypes.Structure):
+    _fields_ = [("input", _VP), ("scale", _VP), ("output", _VP),
+                ("epsilon", ctypes.c_float)]
+
+
+class _LayerNorm(ctypes.Structure):
+    _fields_ = [("input", _VP), ("scale", _VP), ("bias", _VP),
+                ("output", _VP), ("epsilon", ctypes.c_float)]
+
+
+class _TopKCommand(ctypes.Structure):
+    _fields_ = [("logits", _VP), ("values", _VP), ("indices", _VP),
+                ("k", ctypes.c_uint64)]
+
+
+class _Snake(ctypes.Structure):
+    _fields_ = [("input", _VP), ("alpha", _VP), ("output", _VP)]
+
+
+class _ConvTranspose(ctypes.Structure):
+    # the largest member of the reference union (src/m3_op.h:105-116)
+    _fields_ = [("input", _VP), ("weight", _VP), ("bias", _VP),
+                ("output", _VP)] + [(n, ctypes.c_uint64) for n in (
+                    "groups", "stride", "dilation", "pad_left", "pad_right",
+                    "output_padding")]
+
+
+class _Descriptor(ctypes.Union):
+    _fields_ = [("copy", _Unary), ("cast", _Unary), ("add", _Binary),
+                ("mul", _Binary), ("rms_norm", _RmsNorm),
+                ("layer_norm", _LayerNorm), ("gated_silu", _Binary),
+                ("softmax", _Unary), ("top_k", _TopKCommand),
+                ("snake1d", _Snake), ("tanh", _Unary),
+                ("conv_transpose1d", _ConvTranspose)]
+
+
+class Command(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int), ("descriptor", _Descriptor)]
+
+
+STORAGE_DATA = ctypes.CFUNCTYPE(ctypes.c_void_p, ctypes.c_void_p)
+
+
+class BackendOptions(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("storage_data", STORAGE_DATA),
+                ("managed_memory", ctypes.c_bool)]
+
+
+class M3Failure(RuntimeError):
+    """A non-OK m3_status, with the library's message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+_library = None
+
+_SIGNATURES = {
+    "m3_version": (ctypes.c_char_p, []),
+    "m3_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "m3_graph_value_desc_init": (None, [ctypes.POINTER(GraphValueDesc),
+                                        ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_uint8,
+                                        ctypes.POINTER(ctypes.c_uint64)]),
+    "m3_graph_node_desc_init": (None, [ctypes.POINTER(NodeDesc), ctypes.c_int]),
+    "m3_session_options_init": (None, [ctypes.POINTER(SessionOptions)]),
+    "m3_graph_create": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p),
+                                       ctypes.POINTER(M3Error)]),
+    "m3_graph_free": (None, [ctypes.c_void_p]),
+    "m3_graph_add_value": (ctypes.c_int, [ctypes.c_void_p,
+                                          ctypes.POINTER(GraphValueDesc),
+                                          ctypes.POINTER(ctypes.c_uint32),
+                                          ctypes.POINTER(M3Error)]),
+    "m3_graph_set_constant": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32,
+                                             ctypes.c_void_p, ctypes.c_size_t,
+                                             ctypes.POINTER(M3Error)]),
+    "m3_graph_add_inferred_value": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.POINTER(NodeDesc), ctypes.c_size_t,
+        ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32),
+        ctypes.POINTER(M3Error)]),
+    "m3_graph_add_node": (ctypes.c_int, [ctypes.c_void_p,
+                                         ctypes.POINTER(NodeDesc),
+                                         ctypes.POINTER(M3Error)]),
+    "m3_session_create": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.c_void_p,
+                                         ctypes.POINTER(SessionOptions),
+                                         ctypes.POINTER(M3Error)]),
+    "m3_session_free": (None, [ctypes.c_void_p]),
+    "m3_session_write_input": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32,
+                                              ctypes.c_void_p, ctypes.c_size_t,
+                                              ctypes.POINTER(M3Error)]),
+    "m3_session_read_output": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32,
+                                              ctypes.c_void_p, ctypes.c_size_t,
+                                              ctypes.POINTER(M3Error)]),
+    "m3_session_run": (ctypes.c_int, [ctypes.c_void_p,
+                                      ctypes.POINTER(M3Error)]),
+    "m3_session_get_plan_info": (ctypes.c_int, [ctypes.c_void_p,
+                                                ctypes.POINTER(PlanInfo),
+                                                ctypes.POINTER(M3Error)]),
+    "m3_session_get_node_provider": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int),
+        ctypes.POINTER(M3Error)]),
+}
+
+_CUDA_SIGNATURES = {
+    "m3_cuda_session_options_init": (None, [ctypes.POINTER(CudaSessionOptions)]),
+    "m3_cuda_session_create": (ctypes.c_int, [
+        ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
+        ctypes.POINTER(SessionOptions), ctypes.POINTER(CudaSessionOptions),
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_run_async": (ctypes.c_int, [ctypes.c_void_p,
+                                                 ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_synchronize": (ctypes.c_int, [ctypes.c_void_p,
+                                                   ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_value_device_pointer": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p),
+        ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_write_input_device": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_read_output_device": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_swap_values": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "m3_cuda_session_device": (ctypes.c_int, [ctypes.c_void_p]),
+    "m3_cuda_session_get_plan_report": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.POINTER(PlanReport), ctypes.c_char_p,
+        ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_graph_plan": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.POINTER(CudaSessionOptions),
+        ctypes.POINTER(PlanInfo), ctypes.POINTER(PlanReport), ctypes.c_char_p,
+        ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_context_create": (ctypes.c_int, [
+        ctypes.POINTER(BackendOptions), ctypes.POINTER(ctypes.c_void_p),
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_destroy_context": (None, [ctypes.c_void_p]),
+    "m3_cuda_backend_allocate": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_free_storage": (None, [ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p]),
+    "m3_cuda_backend_execute": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.POINTER(Command), ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_write": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_read": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_backend_supports_kind": (ctypes.c_bool, [ctypes.c_int]),
+    "m3_cuda_fill_uniform_host": (ctypes.c_int, [
+        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_fill_normal_host": (ctypes.c_int, [
+        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(M3Error)]),
+    "m3_cuda_fill_uniform_device": (ctypes.c_int, [
+        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_fill_normal_device": (ctypes.c_int, [
+        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_device_count": (ctypes.c_int, []),
+}
+
+
+def bind(lib: ctypes.CDLL, cuda: bool = True) -> ctypes.CDLL:
+    """Declare argument and result types on a loaded m3.h library."""
+    table = dict(_SIGNATURES)
+    if cuda:
+        table.update(_CUDA_SIGNATURES)
+    for name, (restype, argtypes) in table.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    return lib
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load libm3cuda.so (once).  Raises when it has not been built."""
+    global _library
+    if path is None and _library is not None:
+        return _library
+    target = path or LIBRARY_PATH
+    if not os.path.exists(target):
+        raise FileNotFoundError(
+            f"{target} is missing: build it with `make -C {HERE}` "
+            "(the CUDA provider has no fallback)")
+    lib = bind(ctypes.CDLL(target, mode=ctypes.RTLD_LOCAL), cuda=True)
+    if path is None:
+        _library = lib
+    return lib
+
+
+def check(status: int, error: M3Error) -> None:
+    if status != OK:
+        raise M3Failure(status, error.message.decode(errors="replace"))
+
+
+class Graph:
+    """m3_graph of include/m3.h:209-229."""
+
+    def __init__(self, lib: ctypes.CDLL | None = None):
+        self.lib = lib or load()
+        self.handle = ctypes.c_void_p()
+        self.values: list[tuple[int, tuple[int, ...], int]] = []
+        err = M3Error()
+        check(self.lib.m3_graph_create(ctypes.byref(self.handle),
+                                       ctypes.byref(err)), err)
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.m3_graph_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def value(self, role: int, dtype: int, shape: Sequence[int]) -> int:
+        desc = GraphValueDesc()
+        dims = (ctypes.c_uint64 * MAX_RANK)(*shape)
+        self.lib.m3_graph_value_desc_init(ctypes.byref(desc), role, dtype,
+                                          len(shape), dims)
+        out = ctypes.c_uint32()
+        err = M3Error()
+        check(self.lib.m3_graph_add_value(self.handle, ctypes.byref(desc),
+                                          ctypes.byref(out),
+                                          ctypes.byref(err)), err)
+        self.values.append((dtype, tuple(shape), role))
+        return out.value
+
+    def constant(self, dtype: int, array: np.ndarray) -> int:
+        array = np.ascontiguousarray(array)
+        vid = self.value(CONSTANT, dtype, array.shape)
+        err = M3Error()
+        check(self.lib.m3_graph_set_constant(
+            self.handle, vid, array.ctypes.data_as(ctypes.c_void_p),
+            array.nbytes, ctypes.byref(err)), err)
+        return vid
+
+    @staticmethod
+    def node_desc(kind: str | int, inputs: Iterable[int],
+                  outputs: Iterable[int], epsilon: float | None = None,
+                  k: int | None = None) -> NodeDesc:
+        desc = NodeDesc()
+        desc.kind = OPS[kind] if isinstance(kind, str) else kind
+        for i in range(5):
+            desc.inputs[i] = VALUE_NONE
+        for i in range(2):
+            desc.outputs[i] = VALUE_NONE
+        for i, v in enumerate(inputs):
+            desc.inputs[i] = v
+        for i, v in enumerate(outputs):
+            desc.outputs[i] = v
+        if epsilon is not None:
+            desc.parameters.norm.epsilon = epsilon
+        if k is not None:
+            desc.parameters.top_k.k = k
+        return desc
+
+    def node(self, kind: str | int, inputs: Iterable[int],
+             outputs: Iterable[int], **params) -> None:
+        desc = self.node_desc(kind, inputs, outputs, **params)
+        err = M3Error()
+        check(self.lib.m3_graph_add_node(self.handle, ctypes.byref(desc),
+                                         ctypes.byref(err)), err)
+
+    def _shape_of(self, kind: int, inputs: list[int], k: int | None):
+        """Python-side copy of the inferred shape, for read-buffer sizing."""
+        first = self.values[inputs[0]][1]
+        if kind in (OPS["ADD"], OPS["MUL"]):
+            return tuple(np.broadcast_shapes(first, self.values[inputs[1]][1]))
+        if kind == OPS["TOP_K"]:
+            return first[:-1] + (k,)
+        if kind == OPS["ABS_MAX"]:
+            return (1,)
+        return first
+
+    def inferred(self, kind: str | int, inputs: Iterable[int], role: int,
+                 dtype: int, output_index: int = 0, **params) -> int:
+        inputs = list(inputs)
+        desc = self.node_desc(kind, inputs, [], **params)
+        out = ctypes.c_uint32(VALUE_NONE)
+        err = M3Error()
+        check(self.lib.m3_graph_add_inferred_value(
+            self.handle, ctypes.byref(desc), output_index, role, dtype,
+            ctypes.byref(out), ctypes.byref(err)), err)
+        code = desc.kind
+        if code in (OPS["SNAKE1D"], OPS["TANH"], OPS["CLAMP_UNIT"],
+                    OPS["ABS_MAX"]):
+            dtype = F32
+        elif code == OPS["COPY"]:
+            dtype = self.values[inputs[0]][0]
+        elif code == OPS["TOP_K"]:
+            dtype = F32 if output_index == 0 else I32
+        self.values.append((dtype, self._shape_of(code, inputs,
+                                                  params.get("k")), role))
+        return out.value
+
+
+class Session:
+    """m3_session of include/m3.h:240-259 (plus the CUDA extensions when the
+    library is libm3cuda.so)."""
+
+    def __init__(self, graph: Graph, allow_metal: bool = True,
+                 allow_cpu: bool = True, allow_neural_engine: bool = True,
+                 device: int = -1, stream: int | None = None,
+                 fuse: bool = True, cuda: bool = True):
+        self.lib = graph.lib
+        self.values = list(graph.values)
+        self.handle = ctypes.c_void_p()
+        self.cuda = cuda
+        options = SessionOptions(allow_neural_engine, allow_metal, allow_cpu)
+        err = M3Error()
+        if cuda:
+            extra = CudaSessionOptions()
+            self.lib.m3_cuda_session_options_init(ctypes.byref(extra))
+            extra.device = device
+            extra.stream = stream
+            extra.fuse = fuse
+            status = self.lib.m3_cuda_session_create(
+                ctypes.byref(self.handle), graph.handle, ctypes.byref(options),
+                ctypes.byref(extra), ctypes.byref(err))
+        else:
+            status = self.lib.m3_session_create(
+                ctypes.byref(self.handle), graph.handle, ctypes.byref(options),
+                ctypes.byref(err))
+        check(status, err)
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.m3_session_free(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def write(self, vid: int, array: np.ndarray) -> None:
+        array = np.ascontiguousarray(array)
+        err = M3Error()
+        check(self.lib.m3_session_write_input(
+            self.handle, vid, array.ctypes.data_as(ctypes.c_void_p),
+            array.nbytes, ctypes.byref(err)), err)
+
+    def read(self, vid: int, out: np.ndarray | None = None) -> np.ndarray:
+        dtype, shape, _ = self.values[vid]
+        if out is None:
+            out = np.empty(shape, dtype=NUMPY_OF[dtype])
+        err = M3Error()
+        check(self.lib.m3_session_read_output(
+            self.handle, vid, out.ctypes.data_as(ctypes.c_void_p), out.nbytes,
+            ctypes.byref(err)), err)
+        return out
+
+    def run(self) -> None:
+        err = M3Error()
+        check(self.lib.m3_session_run(self.handle, ctypes.byref(err)), err)
+
+    def run_status(self) -> tuple[int, str]:
+        err = M3Error()
+        status = self.lib.m3_session_run(self.handle, ctypes.byref(err))
+        return status, err.message.decode(errors="replace")
+
+    def run_async(self) -> None:
+        err = M3Error()
+        check(self.lib.m3_cuda_session_run_async(self.handle,
+                                                 ctypes.byref(err)), err)
+
+    def synchronize(self) -> None:
+        err = M3Error()
+        check(self.lib.m3_cuda_session_synchronize(self.handle,
+                                                   ctypes.byref(err)), err)
+
+    def plan_info(self) -> PlanInfo:
+        info = PlanInfo()
+        err = M3Error()
+        check(self.lib.m3_session_get_plan_info(
+            self.handle, ctypes.byref(info), ctypes.byref(err)), err)
+        return info
+
+    def provider(self, node: int) -> int:
+        out = ctypes.c_int(-1)
+        err = M3Error()
+        check(self.lib.m3_session_get_node_provider(
+            self.handle, node, ctypes.byref(out), ctypes.byref(err)), err)
+        return out.value
+
+    def plan_report(self) -> tuple[PlanReport, str]:
+        report = PlanReport()
+        text = ctypes.create_string_buffer(4096)
+        err = M3Error()
+        check(self.lib.m3_cuda_session_get_plan_report(
+            self.handle, ctypes.byref(report), text, len(text),
+            ctypes.byref(err)), err)
+        return report, text.value.decode()
+
+    def device_pointer(self, vid: int) -> int:
+        ptr = ctypes.c_void_p()
+        size = ctypes.c_size_t()
+        err = M3Error()
+        check(self.lib.m3_cuda_session_value_device_pointer(
+            self.handle, vid, ctypes.byref(ptr), ctypes.byref(size),
+            ctypes.byref(err)), err)
+        return ptr.value or 0
+
+    def write_device(self, vid: int, pointer: int, nbytes: int) -> None:
+        err = M3Error()
+        check(self.lib.m3_cuda_session_write_input_device(
+            self.handle, vid, ctypes.c_void_p(pointer), nbytes,
+            ctypes.byref(err)), err)
+
+    def read_device(self, vid: int, pointer: int, nbytes: int) -> None:
+        err = M3Error()
+        check(self.lib.m3_cuda_session_read_output_device(
+            self.handle, vid, ctypes.c_void_p(pointer), nbytes,
+            ctypes.byref(err)), err)
+
+    def swap(self, input_vid: int, output_vid: int) -> None:
+        err = M3Error()
+        check(self.lib.m3_cuda_session_swap_values(
+            self.handle, input_vid, output_vid, ctypes.byref(err)), err)
+
+    @property
+    def stream(self) -> int:
+        return self.lib.m3_cuda_session_stream(self.handle) or 0
+
+
+def graph_plan(graph: Graph, fuse: bool = True):
+    """Host-only compile of a graph: (PlanInfo, PlanReport, description)."""
+    lib = graph.lib
+    options = CudaSessionOptions()
+    lib.m3_cuda_session_options_init(ctypes.byref(options))
+    options.fuse = fuse
+    info = PlanInfo()
+    report = PlanReport()
+    text = ctypes.create_string_buffer(4096)
+    err = M3Error()
+    check(lib.m3_cuda_graph_plan(graph.handle, ctypes.byref(options),
+                                 ctypes.byref(info), ctypes.byref(report),
+                                 text, len(text), ctypes.byref(err)), err)
+    return info, report, text.value.decode()
+
+
+def fill_uniform(seed: int, sequence: int, low: float, high: float,
+                 count: int) -> np.ndarray:
+    """The reference RNG's uniform stream scaled to [low, high) (host)."""
+    out = np.empty(count, dtype=np.float32)
+    err = M3Error()
+    check(load().m3_cuda_fill_uniform_host(
+        seed, sequence, low, high, out.ctypes.data_as(ctypes.c_void_p), count,
+        ctypes.byref(err)), err)
+    return out
+
+
+def fill_normal(seed: int, sequence: int, mean: float, deviation: float,
+                count: int) -> np.ndarray:
+    """The reference RNG's Box-Muller normals, mean + deviation * z (host)."""
+    out = np.empty(count, dtype=np.float32)
+    err = M3Error()
+    check(load().m3_cuda_fill_normal_host(
+        seed, sequence, mean, deviation, out.ctypes.data_as(ctypes.c_void_p),
+        count, ctypes.byref(err)), err)
+    return out

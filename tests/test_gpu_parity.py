@@ -1,0 +1,578 @@
+"""GPU parity: libm3cuda.so against the reference CPU provider.
+
+Every case builds one graph twice through the same m3.h API -- once on the
+CUDA library, once on the reference's own CPU provider compiled from its
+sources (oracle/_ref) -- feeds both the same seeded inputs, and compares:
+
+* bit-exact: ADD/MUL/CAST/COPY (incl. broadcast), residual sums, RMSNorm,
+  LayerNorm (the kernels sum in the reference's order), top-k values and
+  indices, clamp, abs-max;
+* softmax probabilities: within 1e-6 relative (F32 reduction bar);
+  the only source of difference is expf (CUDA vs glibc);
+* gated SiLU in F16/BF16: within 1 ulp of the output dtype (expf);
+* snake1d and tanh: within 0x1p-19 absolute-or-relative (sinf/tanhf),
+  the reference's own device tolerance (tests/test_metal_vocoder_activations.c:14).
+
+Where the reference has no operator (abs-max, clamp), the oracle
+restatement (oracle/m3_oracle.c) is the checker.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL_SIN = 2.0 ** -19
+
+
+def bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype.itemsize == 4 else np.uint16)
+
+
+def ordered(b: np.ndarray, width: int) -> np.ndarray:
+    """Map float bit patterns to integers whose order is the float order."""
+    b = b.astype(np.int64)
+    sign = 1 << (width - 1)
+    return np.where(b & sign, -(b & (sign - 1)), b)
+
+
+def ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    width = 8 * a.dtype.itemsize
+    return np.abs(ordered(bits(a), width) - ordered(bits(b), width))
+
+
+def close_abs_or_rel(a, b, tol) -> bool:
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    same_special = (np.isnan(a) & np.isnan(b)) | (a == b)
+    diff = np.abs(a - b)
+    ok = same_special | (diff <= tol) | (diff <= tol * np.maximum(np.abs(a), np.abs(b)))
+    return bool(ok.all())
+
+
+def run_both(m3, ref, build, inputs, fuse=True):
+    """Run `build` on both libraries; returns (cuda_outputs, reference_outputs)."""
+    results = []
+    for lib, cuda in ((m3.load(), True), (ref, False)):
+        g = m3.Graph(lib=lib)
+        handles, outputs = build(g)
+        if cuda:
+            s = m3.Session(g, fuse=fuse)
+        else:
+            s = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
+        for name, vid in handles.items():
+            s.write(vid, inputs[name])
+        s.run()
+        results.append([s.read(v) for v in outputs])
+        if cuda:
+            assert all(s.provider(i) == m3.PROVIDER_CUDA for i in range(len(g.values) and 1))
+        s.close()
+    return results
+
+
+# ------------------------------------------------------------ element-wise
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+@pytest.mark.parametrize("fuse", [True, False])
+def test_binary_broadcast_chain(m3, ref, oracle, gpu, dtype, fuse):
+    dt = getattr(m3, dtype)
+    rng = np.random.default_rng(11)
+    shape = (37, 130)          # ragged: not a multiple of the vector width
+
+    def encode(x):
+        return {"F32": x, "F16": oracle.to_f16(x), "BF16": oracle.to_bf16(x)}[dtype]
+
+    inputs = {"x": encode(rng.standard_normal(shape).astype(np.float32)),
+              "r": encode(rng.standard_normal((1, 130)).astype(np.float32)),
+              "c": encode(rng.standard_normal((37, 1)).astype(np.float32))}
+    scalar = encode(np.array([0.37], np.float32))
+
+    def build(g):
+        x = g.value(m3.INPUT, dt, shape)
+        r = g.value(m3.INPUT, dt, (1, 130))
+        c = g.value(m3.INPUT, dt, (37, 1))
+        k = g.constant(dt, scalar)
+        a = g.inferred("MUL", [x, r], m3.TEMPORARY, dt)
+        g.node("MUL", [x, r], [a])
+        b = g.inferred("ADD", [a, c], m3.TEMPORARY, dt)
+        g.node("ADD", [a, c], [b])
+        d = g.inferred("MUL", [b, k], m3.OUTPUT, dt)
+        g.node("MUL", [b, k], [d])
+        e = g.inferred("ADD", [c, d], m3.OUTPUT, m3.F32)
+        g.node("ADD", [c, d], [e])
+        return {"x": x, "r": r, "c": c}, [d, e]
+
+    mine, theirs = run_both(m3, ref, build, inputs, fuse)
+    for a, b in zip(mine, theirs):
+        assert np.array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("pair", [("F32", "F16"), ("F32", "BF16"), ("F16", "F32"),
+                                  ("BF16", "F16"), ("F16", "BF16"), ("I32", "F32"),
+                                  ("F32", "I32"), ("F16", "I32"), ("F16", "F16")])
+def test_cast_and_copy(m3, ref, oracle, gpu, pair):
+    src, dst = (getattr(m3, p) for p in pair)
+    rng = np.random.default_rng(5)
+    raw = (rng.standard_normal(1003) * 1000).astype(np.float32)
+    raw[:6] = [0.0, -0.0, 1e-8, -65520.0, 70000.0, 2.0 ** -25]
+    if src == m3.F32:
+        x = raw
+    elif src == m3.I32:
+        x = raw.astype(np.int32)
+    elif src == m3.F16:
+        x = oracle.to_f16(raw)
+        x[6:10] = [0x7C00, 0x7E01, 0x7D00, 0x8001]   # inf, qNaN, sNaN payload, -subnormal
+        if dst == m3.I32:
+            x = oracle.to_f16(raw)                    # no NaN/inf for a valid I32 cast
+    else:
+        x = oracle.to_bf16(raw)
+
+    def build(g):
+        v = g.value(m3.INPUT, src, (1003,))
+        y = g.inferred("CAST", [v], m3.OUTPUT, dst)
+        g.node("CAST", [v], [y])
+        z = g.inferred("COPY", [v], m3.OUTPUT, src)
+        g.node("COPY", [v], [z])
+        return {"x": v}, [y, z]
+
+    mine, theirs = run_both(m3, ref, build, {"x": x})
+    for a, b in zip(mine, theirs):
+        assert np.array_equal(bits(a) if a.dtype != np.int32 else a,
+                              bits(b) if b.dtype != np.int32 else b)
+
+
+def test_cast_to_i32_failure_is_atomic(m3, gpu):
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (4,))
+    y = g.inferred("CAST", [x], m3.OUTPUT, m3.I32)
+    g.node("CAST", [x], [y])
+    s = m3.Session(g)
+    s.write(x, np.array([2.9, -2.9, 7.5, -0.5], np.float32))
+    s.run()
+    assert list(s.read(y)) == [2, -2, 7, 0]
+    # tests/test_op_basic.c:141-158: any invalid value fails the whole cast
+    s.write(x, np.array([np.nan, 1.0, np.inf, 2147483648.0], np.float32))
+    status, message = s.run_status()
+    assert status == m3.OUT_OF_RANGE and "I32" in message
+    assert list(s.read(y)) == [2, -2, 7, 0]
+    s.write(x, np.array([1.5, 2.5, 3.5, 4.5], np.float32))
+    s.run()
+    assert list(s.read(y)) == [1, 2, 3, 4]
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+def test_gated_silu(m3, ref, oracle, gpu, dtype):
+    dt = getattr(m3, dtype)
+    rng = np.random.default_rng(3)
+    g32 = (rng.standard_normal((64, 257)) * 4).astype(np.float32)
+    u32 = rng.standard_normal((64, 257)).astype(np.float32)
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+
+    def build(g):
+        a = g.value(m3.INPUT, dt, (64, 257))
+        b = g.value(m3.INPUT, dt, (64, 257))
+        y = g.inferred("GATED_SILU", [a, b], m3.OUTPUT, dt)
+        g.node("GATED_SILU", [a, b], [y])
+        return {"g": a, "u": b}, [y]
+
+    (mine,), (theirs,) = run_both(m3, ref, build, {"g": enc(g32), "u": enc(u32)})
+    if dtype == "F32":
+        assert close_abs_or_rel(mine, theirs, 2.0 ** -20)
+    else:
+        assert ulp_distance(mine, theirs).max() <= 1
+
+
+def test_snake_tanh_clamp_absmax(m3, ref, oracle, gpu):
+    rng = np.random.default_rng(4)
+    x = (rng.standard_normal((2, 24, 1000)) * 0.5).astype(np.float32)
+    x[0, 0, :8] = [0.0, -0.0, 40.0, -40.0, 1e-30, 3.0, -3.0, 1e4]
+    alpha = rng.uniform(0.2, 2.0, (1, 24, 1)).astype(np.float32)
+
+    def build(g):
+        vx = g.value(m3.INPUT, m3.F32, x.shape)
+        va = g.value(m3.INPUT, m3.F32, alpha.shape)
+        z = g.inferred("SNAKE1D", [vx, va], m3.OUTPUT, m3.F32)
+        g.node("SNAKE1D", [vx, va], [z])
+        t = g.inferred("TANH", [z], m3.OUTPUT, m3.F32)
+        g.node("TANH", [z], [t])
+        return {"x": vx, "a": va}, [z, t]
+
+    (z, t), (rz, rt) = run_both(m3, ref, build, {"x": x, "a": alpha})
+    assert close_abs_or_rel(z, rz, TOL_SIN)
+    assert close_abs_or_rel(t, rt, TOL_SIN)
+
+    # extensions: abs-max over the snake output and the clamp (oracle)
+    g = m3.Graph()
+    vx = g.value(m3.INPUT, m3.F32, x.shape)
+    va = g.constant(m3.F32, alpha)
+    vz = g.inferred("SNAKE1D", [vx, va], m3.OUTPUT, m3.F32)
+    g.node("SNAKE1D", [vx, va], [vz])
+    vm = g.inferred("ABS_MAX", [vz], m3.OUTPUT, m3.F32)
+    g.node("ABS_MAX", [vz], [vm])
+    vy = g.inferred("CLAMP_UNIT", [vz], m3.OUTPUT, m3.F32)
+    g.node("CLAMP_UNIT", [vz], [vy])
+    s = m3.Session(g)
+    s.write(vx, x)
+    s.run()
+    z2, m, y = s.read(vz), s.read(vm), s.read(vy)
+    assert np.array_equal(bits(z2), bits(z))
+    om = np.zeros(1, np.float32)
+    assert oracle.run("abs_max", z2, om) == 0
+    assert bits(m)[0] == bits(om)[0]
+    oy = np.zeros_like(z2)
+    assert oracle.run("clamp_unit", z2, oy) == 0
+    assert np.array_equal(bits(y), bits(oy))
+
+
+def test_clamp_special_bits(m3, gpu):
+    source = np.array([0x40000000, 0xC0000000, 0x3F800000, 0xBF800000,
+                       0x00000000, 0x80000000, 0x00000001, 0x80000001,
+                       0x7FC12345, 0xFFC54321, 0x7F800000, 0xFF800000,
+                       0x7FA12345, 0xFFA54321], dtype=np.uint32)
+    expected = [0x3F800000, 0xBF800000, 0x3F800000, 0xBF800000, 0, 0x80000000,
+                1, 0x80000001, 0x7FC12345, 0xFFC54321, 0x3F800000, 0xBF800000,
+                0x7FA12345, 0xFFA54321]
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (14,))
+    y = g.inferred("CLAMP_UNIT", [x], m3.OUTPUT, m3.F32)
+    g.node("CLAMP_UNIT", [x], [y])
+    s = m3.Session(g)
+    s.write(x, source.view(np.float32))
+    s.run()
+    assert list(bits(s.read(y))) == expected
+
+
+def test_abs_max_nan_and_empty(m3, gpu):
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (1000,))
+    m = g.inferred("ABS_MAX", [x], m3.OUTPUT, m3.F32)
+    g.node("ABS_MAX", [x], [m])
+    s = m3.Session(g)
+    data = np.linspace(-3, 2, 1000).astype(np.float32)
+    s.write(x, data)
+    s.run()
+    assert s.read(m)[0] == 3.0
+    data[500] = np.nan
+    s.write(x, data)
+    status, _ = s.run_status()
+    assert status == m3.OUT_OF_RANGE and s.read(m)[0] == 3.0
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (0,))
+    m = g.inferred("ABS_MAX", [x], m3.OUTPUT, m3.F32)
+    g.node("ABS_MAX", [x], [m])
+    s = m3.Session(g)
+    s.run()
+    assert s.read(m)[0] == 0.0
+
+
+# ----------------------------------------------------------- row kernels
+
+
+@pytest.mark.parametrize("width", [1, 7, 128, 1000, 1024, 3000])
+@pytest.mark.parametrize("k", [1, 3])
+def test_softmax_top_k(m3, ref, gpu, width, k):
+    k = min(k, width)
+    rng = np.random.default_rng(width)
+    x = (rng.standard_normal((33, width)) * 3).astype(np.float32)
+    x[rng.random(x.shape) < 0.01] = 20.0
+    x[0, :] = -np.inf                       # all -inf row
+    if width > 2:
+        x[1, 0] = x[1, 2] = np.inf          # +inf entries split the mass
+        x[2, :] = 5.0                       # ties -> lowest indices
+        x[3, 0], x[3, 1] = -0.0, 0.0        # signed zeros compare equal
+
+    def build(g):
+        v = g.value(m3.INPUT, m3.F32, x.shape)
+        p = g.inferred("SOFTMAX", [v], m3.OUTPUT, m3.F32)
+        g.node("SOFTMAX", [v], [p])
+        tv = g.inferred("TOP_K", [v], m3.OUTPUT, m3.F32, 0, k=k)
+        ti = g.inferred("TOP_K", [v], m3.OUTPUT, m3.I32, 1, k=k)
+        g.node("TOP_K", [v], [tv, ti], k=k)
+        return {"x": v}, [p, tv, ti]
+
+    (p, tv, ti), (rp, rtv, rti) = run_both(m3, ref, build, {"x": x})
+    assert np.array_equal(bits(tv), bits(rtv)) and np.array_equal(ti, rti)
+    rel = np.abs(p.astype(np.float64) - rp) / np.maximum(np.abs(rp), 1e-30)
+    assert rel.max() <= 1e-6, rel.max()
+    assert np.array_equal(p[0], rp[0]) and np.array_equal(p[1], rp[1])
+
+
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+def test_softmax_low_precision(m3, ref, oracle, gpu, dtype):
+    dt = getattr(m3, dtype)
+    enc = oracle.to_f16 if dtype == "F16" else oracle.to_bf16
+    rng = np.random.default_rng(9)
+    x = enc((rng.standard_normal((40, 512)) * 3).astype(np.float32))
+
+    def build(g):
+        v = g.value(m3.INPUT, dt, x.shape)
+        p = g.inferred("SOFTMAX", [v], m3.OUTPUT, dt)
+        g.node("SOFTMAX", [v], [p])
+        return {"x": v}, [p]
+
+    (p,), (rp,) = run_both(m3, ref, build, {"x": x})
+    assert ulp_distance(p, rp).max() <= 1
+
+
+def test_softmax_nan_leaves_outputs_untouched(m3, gpu):
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (4, 64))
+    p = g.inferred("SOFTMAX", [x], m3.OUTPUT, m3.F32)
+    g.node("SOFTMAX", [x], [p])
+    tv = g.inferred("TOP_K", [x], m3.OUTPUT, m3.F32, 0, k=2)
+    ti = g.inferred("TOP_K", [x], m3.OUTPUT, m3.I32, 1, k=2)
+    g.node("TOP_K", [x], [tv, ti], k=2)
+    s = m3.Session(g)
+    good = np.arange(256, dtype=np.float32).reshape(4, 64) / 64
+    s.write(x, good)
+    s.run()
+    before = [s.read(v).copy() for v in (p, tv, ti)]
+    bad = good.copy()
+    bad[3, 17] = np.nan
+    s.write(x, bad)
+    status, message = s.run_status()
+    # tests/test_op_sampling.c:83-96
+    assert status == m3.OUT_OF_RANGE and message == "softmax input contains NaN"
+    after = [s.read(v) for v in (p, tv, ti)]
+    for a, b in zip(before, after):
+        assert np.array_equal(a, b)
+    # the session stays usable and commits again
+    s.write(x, good[::-1].copy())
+    s.run()
+    assert not np.array_equal(s.read(p), before[0])
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+@pytest.mark.parametrize("width", [5, 64, 2048, 3000])
+def test_residual_rms_norm_bit_exact(m3, ref, oracle, gpu, dtype, width):
+    dt = getattr(m3, dtype)
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+    rng = np.random.default_rng(width)
+    h = enc(rng.standard_normal((48, width)).astype(np.float32))
+    r = enc(rng.standard_normal((48, width)).astype(np.float32))
+    w = enc(rng.normal(1, 0.05, width).astype(np.float32))
+
+    def build(g):
+        vh = g.value(m3.INPUT, dt, h.shape)
+        vr = g.value(m3.INPUT, dt, r.shape)
+        vw = g.constant(dt, w)
+        s = g.inferred("ADD", [vh, vr], m3.OUTPUT, dt)
+        g.node("ADD", [vh, vr], [s])
+        n = g.inferred("RMS_NORM", [s, vw], m3.OUTPUT, dt, epsilon=1e-6)
+        g.node("RMS_NORM", [s, vw], [n], epsilon=1e-6)
+        return {"h": vh, "r": vr}, [s, n]
+
+    mine, theirs = run_both(m3, ref, build, {"h": h, "r": r})
+    for a, b in zip(mine, theirs):
+        assert np.array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16"])
+@pytest.mark.parametrize("bias", [True, False])
+def test_layer_norm_bit_exact(m3, ref, oracle, gpu, dtype, bias):
+    dt = getattr(m3, dtype)
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16}[dtype]
+    rng = np.random.default_rng(21)
+    x = enc((rng.standard_normal((40, 771)) * 2 + 0.5).astype(np.float32))
+    w = enc(rng.normal(1, 0.1, 771).astype(np.float32))
+    b = enc(rng.normal(0, 0.1, 771).astype(np.float32))
+
+    def build(g):
+        vx = g.value(m3.INPUT, dt, x.shape)
+        vw = g.constant(dt, w)
+        vb = g.constant(dt, b) if bias else m3.VALUE_NONE
+        n = g.inferred("LAYER_NORM", [vx, vw], m3.OUTPUT, m3.F32, epsilon=1e-5)
+        g.node("LAYER_NORM", [vx, vw, vb], [n], epsilon=1e-5)
+        return {"x": vx}, [n]
+
+    (n,), (rn,) = run_both(m3, ref, build, {"x": x})
+    assert np.array_equal(bits(n), bits(rn))
+
+
+# -------------------------------------------------------- session runtime
+
+
+def test_liveness_graph_and_plan_info(m3, gpu):
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (4,))
+    c = np.array([0.5, -1, 2, 3], np.float32)
+    vc = g.constant(m3.F32, c)
+    a = g.inferred("ADD", [x, vc], m3.TEMPORARY, m3.F32)
+    g.node("ADD", [x, vc], [a])
+    t = g.inferred("TANH", [a], m3.TEMPORARY, m3.F32)
+    g.node("TANH", [a], [t])
+    m = g.inferred("MUL", [t, vc], m3.TEMPORARY, m3.F32)
+    g.node("MUL", [t, vc], [m])
+    y = g.inferred("ADD", [m, x], m3.OUTPUT, m3.F32)
+    g.node("ADD", [m, x], [y])
+    s = m3.Session(g)
+    g.close()                                   # the session outlives its graph
+    info = s.plan_info()
+    assert (info.value_count, info.node_count, info.storage_slot_count,
+            info.allocated_bytes) == (6, 4, 5, 80)
+    assert all(s.provider(i) == m3.PROVIDER_CUDA for i in range(4))
+    data = np.array([1.0, 2.0, -3.0, 0.25], np.float32)
+    s.write(x, data)
+    s.run()
+    out = s.read(y)
+    expect = np.tanh(data + c) * c + data        # tests/test_graph_runtime.c:140-146
+    assert np.allclose(out, expect, rtol=1e-6)
+    # role and size checks (tests/test_graph_runtime.c:148-160)
+    with pytest.raises(m3.M3Failure) as failure:
+        s.write(y, data)
+    assert failure.value.status == m3.INVALID_ARGUMENT
+    with pytest.raises(m3.M3Failure) as failure:
+        s.write(x, data[:3])
+    assert failure.value.status == m3.INVALID_ARGUMENT
+
+
+def test_async_runs_and_swap_carry_state(m3, ref, gpu):
+    """Thirty Euler steps carried on the device (run_async + swap) equal
+    thirty synchronous runs with host round trips."""
+    rng = np.random.default_rng(3)
+    shape = (2, 8, 96)
+    x0, vc, vu = (rng.standard_normal(shape).astype(np.float32) for _ in range(3))
+
+    def build(g):
+        x = g.value(m3.INPUT, m3.F32, shape)
+        c = g.value(m3.INPUT, m3.F32, shape)
+        u = g.value(m3.INPUT, m3.F32, shape)
+        k1 = g.constant(m3.F32, np.array([-1], np.float32))
+        kg = g.constant(m3.F32, np.array([4], np.float32))
+        kd = g.constant(m3.F32, np.array([1.0 / 30.0], np.float32))
+        a = g.inferred("MUL", [u, k1], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [u, k1], [a])
+        a2 = g.inferred("ADD", [c, a], m3.TEMPORARY, m3.F32)
+        g.node("ADD", [c, a], [a2])
+        a3 = g.inferred("MUL", [a2, kg], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [a2, kg], [a3])
+        v = g.inferred("ADD", [u, a3], m3.TEMPORARY, m3.F32)
+        g.node("ADD", [u, a3], [v])
+        t = g.inferred("MUL", [v, kd], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [v, kd], [t])
+        xn = g.inferred("ADD", [x, t], m3.OUTPUT, m3.F32)
+        g.node("ADD", [x, t], [xn])
+        xb = g.inferred("CAST", [xn], m3.OUTPUT, m3.BF16)
+        g.node("CAST", [xn], [xb])
+        return x, c, u, xn, xb
+
+    rg = m3.Graph(lib=ref)
+    rx, rc, ru, rxn, rxb = build(rg)
+    rs = m3.Session(rg, allow_metal=False, allow_neural_engine=False, cuda=False)
+    rs.write(rc, vc)
+    rs.write(ru, vu)
+    state = x0
+    for _ in range(30):
+        rs.write(rx, state)
+        rs.run()
+        state = rs.read(rxn).copy()
+    ref_bf16 = rs.read(rxb)
+
+    g = m3.Graph()
+    x, c, u, xn, xb = build(g)
+    s = m3.Session(g)
+    s.write(c, vc)
+    s.write(u, vu)
+    s.write(x, x0)
+    for step in range(30):
+        s.run_async()
+        if step != 29:
+            s.swap(x, xn)
+    s.synchronize()
+    assert np.array_equal(bits(s.read(xn)), bits(state))
+    assert np.array_equal(s.read(xb), ref_bf16)
+
+
+# ------------------------------------------------- backend plug-in path
+
+
+def test_backend_plugin_strided_commands(m3, oracle, gpu):
+    """The vtable functions run reference-layout commands on strided views."""
+    import ctypes
+
+    lib = m3.load()
+    storages = {}
+
+    @m3.STORAGE_DATA
+    def storage_data(storage):
+        return storages[storage]
+
+    options = m3.BackendOptions(0, storage_data, False)
+    context = ctypes.c_void_p()
+    err = m3.M3Error()
+    m3.check(lib.m3_cuda_backend_context_create(ctypes.byref(options),
+                                                ctypes.byref(context),
+                                                ctypes.byref(err)), err)
+
+    def allocate(nbytes):
+        handle, data = ctypes.c_void_p(), ctypes.c_void_p()
+        m3.check(lib.m3_cuda_backend_allocate(context, nbytes, 64,
+                                              ctypes.byref(handle),
+                                              ctypes.byref(data),
+                                              ctypes.byref(err)), err)
+        key = len(storages) + 1
+        storages[key] = data.value
+        return key, data.value
+
+    def view(key, dtype, shape, strides, offset=0):
+        v = m3.TensorView()
+        v.metadata.dtype = dtype
+        v.metadata.rank = len(shape)
+        count = int(np.prod(shape))
+        for i, (n, st) in enumerate(zip(shape, strides)):
+            v.metadata.shape[i] = n
+            v.byte_strides[i] = st
+        v.metadata.element_count = count
+        v.metadata.byte_count = count * m3.ITEMSIZE[dtype]
+        v.byte_offset = offset
+        v.storage = key
+        return v
+
+    # transposed [2,3] view of a [3,2] buffer + row vector [3] -> contiguous
+    backing = np.array([1, 4, 2, 5, 3, 6], np.float32)
+    k_in, p_in = allocate(backing.nbytes)
+    lib.m3_cuda_backend_write(context, p_in, 0, backing.ctypes.data, backing.nbytes,
+                              ctypes.byref(err))
+    vec = np.array([10, 20, 30], np.float32)
+    k_vec, p_vec = allocate(vec.nbytes)
+    lib.m3_cuda_backend_write(context, p_vec, 0, vec.ctypes.data, vec.nbytes,
+                              ctypes.byref(err))
+    k_out, p_out = allocate(24)
+    left = view(k_in, m3.F32, (2, 3), (4, 8))
+    right = view(k_vec, m3.F32, (3,), (4,))
+    out = view(k_out, m3.F32, (2, 3), (12, 4))
+    cmd = (m3.Command * 2)()
+    cmd[0].kind = m3.OPS["ADD"]
+    cmd[0].descriptor.add.left = ctypes.pointer(left)
+    cmd[0].descriptor.add.right = ctypes.pointer(right)
+    cmd[0].descriptor.add.output = ctypes.pointer(out)
+    cmd[1].kind = m3.OPS["SOFTMAX"]
+    cmd[1].descriptor.softmax.input = ctypes.pointer(left)
+    k_p, p_p = allocate(24)
+    probs = view(k_p, m3.F32, (2, 3), (12, 4))
+    cmd[1].descriptor.softmax.output = ctypes.pointer(probs)
+    m3.check(lib.m3_cuda_backend_execute(context, cmd, 2, None, ctypes.byref(err)), err)
+    host = np.zeros(6, np.float32)
+    lib.m3_cuda_backend_read(context, p_out, 0, host.ctypes.data, 24, ctypes.byref(err))
+    assert list(host) == [11, 22, 33, 14, 25, 36]     # tests/test_op_basic.c:214-222
+    lib.m3_cuda_backend_read(context, p_p, 0, host.ctypes.data, 24, ctypes.byref(err))
+    dense = np.lib.stride_tricks.as_strided(backing, (2, 3), (4, 8)).copy()
+    expect = np.zeros_like(dense)
+    assert oracle.run("softmax", dense, expect) == 0
+    assert np.abs(host.reshape(2, 3) - expect).max() <= 1e-6
+    # NaN: the failing command writes nothing and later commands do not run
+    sentinel = np.full(6, -7, np.float32)
+    lib.m3_cuda_backend_write(context, p_p, 0, sentinel.ctypes.data, 24, ctypes.byref(err))
+    poisoned = backing.copy()
+    poisoned[2] = np.nan
+    lib.m3_cuda_backend_write(context, p_in, 0, poisoned.ctypes.data, 24, ctypes.byref(err))
+    status = lib.m3_cuda_backend_execute(context, cmd, 2, None, ctypes.byref(err))
+    assert status == m3.OUT_OF_RANGE
+    lib.m3_cuda_backend_read(context, p_p, 0, host.ctypes.data, 24, ctypes.byref(err))
+    assert list(host) == list(sentinel)
+    for key in list(storages):
+        lib.m3_cuda_backend_free_storage(context, storages[key], storages[key])
+    lib.m3_cuda_backend_destroy_context(context)
