@@ -596,6 +596,15 @@ m3_status m3_cuda_fill_normal_device(uint64_t seed, uint64_t sequence,
 /* Number of CUDA devices visible (0 without a driver or GPU). */
 int m3_cuda_device_count(void);
 
+/* Diagnostics: the kernels narrow F32 to F16/BF16 with the hardware
+ * round-to-nearest-even conversions and apply the reference's NaN payload
+ * rules (src/m3_op_numeric.c:55-130) in software.  This runs every F32 bit
+ * pattern (and every F16 pattern for widening) through both that path and an
+ * integer restatement of the reference encoders on `device` and reports the
+ * number of disagreements (0 expected). */
+m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches,
+                                  m3_error *error);
+
 #ifdef __cplusplus
 }
 #endif

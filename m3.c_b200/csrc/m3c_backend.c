@@ -332,10 +332,14 @@ static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
         p.absmax_out = view_base(b, out) + out->byte_offset;
         p.absmax_command = command;
     } else {
+        size_t vector_bytes = 4U * m3c_dtype_size(out->metadata.dtype);
+
         p.n_outputs = 1;
         p.outputs[0].base = view_base(b, out) + out->byte_offset;
         p.outputs[0].dtype = (int32_t)out->metadata.dtype;
         p.outputs[0].reg = (int16_t)reg;
+        p.outputs[0].scalar_only =
+            ((uintptr_t)p.outputs[0].base % vector_bytes) != 0U ? 1U : 0U;
         p.outputs[0].raw = (code == M3C_OP_MOV &&
                             m3c_dtype_size(out->metadata.dtype) == 2U)
                                ? 1

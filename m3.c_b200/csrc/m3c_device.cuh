@@ -7,6 +7,9 @@
 // conversion instructions quiet NaNs differently, so they are not used.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include <cstdint>
 
 #include "m3c_kernels.h"
@@ -84,15 +87,46 @@ __device__ __forceinline__ uint32_t f32_to_bf16(float value)
     return (bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16;
 }
 
+// Hardware forms of the same codecs.  For every non-NaN input the reference
+// encoders above are IEEE round-to-nearest-even with gradual underflow and
+// overflow to infinity, which is exactly what cvt.rn.f16.f32 and
+// cvt.rn.bf16.f32 compute, and the decoders are exact widenings, which is
+// what cvt.f32.f16 computes; only NaN payloads need the reference's own
+// rules.  m3_cuda_codec_self_test checks the two forms agree on all 2^32 F32
+// and all 2^16 F16 inputs.
+__device__ __forceinline__ uint32_t f32_to_f16_fast(float value)
+{
+    if (value != value) {
+        return f32_to_f16(value);
+    }
+    return __half_as_ushort(__float2half_rn(value));
+}
+
+__device__ __forceinline__ float f16_to_f32_fast(uint32_t half)
+{
+    if ((half & 0x7c00u) == 0x7c00u && (half & 0x3ffu) != 0u) {
+        return f16_to_f32(half);
+    }
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(half)));
+}
+
+__device__ __forceinline__ uint32_t f32_to_bf16_fast(float value)
+{
+    if (value != value) {
+        return f32_to_bf16(value);
+    }
+    return __bfloat16_as_ushort(__float2bfloat16_rn(value));
+}
+
 // src/m3_op_numeric.c:210-222: the value the reference reads back after
 // storing `value` in `dtype`.
 __device__ __forceinline__ float round_to(int dtype, float value)
 {
     if (dtype == M3C_F16) {
-        return f16_to_f32(f32_to_f16(value));
+        return f16_to_f32_fast(f32_to_f16_fast(value));
     }
     if (dtype == M3C_BF16) {
-        return bf16_to_f32(f32_to_bf16(value));
+        return bf16_to_f32(f32_to_bf16_fast(value));
     }
     return value;
 }
@@ -101,7 +135,7 @@ __device__ __forceinline__ float round_to(int dtype, float value)
 __device__ __forceinline__ float widen(int dtype, uint32_t raw)
 {
     if (dtype == M3C_F16) {
-        return f16_to_f32(raw & 0xffffu);
+        return f16_to_f32_fast(raw & 0xffffu);
     }
     if (dtype == M3C_BF16) {
         return bf16_to_f32(raw & 0xffffu);
@@ -113,10 +147,10 @@ __device__ __forceinline__ float widen(int dtype, uint32_t raw)
 __device__ __forceinline__ uint32_t narrow(int dtype, float value)
 {
     if (dtype == M3C_F16) {
-        return f32_to_f16(value);
+        return f32_to_f16_fast(value);
     }
     if (dtype == M3C_BF16) {
-        return f32_to_bf16(value);
+        return f32_to_bf16_fast(value);
     }
     return as_bits(value);
 }

@@ -1,21 +1,29 @@
 // Fused element-wise engine (sm_100a).
 //
 // One launch evaluates a straight-line program of micro-operations over the
-// flat index space of one output shape.  Every thread handles VEC = 4
-// consecutive elements per step of a grid-stride loop:
+// flat index space of one output shape.  Every thread handles blocks of
+// VEC = 4 consecutive elements in a grid-stride loop:
 //   1. load each operand for the block (a 16-byte or 8-byte vector when the
-//      operand runs in output order, one element when the block reads a
-//      single broadcast element, per-element strided/broadcast gathers
-//      otherwise, or an immediate for folded scalar constants),
+//      operand runs in output order or is a broadcast row vector, one element
+//      when the block reads a single broadcast element, per-element strided
+//      gathers otherwise, or an immediate for folded scalar constants),
 //   2. run the ops on 32-bit register words,
 //   3. store the outputs (vector stores; outputs are contiguous).
-// The program is uniform across the grid, so the op dispatch and the register
-// selection are warp-uniform switches over compile-time register indices: the
-// register file stays in registers.
+//
+// Two program forms share this code:
+//   * fixed programs -- the fusion patterns of the benchmark configurations
+//     and the single operators -- are template parameter packs of encoded
+//     ops: every opcode, register index and dtype is a compile-time
+//     constant, the dispatch folds away, and each thread keeps UNROLL blocks
+//     of loads in flight;
+//   * any other program runs the same ops from the kernel parameters through
+//     warp-uniform switches (the register file stays in registers because
+//     every switch arm names a constant register).
+// The host picks the fixed instantiation whose ops equal the planned ones.
 //
 // Arithmetic follows the reference CPU executors statement by statement with
-// F32 rounding per statement (no contraction: the library is compiled with
-// --fmad=false and the float statements below use explicit _rn intrinsics):
+// F32 rounding per statement (explicit _rn intrinsics; the library is also
+// compiled with --fmad=false):
 //   ADD/MUL       src/m3_op_execute_basic.c:61-77
 //   GATED_SILU    src/m3_op_execute_basic.c:104-122
 //   SNAKE1D       src/m3_op_execute_basic.c:183-215
@@ -26,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <initializer_list>
 
 #include "m3c_device.cuh"
 #include "m3c_kernels.h"
@@ -36,8 +45,6 @@ namespace {
 constexpr int VEC = 4;
 constexpr int THREADS = 256;
 constexpr int REGS = M3C_EW_MAX_REGS;
-
-using Word4 = uint32_t[VEC];
 
 struct RegisterFile {
     uint32_t w[REGS][VEC];
@@ -78,21 +85,27 @@ __device__ __forceinline__ int dtype_bytes(int dtype)
     return (dtype == M3C_F16 || dtype == M3C_BF16) ? 2 : 4;
 }
 
+// Byte offset of element f for index spaces of 2^32 elements or more: plain
+// 64-bit division, kept out of line (it is large and rare).
+__device__ __noinline__ int64_t wide_offset(const m3c_operand &op, uint64_t f)
+{
+    int64_t offset = 0;
+    uint64_t q = f;
+    for (int d = 0; d < op.ndim; ++d) {
+        const uint64_t next = q / op.size[d];
+        offset += static_cast<int64_t>(q - next * op.size[d]) * op.stride[d];
+        q = next;
+    }
+    return offset;
+}
+
 // Byte offset of element f of a strided/broadcast operand.
 template <bool WIDE>
 __device__ __forceinline__ int64_t operand_offset(const m3c_operand &op, uint64_t f)
 {
     int64_t offset = 0;
     if (WIDE) {
-        uint64_t q = f;
-#pragma unroll
-        for (int d = 0; d < M3C_MAX_DIMS; ++d) {
-            if (d < op.ndim) {
-                const uint64_t next = q / op.size[d];
-                offset += static_cast<int64_t>(q - next * op.size[d]) * op.stride[d];
-                q = next;
-            }
-        }
+        offset = wide_offset(op, f);
     } else {
         uint32_t q = static_cast<uint32_t>(f);
 #pragma unroll
@@ -117,6 +130,23 @@ __device__ __forceinline__ uint32_t load_one(const m3c_operand &op, int64_t offs
     return *reinterpret_cast<const uint32_t *>(p);
 }
 
+__device__ __forceinline__ void unpack_vector(const unsigned char *at, int dtype, uint32_t (&out)[VEC])
+{
+    if (dtype_bytes(dtype) == 4) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(at));
+        out[0] = v.x;
+        out[1] = v.y;
+        out[2] = v.z;
+        out[3] = v.w;
+    } else {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(at));
+        out[0] = v.x & 0xffffu;
+        out[1] = v.x >> 16;
+        out[2] = v.y & 0xffffu;
+        out[3] = v.y >> 16;
+    }
+}
+
 // Load the VEC words of a full block starting at flat index f.
 template <bool WIDE>
 __device__ __forceinline__ void load_block(const m3c_operand &op, uint64_t f, uint32_t (&out)[VEC])
@@ -127,23 +157,13 @@ __device__ __forceinline__ void load_block(const m3c_operand &op, uint64_t f, ui
         for (int j = 0; j < VEC; ++j) out[j] = op.imm_bits;
         break;
     case M3C_V_CONTIG:
-        if (dtype_bytes(op.dtype) == 4) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(
-                static_cast<const unsigned char *>(op.base) + f * 4u);
-            out[0] = v.x;
-            out[1] = v.y;
-            out[2] = v.z;
-            out[3] = v.w;
-        } else {
-            const uint2 v = *reinterpret_cast<const uint2 *>(
-                static_cast<const unsigned char *>(op.base) + f * 2u);
-            out[0] = v.x & 0xffffu;
-            out[1] = v.x >> 16;
-            out[2] = v.y & 0xffffu;
-            out[3] = v.y >> 16;
-        }
+        unpack_vector(static_cast<const unsigned char *>(op.base) +
+                          f * static_cast<uint64_t>(dtype_bytes(op.dtype)),
+                      op.dtype, out);
         break;
     case M3C_V_VECTOR: {
+        // broadcast rows are re-read by every row of the output: keep them
+        // cacheable (plain loads)
         const unsigned char *at = static_cast<const unsigned char *>(op.base) +
                                   operand_offset<WIDE>(op, f);
         if (dtype_bytes(op.dtype) == 4) {
@@ -289,13 +309,15 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
     case M3C_OP_CLAMP:
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-            // integer selects: the bits of every in-range value (NaN
-            // payloads, signed zeros) pass through unchanged
-            const float v = as_float(a[j]);
-            uint32_t w = a[j];
-            w = v > 1.0f ? 0x3f800000u : w;
-            w = v < -1.0f ? 0xbf800000u : w;
-            d[j] = w;
+            // Decided on the bit pattern alone, so no float instruction can
+            // touch the value: for a non-NaN float, v > 1 exactly when the
+            // sign is clear and the magnitude bits exceed those of 1.0 (up to
+            // +inf), and v < -1 when the sign is set likewise.  NaN payloads,
+            // signed zeros and subnormals pass through unchanged.
+            const uint32_t w = a[j];
+            const uint32_t magnitude = w & 0x7fffffffu;
+            const bool beyond = magnitude > 0x3f800000u && magnitude <= 0x7f800000u;
+            d[j] = beyond ? ((w & 0x80000000u) | 0x3f800000u) : w;
         }
         break;
     case M3C_OP_MOV:
@@ -328,9 +350,9 @@ __device__ __forceinline__ void store_block(const m3c_ew_out &out, uint64_t f, c
         uint32_t h[VEC];
 #pragma unroll
         for (int j = 0; j < VEC; ++j) h[j] = out.raw ? (w[j] & 0xffffu) : narrow(out.dtype, as_float(w[j]));
-        *reinterpret_cast<uint2 *>(p + f * 2u) = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16)));
     } else {
-        *reinterpret_cast<uint4 *>(p + f * 4u) = make_uint4(w[0], w[1], w[2], w[3]);
+        __stcs(reinterpret_cast<uint4 *>(p + f * 4u), make_uint4(w[0], w[1], w[2], w[3]));
     }
 }
 
@@ -351,12 +373,61 @@ __device__ __forceinline__ void store_partial(const m3c_ew_out &out, uint64_t f,
     }
 }
 
-template <bool WIDE>
-__device__ __forceinline__ void process(const m3c_ew_params &p, uint64_t f, int valid, Flags &flags)
+// ----------------------------------------------------------- programs
+
+// Encoded op of a fixed program: code | dst << 8 | a << 16 | b << 24 |
+// rdtype << 32 | aux << 40.
+constexpr uint64_t op_code(int code, int dst, int a, int b, int rdtype, int aux)
 {
-    RegisterFile rf;
+    return static_cast<uint64_t>(code) | (static_cast<uint64_t>(dst) << 8) |
+           (static_cast<uint64_t>(a) << 16) | (static_cast<uint64_t>(b) << 24) |
+           (static_cast<uint64_t>(static_cast<uint8_t>(rdtype)) << 32) |
+           (static_cast<uint64_t>(static_cast<uint8_t>(aux)) << 40);
+}
+
+__device__ __forceinline__ m3c_ew_op decode(uint64_t e, uint16_t command)
+{
+    m3c_ew_op op;
+    op.code = static_cast<uint8_t>(e & 0xffu);
+    op.dst = static_cast<uint8_t>((e >> 8) & 0xffu);
+    op.a = static_cast<uint8_t>((e >> 16) & 0xffu);
+    op.b = static_cast<uint8_t>((e >> 24) & 0xffu);
+    op.rdtype = static_cast<int8_t>((e >> 32) & 0xffu);
+    op.aux = static_cast<int8_t>((e >> 40) & 0xffu);
+    op.command = command;
+    return op;
+}
+
+template <int NOPERANDS, uint64_t... OPS>
+struct Fixed {
+    static constexpr int unroll = 2;
+    static constexpr int operands = NOPERANDS;
+    __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid,
+                                               Flags &flags)
+    {
+        int k = 0;
+        ((run_op(decode(OPS, p.ops[k].command), rf, valid, flags), ++k), ...);
+    }
+};
+
+struct Dynamic {
+    static constexpr int unroll = 1;
+    static constexpr int operands = M3C_EW_MAX_OPERANDS;
+    __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid,
+                                               Flags &flags)
+    {
+        for (int k = 0; k < p.n_ops; ++k) {
+            run_op(p.ops[k], rf, valid, flags);
+        }
+    }
+};
+
+template <bool WIDE, int MAX_OPERANDS>
+__device__ __forceinline__ void load_operands(const m3c_ew_params &p, uint64_t f, int valid,
+                                              RegisterFile &rf)
+{
 #pragma unroll
-    for (int i = 0; i < M3C_EW_MAX_OPERANDS && i < REGS; ++i) {
+    for (int i = 0; i < MAX_OPERANDS && i < REGS; ++i) {
         if (i < p.n_operands) {
             if (valid == VEC) {
                 load_block<WIDE>(p.operands[i], f, rf.w[i]);
@@ -365,15 +436,17 @@ __device__ __forceinline__ void process(const m3c_ew_params &p, uint64_t f, int 
             }
         }
     }
-    for (int k = 0; k < p.n_ops; ++k) {
-        run_op(p.ops[k], rf, valid, flags);
-    }
+}
+
+__device__ __forceinline__ void store_outputs(const m3c_ew_params &p, uint64_t f, int valid,
+                                              const RegisterFile &rf)
+{
 #pragma unroll
     for (int o = 0; o < M3C_EW_MAX_OUTPUTS; ++o) {
         if (o < p.n_outputs) {
             uint32_t w[VEC];
             reg_get(rf, p.outputs[o].reg, w);
-            if (valid == VEC) {
+            if (valid == VEC && !p.outputs[o].scalar_only) {
                 store_block(p.outputs[o], f, w);
             } else {
                 store_partial(p.outputs[o], f, valid, w);
@@ -382,9 +455,10 @@ __device__ __forceinline__ void process(const m3c_ew_params &p, uint64_t f, int 
     }
 }
 
-template <bool WIDE>
+template <class Prog, bool WIDE>
 __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c_ew_params p)
 {
+    constexpr int U = Prog::unroll;
     const bool skip = run_failed(p.status);
     if (p.first_of_run && !skip && blockIdx.x == 0 && threadIdx.x == 0) {
         atomicAdd(&p.status->runs_started, 1u);
@@ -392,14 +466,31 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
     Flags flags{0xffffffffu, 0u};
     if (!skip) {
         const uint64_t blocks = p.count / VEC;
-        const uint64_t stride = static_cast<uint64_t>(gridDim.x) * THREADS;
+        const uint64_t threads = static_cast<uint64_t>(gridDim.x) * THREADS;
         for (uint64_t v = static_cast<uint64_t>(blockIdx.x) * THREADS + threadIdx.x; v < blocks;
-             v += stride) {
-            process<WIDE>(p, v * VEC, VEC, flags);
+             v += threads * U) {
+            // all loads of the U blocks first, so they are in flight together
+            RegisterFile rf[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t b = v + static_cast<uint64_t>(u) * threads;
+                if (b < blocks) load_operands<WIDE, Prog::operands>(p, b * VEC, VEC, rf[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t b = v + static_cast<uint64_t>(u) * threads;
+                if (b < blocks) {
+                    Prog::run(p, rf[u], VEC, flags);
+                    store_outputs(p, b * VEC, VEC, rf[u]);
+                }
+            }
         }
         const int tail = static_cast<int>(p.count - blocks * VEC);
         if (tail != 0 && blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
-            process<WIDE>(p, blocks * VEC, tail, flags);
+            RegisterFile rf;
+            load_operands<WIDE, Prog::operands>(p, blocks * VEC, tail, rf);
+            Prog::run(p, rf, tail, flags);
+            store_outputs(p, blocks * VEC, tail, rf);
         }
     }
     if (flags.fail_command != 0xffffffffu) {
@@ -430,28 +521,137 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
     }
 }
 
+// ------------------------------------------------------ program table
+//
+// The encodings are what the planner (m3c_plan.c) emits for these graphs.
+
+#define E op_code
+#define OPS_MUL_ADD_F32 E(M3C_OP_MUL, 0, 0, 1, 0, 0), E(M3C_OP_ADD, 0, 0, 2, 0, 0)
+#define OPS_CFG_EULER_BF16                                                           \
+    E(M3C_OP_MUL, 1, 0, 1, 0, 0), E(M3C_OP_ADD, 1, 2, 1, 0, 0), E(M3C_OP_MUL, 1, 1, 3, 0, 0), \
+        E(M3C_OP_ADD, 0, 0, 1, 0, 0), E(M3C_OP_MUL, 0, 0, 4, 0, 0), E(M3C_OP_ADD, 0, 5, 0, 0, 0), \
+        E(M3C_OP_ROUND, 1, 0, 0, 2, 0)
+#define OPS_GSILU_F32 E(M3C_OP_GSILU, 0, 0, 1, 0, 0)
+#define OPS_GSILU_F16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 1), E(M3C_OP_WIDEN, 1, 1, 1, 0, 1), E(M3C_OP_GSILU, 0, 0, 1, 1, 1)
+#define OPS_GSILU_BF16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 2), E(M3C_OP_WIDEN, 1, 1, 1, 0, 2), E(M3C_OP_GSILU, 0, 0, 1, 2, 2)
+#define OPS_SNAKE_ABSMAX_CLAMP \
+    E(M3C_OP_SNAKE, 0, 0, 1, 0, 0), E(M3C_OP_ABSMAX, 0, 0, 0, 0, 0), E(M3C_OP_CLAMP, 0, 0, 0, 0, 0)
+#define OPS_SNAKE E(M3C_OP_SNAKE, 0, 0, 1, 0, 0)
+#define OPS_TANH E(M3C_OP_TANH, 0, 0, 0, 0, 0)
+#define OPS_ADD_F32 E(M3C_OP_ADD, 0, 0, 1, 0, 0)
+#define OPS_MUL_F32 E(M3C_OP_MUL, 0, 0, 1, 0, 0)
+#define OPS_ADD_F16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 1), E(M3C_OP_WIDEN, 1, 1, 1, 0, 1), E(M3C_OP_ADD, 0, 0, 1, 1, 0)
+#define OPS_MUL_F16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 1), E(M3C_OP_WIDEN, 1, 1, 1, 0, 1), E(M3C_OP_MUL, 0, 0, 1, 1, 0)
+#define OPS_ADD_BF16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 2), E(M3C_OP_WIDEN, 1, 1, 1, 0, 2), E(M3C_OP_ADD, 0, 0, 1, 2, 0)
+#define OPS_MUL_BF16 \
+    E(M3C_OP_WIDEN, 0, 0, 0, 0, 2), E(M3C_OP_WIDEN, 1, 1, 1, 0, 2), E(M3C_OP_MUL, 0, 0, 1, 2, 0)
+#define OPS_CAST_F32_F16 E(M3C_OP_ROUND, 0, 0, 0, 1, 0)
+#define OPS_CAST_F32_BF16 E(M3C_OP_ROUND, 0, 0, 0, 2, 0)
+#define OPS_CAST_F16_F32 E(M3C_OP_WIDEN, 0, 0, 0, 0, 1), E(M3C_OP_ROUND, 0, 0, 0, 0, 0)
+#define OPS_CAST_BF16_F32 E(M3C_OP_WIDEN, 0, 0, 0, 0, 2), E(M3C_OP_ROUND, 0, 0, 0, 0, 0)
+#define OPS_CLAMP E(M3C_OP_CLAMP, 0, 0, 0, 0, 0)
+#define OPS_MOV E(M3C_OP_MOV, 0, 0, 0, 0, 0)
+
+// X(operand count, ops)
+#define M3C_PROGRAMS(X)                 \
+    X(3, OPS_MUL_ADD_F32)               \
+    X(6, OPS_CFG_EULER_BF16)            \
+    X(2, OPS_GSILU_F32)                 \
+    X(2, OPS_GSILU_F16)                 \
+    X(2, OPS_GSILU_BF16)                \
+    X(2, OPS_SNAKE_ABSMAX_CLAMP)        \
+    X(2, OPS_SNAKE)                     \
+    X(1, OPS_TANH)                      \
+    X(2, OPS_ADD_F32)                   \
+    X(2, OPS_MUL_F32)                   \
+    X(2, OPS_ADD_F16)                   \
+    X(2, OPS_MUL_F16)                   \
+    X(2, OPS_ADD_BF16)                  \
+    X(2, OPS_MUL_BF16)                  \
+    X(1, OPS_CAST_F32_F16)              \
+    X(1, OPS_CAST_F32_BF16)             \
+    X(1, OPS_CAST_F16_F32)              \
+    X(1, OPS_CAST_BF16_F32)             \
+    X(1, OPS_CLAMP)                     \
+    X(1, OPS_MOV)
+
+typedef void (*ew_fn)(m3c_ew_params);
+
+struct Entry {
+    int operands;
+    int count;
+    uint64_t ops[M3C_EW_MAX_OPS];
+    ew_fn kernel;
+};
+
+constexpr int count_of(std::initializer_list<uint64_t> ops)
+{
+    return static_cast<int>(ops.size());
+}
+
+// Fixed programs cover index spaces below 2^32 elements; larger ones use the
+// generic kernel's 64-bit addressing.
+#define M3C_ENTRY(NOPERANDS, OPS) \
+    {NOPERANDS, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPS>, false>},
+
+const Entry PROGRAMS[] = {M3C_PROGRAMS(M3C_ENTRY)};
+
+#undef M3C_ENTRY
+#undef E
+
+uint64_t encode_op(const m3c_ew_op &op)
+{
+    return op_code(op.code, op.dst, op.a, op.b, op.rdtype, op.aux);
+}
+
+const Entry *find_program(const m3c_ew_params &p)
+{
+    for (const Entry &entry : PROGRAMS) {
+        if (entry.count != p.n_ops || entry.operands != p.n_operands) continue;
+        bool same = true;
+        for (int k = 0; k < p.n_ops && same; ++k) same = encode_op(p.ops[k]) == entry.ops[k];
+        if (same) return &entry;
+    }
+    return nullptr;
+}
+
+int sm_count()
+{
+    static int count = 0;
+    if (count == 0) {
+        int device = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+        if (count <= 0) count = 148;
+    }
+    return count;
+}
+
 }  // namespace
 }  // namespace m3c
 
 extern "C" int m3c_launch_ew(const m3c_ew_params *params, void *stream)
 {
-    static int sm_count = 0;
-    if (sm_count == 0) {
-        int device = 0;
-        cudaGetDevice(&device);
-        cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
-        if (sm_count <= 0) sm_count = 148;
+    const bool wide = params->count >= (1ull << 32);
+    const m3c::Entry *entry = wide ? nullptr : m3c::find_program(*params);
+    m3c::ew_fn kernel = entry != nullptr
+                            ? entry->kernel
+                            : (wide ? m3c::ew_kernel<m3c::Dynamic, true> : m3c::ew_kernel<m3c::Dynamic, false>);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, m3c::THREADS, 0) != cudaSuccess ||
+        per_sm < 1) {
+        per_sm = 1;
     }
     const uint64_t blocks_needed = (params->count / m3c::VEC + m3c::THREADS - 1) / m3c::THREADS;
-    // enough resident CTAs to cover HBM latency, a multiple of the SM count
-    const uint64_t cap = static_cast<uint64_t>(sm_count) * 8u;
+    // a persistent grid: every resident CTA of every SM, no more
+    const uint64_t cap = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(per_sm);
     uint64_t grid = blocks_needed < cap ? blocks_needed : cap;
     if (grid == 0) grid = 1;  // empty tensors still run the reduction epilogue
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (params->count >= (1ull << 32)) {
-        m3c::ew_kernel<true><<<static_cast<unsigned>(grid), m3c::THREADS, 0, s>>>(*params);
-    } else {
-        m3c::ew_kernel<false><<<static_cast<unsigned>(grid), m3c::THREADS, 0, s>>>(*params);
-    }
+    kernel<<<static_cast<unsigned>(grid), m3c::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(*params);
     return static_cast<int>(cudaGetLastError());
 }

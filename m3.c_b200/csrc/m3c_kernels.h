@@ -96,7 +96,8 @@ typedef struct {
     void *base;
     int32_t dtype;
     int16_t reg;
-    int16_t raw;        /* register holds raw storage bits (exact copies) */
+    uint8_t raw;         /* register holds raw storage bits (exact copies) */
+    uint8_t scalar_only; /* base not aligned for vector stores */
 } m3c_ew_out;
 
 #define M3C_EW_MAX_OPERANDS 8

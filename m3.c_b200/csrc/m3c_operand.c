@@ -13,6 +13,9 @@ void m3c_fastdiv_init(m3c_fastdiv *fd, uint32_t divisor)
 {
     uint32_t shift = 0U;
 
+    if (divisor == 0U) {
+        divisor = 1U;   /* never used for division: extents of 0 and 1 are dropped */
+    }
     while (shift < 32U && (UINT64_C(1) << shift) < (uint64_t)divisor) {
         ++shift;
     }
@@ -42,6 +45,11 @@ void m3c_operand_setup(m3c_operand *operand, const void *base,
     operand->base = (const unsigned char *)base + byte_offset;
     operand->dtype = (int32_t)metadata->dtype;
     operand->load_as = load_as;
+    if (out->element_count == 0U) {
+        /* nothing is read: an empty iteration space */
+        operand->vclass = M3C_V_UNIFORM;
+        return;
+    }
     /* innermost first; drop unit extents; merge axes that step evenly */
     for (axis = (int)out->rank - 1; axis >= 0; --axis) {
         uint64_t extent = out->shape[axis];

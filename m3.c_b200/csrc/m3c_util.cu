@@ -4,7 +4,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
 
+#include "m3_cuda.h"
 #include "m3c_device.cuh"
 #include "m3c_kernels.h"
 
@@ -120,8 +122,59 @@ __global__ void scan_kernel(const void *data, int dtype, uint64_t count, int mod
     }
 }
 
+// Exhaustive agreement of the hardware-assisted codecs with the integer
+// restatement of the reference's encoders: every F32 bit pattern through
+// both F16 and BF16 narrowing, every F16 pattern through widening.
+__global__ void codec_check_kernel(unsigned long long *mismatches)
+{
+    unsigned long long local = 0;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < (1ull << 32);
+         i += stride) {
+        const float v = as_float(static_cast<uint32_t>(i));
+        local += f32_to_f16_fast(v) != f32_to_f16(v) ? 1u : 0u;
+        local += f32_to_bf16_fast(v) != f32_to_bf16(v) ? 1u : 0u;
+        if (i < 65536u) {
+            local += as_bits(f16_to_f32_fast(static_cast<uint32_t>(i))) !=
+                             as_bits(f16_to_f32(static_cast<uint32_t>(i)))
+                         ? 1u
+                         : 0u;
+        }
+    }
+    if (local != 0) atomicAdd(mismatches, local);
+}
+
 }  // namespace
 }  // namespace m3c
+
+extern "C" m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches, m3_error *error)
+{
+    unsigned long long *counter = nullptr;
+    unsigned long long host = 0;
+    cudaError_t code = cudaSetDevice(device);
+    if (code == cudaSuccess) code = cudaMalloc(&counter, sizeof(*counter));
+    if (code == cudaSuccess) code = cudaMemset(counter, 0, sizeof(*counter));
+    if (code == cudaSuccess) {
+        m3c::codec_check_kernel<<<148 * 16, 256>>>(counter);
+        code = cudaGetLastError();
+    }
+    if (code == cudaSuccess) code = cudaMemcpy(&host, counter, sizeof(host), cudaMemcpyDeviceToHost);
+    if (counter != nullptr) cudaFree(counter);
+    if (code != cudaSuccess) {
+        if (error != nullptr) {
+            error->status = M3_STATUS_INTERNAL;
+            snprintf(error->message, sizeof(error->message), "codec self-test failed: %s",
+                     cudaGetErrorString(code));
+        }
+        return M3_STATUS_INTERNAL;
+    }
+    if (mismatches != nullptr) *mismatches = host;
+    if (error != nullptr) {
+        error->status = M3_STATUS_OK;
+        error->message[0] = '\0';
+    }
+    return M3_STATUS_OK;
+}
 
 extern "C" int m3c_launch_rng_uniform(uint64_t seed, uint64_t sequence, float low, float high,
                                       float *out, uint64_t count, void *stream)

@@ -311,6 +311,8 @@ _CUDA_SIGNATURES = {
         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
         ctypes.POINTER(M3Error)]),
     "m3_cuda_device_count": (ctypes.c_int, []),
+    "m3_cuda_codec_self_test": (ctypes.c_int, [
+        ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(M3Error)]),
 }
 
 
