@@ -553,6 +553,9 @@ def main():
                         help="CPU work budget of the cpu_baseline sample")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--scale", type=float, default=1.0,
+                        help="fraction of the configuration's size (profiling only; "
+                             "reported numbers use 1.0)")
     args = parser.parse_args()
     config = CONFIGS[args.config]
     if args.warmup < 3:
@@ -578,10 +581,10 @@ def main():
     torch.cuda.set_stream(stream)
 
     g = m3.Graph()
-    handles, outputs = config.build(m3, g)
+    handles, outputs = config.build(m3, g, args.scale)
     session = m3.Session(g, device=local, stream=stream.cuda_stream)
     report, plan_text = session.plan_report()
-    data = config.inputs_device(m3, torch, device)
+    data = config.inputs_device(m3, torch, device, args.scale)
     host_in = {}
     for name, vid in handles.items():
         t = data[name]
@@ -637,7 +640,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    bytes_step = config.algorithmic_bytes()
+    bytes_step = config.algorithmic_bytes(args.scale)
     value = bytes_step * world / (ms_per_step / 1e3) / 1e9
 
     # dominant kernel: one launch per run for c1/c2/c4/c5; c3's two launches
@@ -678,7 +681,9 @@ def main():
             "roofline": roofline, "cpu_baseline": baseline, "e2e": e2e,
             "clocks": clocks,
             "gpu_launches": report.launch_count * config.runs_per_step * args.steps,
-            "elems_per_s": config.elements() * world / (ms_per_step / 1e3)}
+            "elems_per_s": config.elements(args.scale) * world / (ms_per_step / 1e3)}
+    if args.scale != 1.0:
+        line["config"]["scale"] = args.scale
     session.close()
     if world > 1:
         dist.destroy_process_group()
@@ -776,7 +781,7 @@ def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, fl
         carried = host_in[config.carry[0]].nbytes * (config.runs_per_step - 1)
         h2d += carried
         d2h += carried
-    return {"value": config.algorithmic_bytes() * world / (ms / 1e3) / 1e9, "unit": "GB/s",
+    return {"value": config.algorithmic_bytes(args.scale) * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 

@@ -605,6 +605,14 @@ int m3_cuda_device_count(void);
 m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches,
                                   m3_error *error);
 
+/* Diagnostics: softmax divides by the row sum with an FMA refinement of the
+ * correctly rounded reciprocal (Markstein, IBM J. Res. Develop. 34(1), 1990)
+ * instead of the IEEE division sequence.  This draws `samples` quotients
+ * e / s with e in [2^-100, 1] and s in [1, 2^24] (the softmax domain) and
+ * reports how many differ from the IEEE division (0 expected). */
+m3_status m3_cuda_division_self_test(int device, uint64_t samples,
+                                     uint64_t *mismatches, m3_error *error);
+
 #ifdef __cplusplus
 }
 #endif

@@ -277,6 +277,8 @@ static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
     memset(&p, 0, sizeof(p));
     p.count = space->element_count;
     p.status = b->status;
+    /* a range-checked cast runs after its scan: skip when the scan failed */
+    p.skip_before = code == M3C_OP_F2I ? command + 1U : command;
     p.first_of_run = 0;
     p.n_operands = 0;
     if (a != NULL) {
@@ -351,6 +353,7 @@ static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
 /* Row operators need a dense row-major input: gather strided views into a
  * temporary device buffer. */
 static int dense_input(cuda_backend *b, const m3_tensor_view *view,
+                       uint32_t command,
                        const void **data, void **temporary)
 {
     m3_tensor_view dense;
@@ -380,6 +383,7 @@ static int dense_input(cuda_backend *b, const m3_tensor_view *view,
         memset(&p, 0, sizeof(p));
         p.count = view->metadata.element_count;
         p.status = b->status;
+        p.skip_before = command;
         p.n_operands = 1;
         m3c_operand_setup(&p.operands[0], view_base(b, view), &view->metadata,
                           view->byte_offset, view->byte_strides,
@@ -424,7 +428,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         }
         if (out->metadata.dtype == M3_DTYPE_I32) {
             const void *data;
-            code = dense_input(b, in, &data, temporary);
+            code = dense_input(b, in, index, &data, temporary);
             if (code == 0) {
                 code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
                                        in->metadata.element_count, 1, index,
@@ -477,7 +481,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         m3c_softmax_params p;
         const void *data;
 
-        code = dense_input(b, in, &data, temporary);
+        code = dense_input(b, in, index, &data, temporary);
         if (code == 0) {
             code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
                                    in->metadata.element_count, 0, index,
@@ -493,6 +497,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         p.rows = p.width ? in->metadata.element_count / p.width : 0U;
         p.status = b->status;
         p.softmax_command = UINT32_MAX;
+        p.skip_before = index + 1U;     /* after the NaN scan of this command */
         p.topk_command = UINT32_MAX;
         if (c->kind == M3_OP_SOFTMAX) {
             p.probs = view_base(b, c->descriptor.softmax.output) +
@@ -529,7 +534,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
              bias->byte_strides[0] != m3c_dtype_size(bias->metadata.dtype))) {
             return -1;  /* strided norm vectors are not supported */
         }
-        code = dense_input(b, in, &data, temporary);
+        code = dense_input(b, in, index, &data, temporary);
         if (code != 0) {
             return code;
         }
@@ -547,6 +552,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         p.out_dtype = (int32_t)out->metadata.dtype;
         p.width = in->metadata.shape[in->metadata.rank - 1U];
         p.rows = p.width ? in->metadata.element_count / p.width : 0U;
+        p.skip_before = index;
         p.epsilon = layer ? c->descriptor.layer_norm.epsilon
                           : c->descriptor.rms_norm.epsilon;
         p.status = b->status;

@@ -94,36 +94,42 @@ __device__ __forceinline__ uint32_t f32_to_bf16(float value)
 // what cvt.f32.f16 computes; only NaN payloads need the reference's own
 // rules.  m3_cuda_codec_self_test checks the two forms agree on all 2^32 F32
 // and all 2^16 F16 inputs.
+// The NaN cases are selected with integer operations, not branches, so the
+// common path stays one conversion instruction plus a few selects.
 __device__ __forceinline__ uint32_t f32_to_f16_fast(float value)
 {
-    if (value != value) {
-        return f32_to_f16(value);
-    }
-    return __half_as_ushort(__float2half_rn(value));
+    const uint32_t bits = as_bits(value);
+    const uint32_t hw = __half_as_ushort(__float2half_rn(value));
+    const uint32_t payload = (bits >> 13) & 0x3ffu;
+    const uint32_t quiet = ((bits >> 16) & 0x8000u) | 0x7e00u | payload | (payload == 0u ? 1u : 0u);
+    return (bits & 0x7fffffffu) > 0x7f800000u ? quiet : hw;
 }
 
 __device__ __forceinline__ float f16_to_f32_fast(uint32_t half)
 {
-    if ((half & 0x7c00u) == 0x7c00u && (half & 0x3ffu) != 0u) {
-        return f16_to_f32(half);
-    }
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(half)));
+    const float hw = __half2float(__ushort_as_half(static_cast<unsigned short>(half)));
+    const uint32_t nan = ((half & 0x8000u) << 16) | 0x7f800000u | ((half & 0x3ffu) << 13);
+    return (half & 0x7fffu) > 0x7c00u ? as_float(nan) : hw;
 }
 
 __device__ __forceinline__ uint32_t f32_to_bf16_fast(float value)
 {
-    if (value != value) {
-        return f32_to_bf16(value);
-    }
-    return __bfloat16_as_ushort(__float2bfloat16_rn(value));
+    const uint32_t bits = as_bits(value);
+    const uint32_t hw = __bfloat16_as_ushort(__float2bfloat16_rn(value));
+    return (bits & 0x7fffffffu) > 0x7f800000u ? ((bits >> 16) | 0x40u) : hw;
 }
 
 // src/m3_op_numeric.c:210-222: the value the reference reads back after
-// storing `value` in `dtype`.
+// storing `value` in `dtype`.  For F16 the NaN round trip keeps the top nine
+// payload bits, sets the quiet bit and never yields an all-zero payload.
 __device__ __forceinline__ float round_to(int dtype, float value)
 {
     if (dtype == M3C_F16) {
-        return f16_to_f32_fast(f32_to_f16_fast(value));
+        const uint32_t bits = as_bits(value);
+        const float hw = __half2float(__float2half_rn(value));
+        const uint32_t nan = (bits & 0xffffe000u) | 0x400000u |
+                             ((bits & 0x7fe000u) == 0u ? 0x2000u : 0u);
+        return (bits & 0x7fffffffu) > 0x7f800000u ? as_float(nan) : hw;
     }
     if (dtype == M3C_BF16) {
         return bf16_to_f32(f32_to_bf16_fast(value));
@@ -155,6 +161,21 @@ __device__ __forceinline__ uint32_t narrow(int dtype, float value)
     return as_bits(value);
 }
 
+// The correctly rounded quotient a / b from y = RN(1/b), after P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Develop. 34(1), 1990: q0 = RN(a y) is within one
+// ulp of a / b, the remainder r = a - b q0 is exact with a fused
+// multiply-add, and RN(q0 + r y) = RN(a / b) -- provided nothing under- or
+// overflows, so callers keep tiny or special operands on the IEEE division.
+// m3_cuda_division_self_test compares it with __fdiv_rn on the softmax
+// domain.
+__device__ __forceinline__ float div_markstein(float a, float b, float y)
+{
+    const float q0 = __fmul_rn(a, y);
+    const float r = __fmaf_rn(-q0, b, a);
+    return __fmaf_rn(r, y, q0);
+}
+
 // Granlund-Montgomery division by an invariant 32-bit divisor.
 __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const m3c_fastdiv &d)
 {
@@ -162,10 +183,16 @@ __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const m3c_fastdiv &d)
     return static_cast<uint32_t>(t >> d.shift);
 }
 
-// Status of a session's run: has an earlier command failed?
+// Status of a session's run: has a command before `bound` failed?
+__device__ __forceinline__ bool failed_before(const m3c_status *status, uint32_t bound)
+{
+    return *reinterpret_cast<const volatile uint32_t *>(&status->fail_command) < bound;
+}
+
+// Has any command of the run failed?
 __device__ __forceinline__ bool run_failed(const m3c_status *status)
 {
-    return *reinterpret_cast<const volatile uint32_t *>(&status->fail_command) != 0xffffffffu;
+    return failed_before(status, 0xffffffffu);
 }
 
 __device__ __forceinline__ void record_failure(m3c_status *status, uint32_t command)

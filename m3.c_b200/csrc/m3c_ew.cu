@@ -459,7 +459,7 @@ template <class Prog, bool WIDE>
 __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c_ew_params p)
 {
     constexpr int U = Prog::unroll;
-    const bool skip = run_failed(p.status);
+    const bool skip = failed_before(p.status, p.skip_before);
     if (p.first_of_run && !skip && blockIdx.x == 0 && threadIdx.x == 0) {
         atomicAdd(&p.status->runs_started, 1u);
     }
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
             __threadfence();
             const uint32_t result = atomicExch(&p.reduce->max_bits, 0u);
             atomicExch(&p.reduce->done_ctas, 0u);
-            if (!run_failed(p.status)) {
+            if (!failed_before(p.status, p.absmax_command + 1u)) {
                 *static_cast<uint32_t *>(p.absmax_out) = result;
             }
         }

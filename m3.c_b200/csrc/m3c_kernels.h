@@ -106,7 +106,10 @@ typedef struct {
 #define M3C_EW_MAX_REGS 8
 
 /* Device status of a session: the first failing command and its code, and the
- * number of runs that started clean since the last synchronise. */
+ * number of runs that started clean since the last synchronise.  A launch
+ * skips its work when a command before its `skip_before` bound has failed
+ * (an earlier command of the run), but not for failures of its own
+ * commands, so unchecked commands of a fused launch always complete. */
 typedef struct {
     uint32_t fail_command;  /* UINT32_MAX when clean */
     uint32_t fail_code;
@@ -132,7 +135,7 @@ typedef struct {
     m3c_reduce_scratch *reduce;
     void *absmax_out;               /* one F32 element */
     uint32_t absmax_command;
-    uint32_t reserved;
+    uint32_t skip_before;           /* skip when a command < this failed */
     m3c_operand operands[M3C_EW_MAX_OPERANDS];
     m3c_ew_op ops[M3C_EW_MAX_OPS];
     m3c_ew_out outputs[M3C_EW_MAX_OUTPUTS];
@@ -155,7 +158,7 @@ typedef struct {
     int32_t *top_indices;       /* [rows, k] I32 */
     uint64_t k;
     uint32_t topk_command;
-    uint32_t reserved;
+    uint32_t skip_before;       /* skip when a command < this failed */
 } m3c_softmax_params;
 
 typedef struct {
@@ -175,7 +178,7 @@ typedef struct {
     uint64_t rows;
     uint64_t width;
     float epsilon;
-    uint32_t reserved;
+    uint32_t skip_before;       /* skip when a command < this failed */
     m3c_status *status;
 } m3c_norm_params;
 

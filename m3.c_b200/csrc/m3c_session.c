@@ -445,6 +445,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         }
         p.first_of_run = first ? 1 : 0;
         p.status = s->status_device;
+        p.skip_before = (uint32_t)l->first_node;
         if (l->has_absmax) {
             p.reduce = &s->reduce[index];
             p.absmax_out = ref_pointer(s, l->absmax_out);
@@ -462,6 +463,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         p.width = in->shape[in->rank - 1U];
         p.rows = p.width ? in->element_count / p.width : 0U;
         p.status = s->status_device;
+        p.skip_before = (uint32_t)l->first_node;
         p.softmax_command = l->command_a;
         p.topk_command = l->command_b;
         if (l->row_out.value != UINT32_MAX) {
@@ -498,6 +500,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         p.rows = p.width ? in->element_count / p.width : 0U;
         p.epsilon = l->epsilon;
         p.status = s->status_device;
+        p.skip_before = (uint32_t)l->first_node;
         return m3c_launch_norm(&p, s->stream);
     }
 }

@@ -134,6 +134,8 @@ __global__ void codec_check_kernel(unsigned long long *mismatches)
         const float v = as_float(static_cast<uint32_t>(i));
         local += f32_to_f16_fast(v) != f32_to_f16(v) ? 1u : 0u;
         local += f32_to_bf16_fast(v) != f32_to_bf16(v) ? 1u : 0u;
+        local += as_bits(round_to(M3C_F16, v)) != as_bits(f16_to_f32(f32_to_f16(v))) ? 1u : 0u;
+        local += as_bits(round_to(M3C_BF16, v)) != as_bits(bf16_to_f32(f32_to_bf16(v))) ? 1u : 0u;
         if (i < 65536u) {
             local += as_bits(f16_to_f32_fast(static_cast<uint32_t>(i))) !=
                              as_bits(f16_to_f32(static_cast<uint32_t>(i)))
@@ -144,8 +146,66 @@ __global__ void codec_check_kernel(unsigned long long *mismatches)
     if (local != 0) atomicAdd(mismatches, local);
 }
 
+// Markstein quotients against __fdiv_rn on the softmax domain: numerators
+// e in [2^-100, 1] (exponentials of non-positive arguments), denominators
+// s in [1, 2^24] (a sum whose largest term is 1).  Pairs come from a
+// splitmix64 stream; every exponent of both ranges is covered.
+__global__ void division_check_kernel(uint64_t samples, unsigned long long *mismatches)
+{
+    unsigned long long local = 0;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < samples;
+         i += stride) {
+        uint64_t z = (i + 1) * 0x9e3779b97f4a7c15ull;
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+        z ^= z >> 31;
+        const uint32_t lo = static_cast<uint32_t>(z);
+        const uint32_t hi = static_cast<uint32_t>(z >> 32);
+        // e: exponent in [-100, -1] or exactly 1.0; s: exponent in [0, 23]
+        const uint32_t e_exp = 127u - 100u + (lo >> 23) % 100u;
+        float e = as_float((e_exp << 23) | (lo & 0x7fffffu));
+        if ((lo & 0xffffu) == 0u) e = 1.0f;
+        const uint32_t s_exp = 127u + (hi >> 23) % 24u;
+        const float s = as_float((s_exp << 23) | (hi & 0x7fffffu));
+        const float y = __frcp_rn(s);
+        local += as_bits(div_markstein(e, s, y)) != as_bits(__fdiv_rn(e, s)) ? 1u : 0u;
+    }
+    if (local != 0) atomicAdd(mismatches, local);
+}
+
 }  // namespace
 }  // namespace m3c
+
+extern "C" m3_status m3_cuda_division_self_test(int device, uint64_t samples, uint64_t *mismatches,
+                                                m3_error *error)
+{
+    unsigned long long *counter = nullptr;
+    unsigned long long host = 0;
+    cudaError_t code = cudaSetDevice(device);
+    if (code == cudaSuccess) code = cudaMalloc(&counter, sizeof(*counter));
+    if (code == cudaSuccess) code = cudaMemset(counter, 0, sizeof(*counter));
+    if (code == cudaSuccess) {
+        m3c::division_check_kernel<<<148 * 16, 256>>>(samples, counter);
+        code = cudaGetLastError();
+    }
+    if (code == cudaSuccess) code = cudaMemcpy(&host, counter, sizeof(host), cudaMemcpyDeviceToHost);
+    if (counter != nullptr) cudaFree(counter);
+    if (code != cudaSuccess) {
+        if (error != nullptr) {
+            error->status = M3_STATUS_INTERNAL;
+            snprintf(error->message, sizeof(error->message), "division self-test failed: %s",
+                     cudaGetErrorString(code));
+        }
+        return M3_STATUS_INTERNAL;
+    }
+    if (mismatches != nullptr) *mismatches = host;
+    if (error != nullptr) {
+        error->status = M3_STATUS_OK;
+        error->message[0] = '\0';
+    }
+    return M3_STATUS_OK;
+}
 
 extern "C" m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches, m3_error *error)
 {

@@ -313,6 +313,9 @@ _CUDA_SIGNATURES = {
     "m3_cuda_device_count": (ctypes.c_int, []),
     "m3_cuda_codec_self_test": (ctypes.c_int, [
         ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(M3Error)]),
+    "m3_cuda_division_self_test": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
+        ctypes.POINTER(M3Error)]),
 }
 
 

@@ -85,6 +85,16 @@ def test_hardware_codecs_match_reference_encoders_exhaustively(m3, gpu):
     assert mismatches.value == 0
 
 
+def test_markstein_division_matches_ieee_on_softmax_domain(m3, gpu):
+    import ctypes
+
+    mismatches = ctypes.c_uint64(12345)
+    err = m3.M3Error()
+    m3.check(m3.load().m3_cuda_division_self_test(0, 1 << 32, ctypes.byref(mismatches),
+                                                  ctypes.byref(err)), err)
+    assert mismatches.value == 0
+
+
 # ------------------------------------------------------------ element-wise
 
 
@@ -175,6 +185,33 @@ def test_cast_to_i32_failure_is_atomic(m3, gpu):
     s.write(x, np.array([1.5, 2.5, 3.5, 4.5], np.float32))
     s.run()
     assert list(s.read(y)) == [1, 2, 3, 4]
+
+
+def test_fused_failure_keeps_earlier_commands(m3, gpu):
+    """ADD then a range-checked CAST fuse into one launch.  When the cast
+    fails, the reference has already stored the ADD (it ran first), so the
+    ADD output must be complete while the cast output is unchanged."""
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (300_000,))
+    c = g.constant(m3.F32, np.array([0.5], np.float32))
+    y = g.inferred("ADD", [x, c], m3.OUTPUT, m3.F32)
+    g.node("ADD", [x, c], [y])
+    z = g.inferred("CAST", [y], m3.OUTPUT, m3.I32)
+    g.node("CAST", [y], [z])
+    s = m3.Session(g)
+    _, text = s.plan_report()
+    assert text.startswith("ew[ADD,CAST]")
+    data = np.arange(300_000, dtype=np.float32)
+    s.write(x, data)
+    s.run()
+    before_z = s.read(z).copy()
+    data2 = data * 2
+    data2[-1] = 3e9                       # out of the I32 range after the add
+    s.write(x, data2)
+    status, _ = s.run_status()
+    assert status == m3.OUT_OF_RANGE
+    assert np.array_equal(s.read(y), data2 + np.float32(0.5))
+    assert np.array_equal(s.read(z), before_z)
 
 
 @pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
