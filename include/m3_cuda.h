@@ -613,6 +613,55 @@ m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches,
 m3_status m3_cuda_division_self_test(int device, uint64_t samples,
                                      uint64_t *mismatches, m3_error *error);
 
+/* ------------------------------------------------------------------------
+ * Abs-max without allocation.  No counterpart in the reference: m3.c has no
+ * device memory to manage, so it has no allocation-free variant either.
+ *
+ * Who needs it: the session and the backend plug-in both allocate device
+ * memory for their reduction scratch (cudaMalloc at creation).  Some callers
+ * cannot do that at the point where they want a peak level: a real-time audio
+ * render thread must not call cudaMalloc or cudaFree, whose latency has no
+ * bound (they take driver locks, and cudaFree waits for the whole device to go
+ * idle); and a caller that has already divided the device's memory among its
+ * own pools has none left to hand out.  This entry point needs no memory
+ * beyond what the caller passes in: its scratch is a fixed array compiled
+ * into this library's device code.
+ *
+ * m3_cuda_abs_max_static computes M3_OP_ABS_MAX of each of `tensor_count`
+ * dense tensors of `dtype` (F32, F16 or BF16) that live on `device`:
+ * maxima[i] (device memory, 4-byte aligned, F32) receives max |x| over the
+ * element_counts[i] elements at inputs[i], exactly as a graph or backend
+ * ABS_MAX command would compute it (the same kernel and program); an empty
+ * tensor gives +0.  A tensor holding a NaN leaves its maxima[i] untouched; the
+ * others are still written, and the call returns M3_STATUS_OUT_OF_RANGE
+ * naming the first such tensor.  The work runs on `stream` (a cudaStream_t;
+ * NULL is the legacy default stream) and the call waits for that stream to
+ * finish before it returns.
+ *
+ * Limit: at most M3_CUDA_ABS_MAX_STATIC_MAX_TENSORS tensors per call (the
+ * scratch holds one reduction slot and one status word set per tensor,
+ * 24 bytes each, 1.5 KiB in all); more returns M3_STATUS_INVALID_ARGUMENT
+ * before any device work.  Each call zeroes the reduction slots it uses and
+ * resets their status words before its kernels start.
+ *
+ * The scratch is one array per device, shared by every caller in the process:
+ * two calls on the same device whose work overlaps in time (from two host
+ * threads, or on two streams) race on it and return wrong maxima.  Callers
+ * must serialise calls per device.
+ *
+ * The first call on each device looks the scratch up with
+ * cudaGetSymbolAddress, with `device` made current; that lookup can load this
+ * library's device code.  Make the first call for each device before any
+ * stream capture begins.  The calling thread's current device is restored
+ * before return. */
+#define M3_CUDA_ABS_MAX_STATIC_MAX_TENSORS 64U
+
+m3_status m3_cuda_abs_max_static(int device, void *stream, m3_dtype dtype,
+                                 const void *const *inputs,
+                                 const uint64_t *element_counts,
+                                 size_t tensor_count, float *maxima,
+                                 m3_error *error);
+
 #ifdef __cplusplus
 }
 #endif

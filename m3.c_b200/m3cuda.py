@@ -316,6 +316,10 @@ _CUDA_SIGNATURES = {
     "m3_cuda_division_self_test": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
         ctypes.POINTER(M3Error)]),
+    "m3_cuda_abs_max_static": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_uint64),
+        ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(M3Error)]),
 }
 
 
@@ -622,3 +626,21 @@ def fill_normal(seed: int, sequence: int, mean: float, deviation: float,
         seed, sequence, mean, deviation, out.ctypes.data_as(ctypes.c_void_p),
         count, ctypes.byref(err)), err)
     return out
+
+
+ABS_MAX_STATIC_MAX_TENSORS = 64
+
+
+def abs_max_static(dtype: int, pointers, counts, maxima: int, device: int = 0,
+                   stream: int = 0) -> None:
+    """m3_cuda_abs_max_static: max |x| of each device tensor into `maxima`
+    (a device F32 array), using no allocation; see include/m3_cuda.h.
+    Raises M3Failure with the library's status and message."""
+    n = len(pointers)
+    if len(counts) != n:
+        raise ValueError("one element count per input pointer")
+    inputs = (ctypes.c_void_p * max(n, 1))(*pointers)
+    sizes = (ctypes.c_uint64 * max(n, 1))(*counts)
+    err = M3Error()
+    check(load().m3_cuda_abs_max_static(device, stream, dtype, inputs, sizes,
+                                        n, maxima, ctypes.byref(err)), err)
