@@ -56,6 +56,14 @@ def oraclemod():
     return _module("m3_oracle_py", os.path.join(ROOT, "oracle", "oracle.py"))
 
 
+def shardsmod():
+    return _module("m3_shards", os.path.join(ROOT, "m3.c_b200", "shards.py"))
+
+
+# this process's rank: its input slab is drawn from its own PCG32 streams
+RANK = int(os.environ.get("RANK", "0"))
+
+
 METRIC = ("achieved HBM GB/s (fraction of B200 peak) per op; "
           "elems/s at 1/2/4/8 GPUs vs CPU")
 
@@ -354,9 +362,12 @@ def f16_bits(values: np.ndarray) -> np.ndarray:
 
 
 def fill(m3, kind, seed, sequence, a, b, tensor, stream):
+    """Device fill from the reference RNG; rank r > 0 draws its slab from the
+    rank's own streams (rank 0 uses the configuration's streams)."""
     lib = m3.load()
     err = m3.M3Error()
     fn = lib.m3_cuda_fill_normal_device if kind == "normal" else lib.m3_cuda_fill_uniform_device
+    sequence = shardsmod().shard_sequence(sequence, RANK)
     m3.check(fn(seed, sequence, a, b, ctypes.c_void_p(tensor.data_ptr()), tensor.numel(),
                 ctypes.c_void_p(stream), ctypes.byref(err)), err)
 
@@ -608,7 +619,7 @@ def main():
                 session.swap(*config.carry)
         if collective is not None:
             session.read_device(outputs[0], collective.data_ptr(), 4)
-            dist.all_reduce(collective, op=dist.ReduceOp.MAX)
+            shardsmod().global_abs_max_bits(collective)
 
     for _ in range(args.warmup):
         one_step()
@@ -636,9 +647,7 @@ def main():
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(per_step)
     if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        total_ms = shardsmod().max_over_ranks(total_ms, device)
     ms_per_step = total_ms / args.steps
     bytes_step = config.algorithmic_bytes(args.scale)
     value = bytes_step * world / (ms_per_step / 1e3) / 1e9
@@ -772,9 +781,7 @@ def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, fl
         times.append(a.elapsed_time(b))
     ms = statistics.mean(times)
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = shardsmod().max_over_ranks(ms, device)
     h2d = sum(b.nbytes for b in host_in.values())
     d2h = sum(b.nbytes for b in host_out.values())
     if config.name == "c4":
