@@ -35,6 +35,7 @@
 
 #include <cstdint>
 #include <initializer_list>
+#include <utility>
 
 #include "m3c_device.cuh"
 #include "m3c_kernels.h"
@@ -191,6 +192,91 @@ __device__ __forceinline__ void load_block(const m3c_operand &op, uint64_t f, ui
 #pragma unroll
         for (int j = 0; j < VEC; ++j) out[j] = load_one(op, operand_offset<WIDE>(op, f + j));
         break;
+    }
+}
+
+// ------------------------------------------------ compile-time signatures
+//
+// A fixed program may also fix how its operands are addressed and how its
+// outputs are stored, so that loads and stores compile to straight-line code
+// with no class, dtype or register dispatch.  Operand i is described by byte
+// i of an operand signature: vclass | dtype << 3 | (ndim - 1) << 5 (ndim only
+// for the classes that compute offsets); 0xff leaves the operand to the
+// run-time switch.  An output signature holds the output count in bits 0-3
+// and, for output o, byte o + 1 = register | dtype << 3 | raw << 5; 0 leaves
+// the outputs to run time.
+
+constexpr uint64_t ANY_OPERANDS = ~0ull;
+
+constexpr uint32_t operand_byte(int vclass, int dtype, int ndim)
+{
+    return static_cast<uint32_t>(vclass) | (static_cast<uint32_t>(dtype) << 3) |
+           (static_cast<uint32_t>(vclass == M3C_V_CONTIG || vclass == M3C_V_IMM ? 0 : ndim - 1) << 5);
+}
+
+constexpr uint32_t output_byte(int reg, int dtype, int raw)
+{
+    return static_cast<uint32_t>(reg) | (static_cast<uint32_t>(dtype) << 3) | (static_cast<uint32_t>(raw) << 5);
+}
+
+// Byte offset of element f through the first NDIM dimensions (narrow index).
+template <int NDIM>
+__device__ __forceinline__ int64_t operand_offset_c(const m3c_operand &op, uint32_t f)
+{
+    int64_t offset = 0;
+    uint32_t q = f;
+#pragma unroll
+    for (int d = 0; d < NDIM; ++d) {
+        const uint32_t next = fastdiv(q, op.fdiv[d]);
+        offset += static_cast<int64_t>(q - next * static_cast<uint32_t>(op.size[d])) * op.stride[d];
+        q = next;
+    }
+    return offset;
+}
+
+template <uint32_t SIG>
+__device__ __forceinline__ void load_block_c(const m3c_operand &op, uint64_t f, uint32_t (&out)[VEC])
+{
+    constexpr int CLS = SIG & 7u;
+    constexpr int DT = (SIG >> 3) & 3u;
+    constexpr int NDIM = static_cast<int>((SIG >> 5) & 7u) + 1;
+    constexpr int EB = DT == M3C_F16 || DT == M3C_BF16 ? 2 : 4;
+    const unsigned char *base = static_cast<const unsigned char *>(op.base);
+    if constexpr (CLS == M3C_V_IMM) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) out[j] = op.imm_bits;
+    } else if constexpr (CLS == M3C_V_CONTIG || CLS == M3C_V_VECTOR) {
+        const unsigned char *at = CLS == M3C_V_CONTIG
+                                      ? base + f * static_cast<uint64_t>(EB)
+                                      : base + operand_offset_c<NDIM>(op, static_cast<uint32_t>(f));
+        if constexpr (EB == 4) {
+            // broadcast rows are re-read by every output row: keep them
+            // cacheable; streamed operands bypass with __ldcs
+            const uint4 v = CLS == M3C_V_CONTIG ? __ldcs(reinterpret_cast<const uint4 *>(at))
+                                                : *reinterpret_cast<const uint4 *>(at);
+            out[0] = v.x;
+            out[1] = v.y;
+            out[2] = v.z;
+            out[3] = v.w;
+        } else {
+            const uint2 v = CLS == M3C_V_CONTIG ? __ldcs(reinterpret_cast<const uint2 *>(at))
+                                                : *reinterpret_cast<const uint2 *>(at);
+            out[0] = v.x & 0xffffu;
+            out[1] = v.x >> 16;
+            out[2] = v.y & 0xffffu;
+            out[3] = v.y >> 16;
+        }
+    } else if constexpr (CLS == M3C_V_UNIFORM) {
+        const unsigned char *at = base + operand_offset_c<NDIM>(op, static_cast<uint32_t>(f));
+        const uint32_t w = EB == 2 ? *reinterpret_cast<const uint16_t *>(at) : *reinterpret_cast<const uint32_t *>(at);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) out[j] = w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+            const unsigned char *at = base + operand_offset_c<NDIM>(op, static_cast<uint32_t>(f + j));
+            out[j] = EB == 2 ? *reinterpret_cast<const uint16_t *>(at) : *reinterpret_cast<const uint32_t *>(at);
+        }
     }
 }
 
@@ -356,6 +442,22 @@ __device__ __forceinline__ void store_block(const m3c_ew_out &out, uint64_t f, c
     }
 }
 
+template <uint32_t SIG>
+__device__ __forceinline__ void store_block_c(const m3c_ew_out &out, uint64_t f, const uint32_t (&w)[VEC])
+{
+    constexpr int DT = (SIG >> 3) & 3u;
+    constexpr bool RAW = ((SIG >> 5) & 1u) != 0u;
+    unsigned char *p = static_cast<unsigned char *>(out.base);
+    if constexpr (DT == M3C_F16 || DT == M3C_BF16) {
+        uint32_t h[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) h[j] = RAW ? (w[j] & 0xffffu) : narrow(DT, as_float(w[j]));
+        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16)));
+    } else {
+        __stcs(reinterpret_cast<uint4 *>(p + f * 4u), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+}
+
 __device__ __forceinline__ void store_partial(const m3c_ew_out &out, uint64_t f, int valid,
                                               const uint32_t (&w)[VEC])
 {
@@ -398,10 +500,12 @@ __device__ __forceinline__ m3c_ew_op decode(uint64_t e, uint16_t command)
     return op;
 }
 
-template <int NOPERANDS, uint64_t... OPS>
+template <int NOPERANDS, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
 struct Fixed {
     static constexpr int unroll = 2;
     static constexpr int operands = NOPERANDS;
+    static constexpr uint64_t opsig = OPSIG;
+    static constexpr uint64_t outsig = OUTSIG;
     __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid,
                                                Flags &flags)
     {
@@ -413,6 +517,8 @@ struct Fixed {
 struct Dynamic {
     static constexpr int unroll = 1;
     static constexpr int operands = M3C_EW_MAX_OPERANDS;
+    static constexpr uint64_t opsig = ANY_OPERANDS;
+    static constexpr uint64_t outsig = 0u;
     __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid,
                                                Flags &flags)
     {
@@ -438,6 +544,36 @@ __device__ __forceinline__ void load_operands(const m3c_ew_params &p, uint64_t f
     }
 }
 
+template <class Prog, int I>
+__device__ __forceinline__ void load_operand_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
+{
+    constexpr uint32_t sig = static_cast<uint32_t>((Prog::opsig >> (8 * I)) & 0xffu);
+    if constexpr (sig == 0xffu) {
+        load_block<false>(p.operands[I], f, rf.w[I]);
+    } else {
+        load_block_c<sig>(p.operands[I], f, rf.w[I]);
+    }
+}
+
+template <class Prog, int... I>
+__device__ __forceinline__ void load_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf,
+                                          std::integer_sequence<int, I...>)
+{
+    (load_operand_full<Prog, I>(p, f, rf), ...);
+}
+
+// All operands of a full block: through the program's signature when it has
+// one (narrow index only), else the run-time dispatch.
+template <class Prog, bool WIDE>
+__device__ __forceinline__ void load_block_all(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
+{
+    if constexpr (Prog::opsig != ANY_OPERANDS && !WIDE) {
+        load_full<Prog>(p, f, rf, std::make_integer_sequence<int, Prog::operands>{});
+    } else {
+        load_operands<WIDE, Prog::operands>(p, f, VEC, rf);
+    }
+}
+
 __device__ __forceinline__ void store_outputs(const m3c_ew_params &p, uint64_t f, int valid,
                                               const RegisterFile &rf)
 {
@@ -452,6 +588,36 @@ __device__ __forceinline__ void store_outputs(const m3c_ew_params &p, uint64_t f
                 store_partial(p.outputs[o], f, valid, w);
             }
         }
+    }
+}
+
+template <class Prog, int O>
+__device__ __forceinline__ void store_output_full(const m3c_ew_params &p, uint64_t f, const RegisterFile &rf)
+{
+    constexpr uint32_t sig = static_cast<uint32_t>((Prog::outsig >> (8 * (O + 1))) & 0xffu);
+    constexpr int REG = sig & 7u;
+    if (!p.outputs[O].scalar_only) {
+        store_block_c<sig>(p.outputs[O], f, rf.w[REG]);
+    } else {
+        store_partial(p.outputs[O], f, VEC, rf.w[REG]);
+    }
+}
+
+template <class Prog, int... O>
+__device__ __forceinline__ void store_full(const m3c_ew_params &p, uint64_t f, const RegisterFile &rf,
+                                           std::integer_sequence<int, O...>)
+{
+    (store_output_full<Prog, O>(p, f, rf), ...);
+}
+
+// All outputs of a full block.
+template <class Prog>
+__device__ __forceinline__ void store_block_all(const m3c_ew_params &p, uint64_t f, const RegisterFile &rf)
+{
+    if constexpr (Prog::outsig != 0u) {
+        store_full<Prog>(p, f, rf, std::make_integer_sequence<int, static_cast<int>(Prog::outsig & 0xfu)>{});
+    } else {
+        store_outputs(p, f, VEC, rf);
     }
 }
 
@@ -474,14 +640,14 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const uint64_t b = v + static_cast<uint64_t>(u) * threads;
-                if (b < blocks) load_operands<WIDE, Prog::operands>(p, b * VEC, VEC, rf[u]);
+                if (b < blocks) load_block_all<Prog, WIDE>(p, b * VEC, rf[u]);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const uint64_t b = v + static_cast<uint64_t>(u) * threads;
                 if (b < blocks) {
                     Prog::run(p, rf[u], VEC, flags);
-                    store_outputs(p, b * VEC, VEC, rf[u]);
+                    store_block_all<Prog>(p, b * VEC, rf[u]);
                 }
             }
         }
@@ -557,33 +723,90 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
 #define OPS_CLAMP E(M3C_OP_CLAMP, 0, 0, 0, 0, 0)
 #define OPS_MOV E(M3C_OP_MOV, 0, 0, 0, 0, 0)
 
-// X(operand count, ops)
-#define M3C_PROGRAMS(X)                 \
-    X(3, OPS_MUL_ADD_F32)               \
-    X(6, OPS_CFG_EULER_BF16)            \
-    X(2, OPS_GSILU_F32)                 \
-    X(2, OPS_GSILU_F16)                 \
-    X(2, OPS_GSILU_BF16)                \
-    X(2, OPS_SNAKE_ABSMAX_CLAMP)        \
-    X(2, OPS_SNAKE)                     \
-    X(1, OPS_TANH)                      \
-    X(2, OPS_ADD_F32)                   \
-    X(2, OPS_MUL_F32)                   \
-    X(2, OPS_ADD_F16)                   \
-    X(2, OPS_MUL_F16)                   \
-    X(2, OPS_ADD_BF16)                  \
-    X(2, OPS_MUL_BF16)                  \
-    X(1, OPS_CAST_F32_F16)              \
-    X(1, OPS_CAST_F32_BF16)             \
-    X(1, OPS_CAST_F16_F32)              \
-    X(1, OPS_CAST_BF16_F32)             \
-    X(1, OPS_CLAMP)                     \
-    X(1, OPS_MOV)
+constexpr uint64_t operand_sig(std::initializer_list<uint32_t> bytes)
+{
+    uint64_t sig = 0;
+    int i = 0;
+    for (uint32_t byte : bytes) sig |= static_cast<uint64_t>(byte) << (8 * i++);
+    return sig;
+}
+
+constexpr uint64_t output_sig(std::initializer_list<uint32_t> bytes)
+{
+    uint64_t sig = bytes.size();
+    int i = 1;
+    for (uint32_t byte : bytes) sig |= static_cast<uint64_t>(byte) << (8 * i++);
+    return sig;
+}
+
+#define C32 operand_byte(M3C_V_CONTIG, M3C_F32, 1)
+#define C16 operand_byte(M3C_V_CONTIG, M3C_F16, 1)
+#define CB16 operand_byte(M3C_V_CONTIG, M3C_BF16, 1)
+#define I32C operand_byte(M3C_V_IMM, M3C_F32, 1)
+#define V32_1 operand_byte(M3C_V_VECTOR, M3C_F32, 1)
+#define U32_2 operand_byte(M3C_V_UNIFORM, M3C_F32, 2)
+#define OUT(reg, dtype) output_byte(reg, dtype, 0)
+#define RAWOUT(reg, dtype) output_byte(reg, dtype, 1)
+
+// X(operand count, operand signature, output signature, ops).  Entries with
+// signatures come first: they are the addressing patterns of the benchmark
+// graphs and of plain same-shape operators; the signature-free entries
+// behind them take any addressing.
+#define M3C_PROGRAMS(X)                                                                 \
+    X(3, (operand_sig({C32, V32_1, V32_1})), (output_sig({OUT(0, M3C_F32)})), OPS_MUL_ADD_F32) \
+    X(6, (operand_sig({C32, I32C, C32, I32C, I32C, C32})),                                \
+      (output_sig({OUT(0, M3C_F32), OUT(1, M3C_BF16)})), OPS_CFG_EULER_BF16)             \
+    X(2, (operand_sig({C32, C32})), (output_sig({OUT(0, M3C_F32)})), OPS_GSILU_F32)        \
+    X(2, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_GSILU_F16)        \
+    X(2, (operand_sig({CB16, CB16})), (output_sig({OUT(0, M3C_BF16)})), OPS_GSILU_BF16)    \
+    X(2, (operand_sig({C32, U32_2})), (output_sig({OUT(0, M3C_F32)})), OPS_SNAKE_ABSMAX_CLAMP) \
+    X(2, (operand_sig({C32, U32_2})), (output_sig({OUT(0, M3C_F32)})), OPS_SNAKE)          \
+    X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_F32)})), OPS_TANH)                  \
+    X(2, (operand_sig({C32, C32})), (output_sig({OUT(0, M3C_F32)})), OPS_ADD_F32)          \
+    X(2, (operand_sig({C32, C32})), (output_sig({OUT(0, M3C_F32)})), OPS_MUL_F32)          \
+    X(2, (operand_sig({C32, V32_1})), (output_sig({OUT(0, M3C_F32)})), OPS_ADD_F32)        \
+    X(2, (operand_sig({C32, V32_1})), (output_sig({OUT(0, M3C_F32)})), OPS_MUL_F32)        \
+    X(2, (operand_sig({C32, I32C})), (output_sig({OUT(0, M3C_F32)})), OPS_ADD_F32)         \
+    X(2, (operand_sig({C32, I32C})), (output_sig({OUT(0, M3C_F32)})), OPS_MUL_F32)         \
+    X(2, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_ADD_F16)          \
+    X(2, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_MUL_F16)          \
+    X(2, (operand_sig({CB16, CB16})), (output_sig({OUT(0, M3C_BF16)})), OPS_ADD_BF16)      \
+    X(2, (operand_sig({CB16, CB16})), (output_sig({OUT(0, M3C_BF16)})), OPS_MUL_BF16)      \
+    X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_F16)})), OPS_CAST_F32_F16)          \
+    X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_BF16)})), OPS_CAST_F32_BF16)        \
+    X(1, (operand_sig({C16})), (output_sig({OUT(0, M3C_F32)})), OPS_CAST_F16_F32)          \
+    X(1, (operand_sig({CB16})), (output_sig({OUT(0, M3C_F32)})), OPS_CAST_BF16_F32)        \
+    X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_F32)})), OPS_CLAMP)                 \
+    X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_F32)})), OPS_MOV)                   \
+    X(1, (operand_sig({C16})), (output_sig({RAWOUT(0, M3C_F16)})), OPS_MOV)                \
+    X(1, (operand_sig({CB16})), (output_sig({RAWOUT(0, M3C_BF16)})), OPS_MOV)              \
+    X(3, ANY_OPERANDS, 0u, OPS_MUL_ADD_F32)                                                          \
+    X(6, ANY_OPERANDS, 0u, OPS_CFG_EULER_BF16)                                                       \
+    X(2, ANY_OPERANDS, 0u, OPS_GSILU_F32)                                                            \
+    X(2, ANY_OPERANDS, 0u, OPS_GSILU_F16)                                                            \
+    X(2, ANY_OPERANDS, 0u, OPS_GSILU_BF16)                                                           \
+    X(2, ANY_OPERANDS, 0u, OPS_SNAKE_ABSMAX_CLAMP)                                                   \
+    X(2, ANY_OPERANDS, 0u, OPS_SNAKE)                                                                \
+    X(1, ANY_OPERANDS, 0u, OPS_TANH)                                                                 \
+    X(2, ANY_OPERANDS, 0u, OPS_ADD_F32)                                                              \
+    X(2, ANY_OPERANDS, 0u, OPS_MUL_F32)                                                              \
+    X(2, ANY_OPERANDS, 0u, OPS_ADD_F16)                                                              \
+    X(2, ANY_OPERANDS, 0u, OPS_MUL_F16)                                                              \
+    X(2, ANY_OPERANDS, 0u, OPS_ADD_BF16)                                                             \
+    X(2, ANY_OPERANDS, 0u, OPS_MUL_BF16)                                                             \
+    X(1, ANY_OPERANDS, 0u, OPS_CAST_F32_F16)                                                         \
+    X(1, ANY_OPERANDS, 0u, OPS_CAST_F32_BF16)                                                        \
+    X(1, ANY_OPERANDS, 0u, OPS_CAST_F16_F32)                                                         \
+    X(1, ANY_OPERANDS, 0u, OPS_CAST_BF16_F32)                                                        \
+    X(1, ANY_OPERANDS, 0u, OPS_CLAMP)                                                                \
+    X(1, ANY_OPERANDS, 0u, OPS_MOV)
 
 typedef void (*ew_fn)(m3c_ew_params);
 
 struct Entry {
     int operands;
+    uint64_t opsig;
+    uint64_t outsig;
     int count;
     uint64_t ops[M3C_EW_MAX_OPS];
     ew_fn kernel;
@@ -596,17 +819,55 @@ constexpr int count_of(std::initializer_list<uint64_t> ops)
 
 // Fixed programs cover index spaces below 2^32 elements; larger ones use the
 // generic kernel's 64-bit addressing.
-#define M3C_ENTRY(NOPERANDS, OPS) \
-    {NOPERANDS, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPS>, false>},
+#define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS) \
+    {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>},
 
 const Entry PROGRAMS[] = {M3C_PROGRAMS(M3C_ENTRY)};
 
 #undef M3C_ENTRY
 #undef E
+#undef C32
+#undef C16
+#undef CB16
+#undef I32C
+#undef V32_1
+#undef U32_2
+#undef OUT
+#undef RAWOUT
 
 uint64_t encode_op(const m3c_ew_op &op)
 {
     return op_code(op.code, op.dst, op.a, op.b, op.rdtype, op.aux);
+}
+
+// Signature byte of a run-time operand; 0xfe (never a table value) where the
+// operand's addressing has no signature form.
+uint32_t runtime_operand_byte(const m3c_operand &op)
+{
+    const bool offsets = op.vclass != M3C_V_CONTIG && op.vclass != M3C_V_IMM;
+    if (offsets && (op.ndim < 1 || op.ndim > 8)) return 0xfeu;
+    if (op.dtype < 0 || op.dtype > 3) return 0xfeu;
+    return operand_byte(op.vclass, op.dtype, offsets ? op.ndim : 1);
+}
+
+bool signature_matches(const Entry &entry, const m3c_ew_params &p)
+{
+    if (entry.opsig != ANY_OPERANDS) {
+        for (int i = 0; i < p.n_operands; ++i) {
+            if (((entry.opsig >> (8 * i)) & 0xffu) != runtime_operand_byte(p.operands[i])) return false;
+        }
+    }
+    if (entry.outsig != 0u) {
+        if (static_cast<int>(entry.outsig & 0xfu) != p.n_outputs) return false;
+        for (int o = 0; o < p.n_outputs; ++o) {
+            const m3c_ew_out &out = p.outputs[o];
+            if (out.reg < 0 || out.reg > 7 || out.dtype < 0 || out.dtype > 3) return false;
+            if (((entry.outsig >> (8 * (o + 1))) & 0xffu) != output_byte(out.reg, out.dtype, out.raw ? 1 : 0)) {
+                return false;
+            }
+        }
+    }
+    return true;
 }
 
 const Entry *find_program(const m3c_ew_params &p)
@@ -615,7 +876,7 @@ const Entry *find_program(const m3c_ew_params &p)
         if (entry.count != p.n_ops || entry.operands != p.n_operands) continue;
         bool same = true;
         for (int k = 0; k < p.n_ops && same; ++k) same = encode_op(p.ops[k]) == entry.ops[k];
-        if (same) return &entry;
+        if (same && signature_matches(entry, p)) return &entry;
     }
     return nullptr;
 }

@@ -75,6 +75,10 @@ void m3c_operand_setup(m3c_operand *operand, const void *base,
         strides[ndim] = stride;
         ++ndim;
     }
+    /* outer axes that do not move add nothing to any offset */
+    while (ndim > 1 && strides[ndim - 1] == 0) {
+        --ndim;
+    }
     operand->ndim = ndim;
     for (d = 0; d < ndim; ++d) {
         operand->size[d] = sizes[d];

@@ -132,9 +132,12 @@ __device__ __forceinline__ void cp_async_wait_all()
 
 // Geometry of one tile: `rows` rows of `width` elements, `nvec` 16-byte
 // vectors each.  Raw rows sit `raw_pitch` bytes apart (width * bytes + 16:
-// the 16-byte pad puts row r of the ordered-sum lanes on different banks);
-// softmax keeps F32 exponentials `f32_pitch` floats apart (in place over the
-// raw rows for F32 input, else in a second area at `f32_offset`).
+// the 16-byte pad puts the rows read by the ordered-sum lanes on different
+// banks).  Softmax keeps F32 exponentials `f32_pitch` floats apart, in place
+// over the raw rows for F32 input, else in a second area at `f32_offset`.
+// The residual norm stages its second operand in a second raw area at
+// `b_offset`; the norms keep the scale (and bias) widened to F32 at
+// `param_offset`.  With fewer than 8 rows, `group` warps share a row.
 struct Tile {
     int rows;
     int width;
@@ -142,15 +145,19 @@ struct Tile {
     int raw_pitch;
     int f32_pitch;
     int f32_offset;
-    int stages;      // raw areas per tile: 2 for the residual norm
+    int b_offset;
+    int param_offset;
+    int group;
 };
 
 struct RowState {
-    float maximum[TILE_MAX_ROWS];
-    float sum[TILE_MAX_ROWS];        // softmax: sum; norms: inverse
-    float reciprocal[TILE_MAX_ROWS];
+    float sum[TILE_MAX_ROWS];         // softmax: exponential sum; norms: inverse
+    float reciprocal[TILE_MAX_ROWS];  // softmax: RN(1 / sum)
     float mean[TILE_MAX_ROWS];
-    int special[TILE_MAX_ROWS];      // softmax: row of +-inf maximum
+    int special[TILE_MAX_ROWS];       // softmax: row whose maximum is +-inf
+    float part_max[TILE_WARPS];       // per-warp candidates of a row group
+    uint32_t part_index[TILE_WARPS];
+    int part_nan[TILE_WARPS];
     int skip;
 };
 
@@ -170,19 +177,21 @@ __device__ __forceinline__ bool cta_skips(const m3c_status *status, uint32_t ski
     return st.skip != 0;
 }
 
-// Copy `live` rows of a dense [rows, nvec * 16 bytes] tensor into shared
-// memory.
+// Copy `live` rows of a dense tensor of `nvec` 16-byte vectors per row,
+// starting at row `row0`, into shared memory rows `pitch` bytes apart.
 __device__ __forceinline__ void tile_copy(unsigned char *dst, const uint4 *src, uint64_t row0,
-                                          int live, const Tile &g)
+                                          int live, int nvec, int pitch)
 {
-    for (int idx = static_cast<int>(threadIdx.x); idx < live * g.nvec; idx += TILE_THREADS) {
-        const int r = idx / g.nvec;
-        const int v = idx - r * g.nvec;
-        cp_async16(dst + r * g.raw_pitch + v * 16, src + (row0 + r) * static_cast<uint64_t>(g.nvec) + v);
+    for (int r = 0; r < live; ++r) {
+        const uint4 *row = src + (row0 + r) * static_cast<uint64_t>(nvec);
+        for (int v = static_cast<int>(threadIdx.x); v < nvec; v += TILE_THREADS) {
+            cp_async16(dst + r * pitch + v * 16, row + v);
+        }
     }
 }
 
-// Widen the EPV elements of 16-byte vector v of a raw row.
+// Widen the 16 / EB elements of 16-byte vector v of a raw row (the
+// reference's codecs, NaN payloads included).
 template <int EB>
 __device__ __forceinline__ void raw_vector(const unsigned char *row, int v, int dtype, float (&x)[16 / EB])
 {
@@ -239,23 +248,48 @@ __device__ __forceinline__ float ordered_sum_f32(const float *row, int width)
     return s;
 }
 
-// Ordered sums over a raw row: kind 0 sum of x, 1 sum of x*x, 2 sum of
-// (x - mean)^2 -- each product and difference rounded to F32 on its own.
+// Plain widening for the ordered sums: a NaN anywhere makes the sum NaN
+// whatever its payload, so the hardware conversion is enough here.
+template <int EB>
+__device__ __forceinline__ void sum_vector(const unsigned char *row, int v, int dtype, float (&x)[16 / EB])
+{
+    const uint4 q = reinterpret_cast<const uint4 *>(row)[v];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (EB == 4) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) x[t] = as_float(w[t]);
+    } else if (dtype == M3C_F16) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            x[t] = __half2float(__ushort_as_half(static_cast<unsigned short>((w[t >> 1] >> ((t & 1) * 16)) & 0xffffu)));
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) x[t] = as_float((t & 1) ? (w[t >> 1] & 0xffff0000u) : (w[t >> 1] << 16));
+    }
+}
+
+// Ordered sums over a raw row: KIND 0 sum of x, 1 sum of x*x, 2 sum of
+// (x - mean)^2, each product and difference rounded to F32 on its own (the
+// statements of src/m3_op_execute_dense.c:128-140 and :175-191).  For F16 the
+// square of a value is exact in F32 (11-bit significands, no overflow or
+// underflow), so RN(s + RN(x*x)) is one fused multiply-add.
 template <int EB, int KIND>
 __device__ __forceinline__ float ordered_raw(const unsigned char *row, int nvec, int dtype, float mean)
 {
     constexpr int EPV = 16 / EB;
     float s = 0.0f;
-#pragma unroll 4
+    const bool exact_squares = EB == 2 && dtype == M3C_F16;
+#pragma unroll 2
     for (int v = 0; v < nvec; ++v) {
         float x[EPV];
-        raw_vector<EB>(row, v, dtype, x);
+        sum_vector<EB>(row, v, dtype, x);
 #pragma unroll
         for (int t = 0; t < EPV; ++t) {
             if (KIND == 0) {
                 s = __fadd_rn(s, x[t]);
             } else if (KIND == 1) {
-                s = __fadd_rn(s, __fmul_rn(x[t], x[t]));
+                s = exact_squares ? __fmaf_rn(x[t], x[t], s) : __fadd_rn(s, __fmul_rn(x[t], x[t]));
             } else {
                 const float c = __fsub_rn(x[t], mean);
                 s = __fadd_rn(s, __fmul_rn(c, c));
@@ -265,10 +299,21 @@ __device__ __forceinline__ float ordered_raw(const unsigned char *row, int nvec,
     return s;
 }
 
-template <int EB>
-__global__ void __launch_bounds__(TILE_THREADS)
+// The IEEE quotient out of line, so that the rare operands that need it do
+// not put the whole division sequence on every element's path.
+__device__ __noinline__ float ieee_div(float a, float b) { return __fdiv_rn(a, b); }
+
+// Softmax and/or TOP_K of up to 8 rows per tile.  Per tile: one cp.async
+// copy of the rows; one pass per row (a warp, or a group of warps for wide
+// rows) for maximum, first index of the maximum and NaN; the exponentials;
+// the reference's left-to-right sums on the lanes of warp 0, one row each;
+// then the probabilities, e / sum, with Markstein's refinement of the
+// correctly rounded reciprocal.
+template <int IN, int OUT>
+__global__ void __launch_bounds__(TILE_THREADS, 6)
     softmax_tile_kernel(const __grid_constant__ m3c_softmax_params p, Tile g)
 {
+    constexpr int EB = IN == M3C_F32 ? 4 : 2;
     constexpr int EPV = 16 / EB;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ RowState st;
@@ -282,130 +327,147 @@ __global__ void __launch_bounds__(TILE_THREADS)
     const float pos_inf = __int_as_float(0x7f800000);
     const uint32_t first_command = p.softmax_command < p.topk_command ? p.softmax_command : p.topk_command;
     const uint64_t tiles = (p.rows + g.rows - 1) / g.rows;
-    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(p.probs_dtype);
+    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(OUT);
+    const int r = warp / g.group;      // this warp's row in the tile
+    const int sub = warp % g.group;    // and its place in the row's group
+    const int stride = g.group * WARP;
     for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint64_t row0 = tile * g.rows;
         const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(g.rows) ? p.rows - row0 : g.rows);
-        tile_copy(smem, in, row0, live, g);
+        tile_copy(smem, in, row0, live, g.nvec, g.raw_pitch);
         cp_async_wait_all();
         __syncthreads();
-        // one warp per row: the order-free statistics and the exponentials
-        for (int r = warp; r < live; r += TILE_WARPS) {
-            const unsigned char *raw = smem + r * g.raw_pitch;
-            float *erow = ebuf + r * g.f32_pitch;
-            float maximum = -pos_inf;
-            bool nan = false;
-            for (int v = lane; v < g.nvec; v += WARP) {
+
+        // maximum, its first index and NaN, for the warp's share of its row
+        const bool active = r < live;
+        const unsigned char *raw = smem + r * g.raw_pitch;
+        float best = -pos_inf;
+        uint32_t best_i = 0xffffffffu;
+        bool nan = false;
+        if (active) {
+            for (int v = sub * WARP + lane; v < g.nvec; v += stride) {
                 float x[EPV];
-                raw_vector<EB>(raw, v, p.in_dtype, x);
+                raw_vector<EB>(raw, v, IN, x);
 #pragma unroll
                 for (int t = 0; t < EPV; ++t) {
-                    maximum = x[t] > maximum ? x[t] : maximum;
+                    const bool greater = x[t] > best;
+                    best = greater ? x[t] : best;
+                    best_i = greater ? static_cast<uint32_t>(v * EPV + t) : best_i;
                     nan |= x[t] != x[t];
                 }
             }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float other = __shfl_xor_sync(0xffffffffu, maximum, off);
-                maximum = other > maximum ? other : maximum;
+        }
+        warp_best(best, best_i);
+        nan = __any_sync(0xffffffffu, nan);
+        if (g.group > 1) {
+            if (lane == 0) {
+                st.part_max[warp] = best;
+                st.part_index[warp] = best_i;
+                st.part_nan[warp] = nan ? 1 : 0;
             }
-            if (__any_sync(0xffffffffu, nan) && lane == 0) {
-                record_failure(p.status, first_command);
-            }
-            if (p.top_values != nullptr) {
-                // the first index holding the maximum (+0 == -0), and its value
-                float best_v = -pos_inf;
-                uint32_t best_i = 0xffffffffu;
-                for (int v = lane; v < g.nvec; v += WARP) {
-                    float x[EPV];
-                    raw_vector<EB>(raw, v, p.in_dtype, x);
-#pragma unroll
-                    for (int t = 0; t < EPV; ++t) {
-                        const uint32_t j = static_cast<uint32_t>(v * EPV + t);
-                        if (x[t] == maximum && j < best_i) {
-                            best_i = j;
-                            best_v = x[t];
-                        }
-                    }
+            __syncthreads();
+            for (int s = 0; s < g.group; ++s) {
+                const int w = r * g.group + s;
+                if (precedes(st.part_max[w], st.part_index[w], best, best_i)) {
+                    best = st.part_max[w];
+                    best_i = st.part_index[w];
                 }
+                nan |= st.part_nan[w] != 0;
+            }
+        }
+        // a row of -inf only: the first index (NaN rows fail the command)
+        if (best_i == 0xffffffffu) best_i = 0u;
+        if (active && nan && sub == 0 && lane == 0) {
+            record_failure(p.status, first_command);
+        }
+        if (active && p.top_values != nullptr && sub == 0) {
+            const uint64_t row = row0 + r;
+            if (p.k == 1) {
+                if (lane == 0) {
+                    p.top_values[row] = best;
+                    p.top_indices[row] = static_cast<int32_t>(best_i);
+                }
+            } else {
                 top_k_row(
                     [&](uint64_t j) {
                         return EB == 4 ? reinterpret_cast<const float *>(raw)[j]
-                                       : widen(p.in_dtype, reinterpret_cast<const uint16_t *>(raw)[j]);
+                                       : widen(IN, reinterpret_cast<const uint16_t *>(raw)[j]);
                     },
-                    static_cast<uint64_t>(g.width), p.k, best_v, best_i, p.top_values + (row0 + r) * p.k,
-                    p.top_indices + (row0 + r) * p.k, lane);
-            }
-            if (p.probs == nullptr) {
-                continue;
-            }
-            if (maximum == -pos_inf || maximum == pos_inf) {
-                // src/m3_op_execute_basic.c:165-170: final probabilities now
-                uint32_t infinities = 0u;
-                for (int v = lane; v < g.nvec; v += WARP) {
-                    float x[EPV];
-                    raw_vector<EB>(raw, v, p.in_dtype, x);
-#pragma unroll
-                    for (int t = 0; t < EPV; ++t) infinities += x[t] == pos_inf ? 1u : 0u;
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) infinities += __shfl_xor_sync(0xffffffffu, infinities, off);
-                const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
-                __syncwarp();
-                for (int v = lane; v < g.nvec; v += WARP) {
-                    float x[EPV];
-                    raw_vector<EB>(raw, v, p.in_dtype, x);
-#pragma unroll
-                    for (int t = 0; t < EPV; ++t) {
-                        erow[v * EPV + t] = (maximum == pos_inf && x[t] == pos_inf) ? share : 0.0f;
-                    }
-                }
-                if (lane == 0) st.special[r] = 1;
-            } else {
-                // F32 input: the exponentials overwrite the row, each lane
-                // only the vector it has just read
-                __syncwarp();
-                for (int v = lane; v < g.nvec; v += WARP) {
-                    float x[EPV];
-                    raw_vector<EB>(raw, v, p.in_dtype, x);
-#pragma unroll
-                    for (int t = 0; t < EPV; ++t) erow[v * EPV + t] = expf(__fsub_rn(x[t], maximum));
-                }
-                if (lane == 0) st.special[r] = 0;
+                    static_cast<uint64_t>(g.width), p.k, best, best_i, p.top_values + row * p.k,
+                    p.top_indices + row * p.k, lane);
             }
         }
-        __syncthreads();
         if (p.probs != nullptr) {
-            // the reference's left-to-right sums, one row per lane of warp 0
-            if (threadIdx.x < static_cast<unsigned>(live)) {
-                const int r = static_cast<int>(threadIdx.x);
-                if (!st.special[r]) {
-                    const float sum = ordered_sum_f32(ebuf + r * g.f32_pitch, g.width);
-                    st.sum[r] = sum;
-                    st.reciprocal[r] = __frcp_rn(sum);
+            if (p.k > 1 && p.top_values != nullptr) {
+                __syncthreads();  // the top-k passes read rows the exponentials overwrite
+            }
+            float *erow = ebuf + r * g.f32_pitch;
+            if (active && (best == -pos_inf || best == pos_inf)) {
+                // src/m3_op_execute_basic.c:165-170: final probabilities now,
+                // by the first warp of the row's group
+                if (sub == 0) {
+                    uint32_t infinities = 0u;
+                    for (int v = lane; v < g.nvec; v += WARP) {
+                        float x[EPV];
+                        raw_vector<EB>(raw, v, IN, x);
+#pragma unroll
+                        for (int t = 0; t < EPV; ++t) infinities += x[t] == pos_inf ? 1u : 0u;
+                    }
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) {
+                        infinities += __shfl_xor_sync(0xffffffffu, infinities, off);
+                    }
+                    const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
+                    __syncwarp();
+                    for (int v = lane; v < g.nvec; v += WARP) {
+                        float x[EPV];
+                        raw_vector<EB>(raw, v, IN, x);
+#pragma unroll
+                        for (int t = 0; t < EPV; ++t) {
+                            erow[v * EPV + t] = (best == pos_inf && x[t] == pos_inf) ? share : 0.0f;
+                        }
+                    }
+                    if (lane == 0) st.special[r] = 1;
                 }
+            } else if (active) {
+                // each lane overwrites only the vector it has just read
+                for (int v = sub * WARP + lane; v < g.nvec; v += stride) {
+                    float x[EPV];
+                    raw_vector<EB>(raw, v, IN, x);
+#pragma unroll
+                    for (int t = 0; t < EPV; ++t) erow[v * EPV + t] = expf(__fsub_rn(x[t], best));
+                }
+                if (sub == 0 && lane == 0) st.special[r] = 0;
+            }
+            __syncthreads();
+            // the reference's left-to-right sums, one row per lane of warp 0
+            if (threadIdx.x < static_cast<unsigned>(live) && !st.special[threadIdx.x]) {
+                const float sum = ordered_sum_f32(ebuf + threadIdx.x * g.f32_pitch, g.width);
+                st.sum[threadIdx.x] = sum;
+                st.reciprocal[threadIdx.x] = __frcp_rn(sum);
             }
             __syncthreads();
             // probabilities expf(x - max) / sum (src/m3_op_execute_basic.c:171-178)
-            unsigned char *out = static_cast<unsigned char *>(p.probs);
+            unsigned char *out = static_cast<unsigned char *>(p.probs) + row0 * out_pitch;
             const int per_row = g.width / 4;
-            for (int idx = static_cast<int>(threadIdx.x); idx < live * per_row; idx += TILE_THREADS) {
-                const int r = idx / per_row;
-                const int j4 = idx - r * per_row;
-                const float4 e = reinterpret_cast<const float4 *>(ebuf + r * g.f32_pitch)[j4];
-                float pr[4] = {e.x, e.y, e.z, e.w};
-                if (!st.special[r]) {
-                    const float sum = st.sum[r];
-                    const float y = st.reciprocal[r];
+            for (int rr = 0; rr < live; ++rr) {
+                const float4 *e4 = reinterpret_cast<const float4 *>(ebuf + rr * g.f32_pitch);
+                const bool special = st.special[rr] != 0;
+                const float sum = st.sum[rr];
+                const float y = st.reciprocal[rr];
+                for (int j4 = static_cast<int>(threadIdx.x); j4 < per_row; j4 += TILE_THREADS) {
+                    const float4 e = e4[j4];
+                    float pr[4] = {e.x, e.y, e.z, e.w};
+                    if (!special) {
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        // e in [2^-100, 1] and sum >= 1: Markstein's quotient is
-                        // the IEEE one; tiny e stays on the IEEE division
-                        pr[t] = (pr[t] >= 0x1p-100f || pr[t] == 0.0f) ? div_markstein(pr[t], sum, y)
-                                                                      : __fdiv_rn(pr[t], sum);
+                        for (int t = 0; t < 4; ++t) {
+                            // e in [2^-100, 1] and sum >= 1: Markstein's quotient
+                            // is the IEEE one; smaller e stays on the IEEE division
+                            pr[t] = pr[t] >= 0x1p-100f ? div_markstein(pr[t], sum, y) : ieee_div(pr[t], sum);
+                        }
                     }
+                    store_vec<4>(out + rr * out_pitch, OUT, static_cast<uint64_t>(j4) * 4u, pr);
                 }
-                store_vec<4>(out + (row0 + r) * out_pitch, p.probs_dtype, static_cast<uint64_t>(j4) * 4u, pr);
             }
         }
         __syncthreads();
@@ -414,10 +476,11 @@ __global__ void __launch_bounds__(TILE_THREADS)
 
 // RMSNorm / LayerNorm with an optional residual-add prologue (RESID: the
 // input is round_in(x + b), optionally stored to sum_out).
-template <int EB, bool RESID>
+template <int IN, int OUT, bool RESID>
 __global__ void __launch_bounds__(TILE_THREADS)
     norm_tile_kernel(const __grid_constant__ m3c_norm_params p, Tile g)
 {
+    constexpr int EB = IN == M3C_F32 ? 4 : 2;
     constexpr int EPV = 16 / EB;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ RowState st;
@@ -427,39 +490,49 @@ __global__ void __launch_bounds__(TILE_THREADS)
     const uint4 *xa = static_cast<const uint4 *>(p.x);
     const uint4 *xb = static_cast<const uint4 *>(p.resid_b);
     uint4 *sum_out = static_cast<uint4 *>(p.sum_out);
-    unsigned char *bstage = smem + g.rows * g.raw_pitch;
+    unsigned char *bstage = smem + g.b_offset;
+    float *scale = reinterpret_cast<float *>(smem + g.param_offset);
+    float *bias = scale + g.width;
+    for (int j = static_cast<int>(threadIdx.x); j < g.width; j += TILE_THREADS) {
+        scale[j] = load_elem(p.scale, p.scale_dtype, j);
+        if (p.bias != nullptr) bias[j] = load_elem(p.bias, p.bias_dtype, j);
+    }
     const uint64_t tiles = (p.rows + g.rows - 1) / g.rows;
     const float channels = __int2float_rn(g.width);
-    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(p.out_dtype);
+    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(OUT);
     for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint64_t row0 = tile * g.rows;
         const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(g.rows) ? p.rows - row0 : g.rows);
-        tile_copy(smem, xa, row0, live, g);
-        if constexpr (RESID) tile_copy(bstage, xb, row0, live, g);
+        tile_copy(smem, xa, row0, live, g.nvec, g.raw_pitch);
+        if constexpr (RESID) tile_copy(bstage, xb, row0, live, g.nvec, g.raw_pitch);
         cp_async_wait_all();
         __syncthreads();
         if constexpr (RESID) {
             // src/m3_op_execute_basic.c:61-77: one F32 add, stored in the
             // sum's dtype; the stored bits replace x in shared memory
-            for (int idx = static_cast<int>(threadIdx.x); idx < live * g.nvec; idx += TILE_THREADS) {
-                const int r = idx / g.nvec;
-                const int v = idx - r * g.nvec;
-                float a[EPV];
-                float b[EPV];
-                uint32_t raw[EPV];
-                raw_vector<EB>(smem + r * g.raw_pitch, v, p.in_dtype, a);
-                raw_vector<EB>(bstage + r * g.raw_pitch, v, p.in_dtype, b);
+            for (int r = 0; r < live; ++r) {
+                uint4 *arow = reinterpret_cast<uint4 *>(smem + r * g.raw_pitch);
+                const unsigned char *brow = bstage + r * g.raw_pitch;
+                for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
+                    float a[EPV];
+                    float b[EPV];
+                    uint32_t raw[EPV];
+                    raw_vector<EB>(reinterpret_cast<const unsigned char *>(arow), v, IN, a);
+                    raw_vector<EB>(brow, v, IN, b);
 #pragma unroll
-                for (int t = 0; t < EPV; ++t) raw[t] = narrow(p.in_dtype, __fadd_rn(a[t], b[t]));
-                uint4 packed;
-                if (EB == 4) {
-                    packed = make_uint4(raw[0], raw[1], raw[2], raw[3]);
-                } else {
-                    packed = make_uint4(raw[0] | (raw[1] << 16), raw[2] | (raw[3] << 16),
-                                        raw[4] | (raw[5] << 16), raw[6] | (raw[7] << 16));
+                    for (int t = 0; t < EPV; ++t) raw[t] = narrow(IN, __fadd_rn(a[t], b[t]));
+                    uint4 packed;
+                    if (EB == 4) {
+                        packed = make_uint4(raw[0], raw[1], raw[2], raw[3]);
+                    } else {
+                        packed = make_uint4(raw[0] | (raw[1] << 16), raw[2] | (raw[3] << 16),
+                                            raw[4] | (raw[5] << 16), raw[6] | (raw[7] << 16));
+                    }
+                    arow[v] = packed;
+                    if (sum_out != nullptr) {
+                        __stcs(sum_out + (row0 + r) * static_cast<uint64_t>(g.nvec) + v, packed);
+                    }
                 }
-                reinterpret_cast<uint4 *>(smem + r * g.raw_pitch)[v] = packed;
-                if (sum_out != nullptr) __stcs(sum_out + (row0 + r) * static_cast<uint64_t>(g.nvec) + v, packed);
             }
             __syncthreads();
         }
@@ -469,43 +542,55 @@ __global__ void __launch_bounds__(TILE_THREADS)
             const unsigned char *row = smem + r * g.raw_pitch;
             if (p.layer_norm) {
                 // src/m3_op_execute_dense.c:175-194
-                const float mean = __fdiv_rn(ordered_raw<EB, 0>(row, g.nvec, p.in_dtype, 0.0f), channels);
-                const float centred = ordered_raw<EB, 2>(row, g.nvec, p.in_dtype, mean);
+                const float mean = __fdiv_rn(ordered_raw<EB, 0>(row, g.nvec, IN, 0.0f), channels);
+                const float centred = ordered_raw<EB, 2>(row, g.nvec, IN, mean);
                 st.mean[r] = mean;
                 st.sum[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(centred, channels), p.epsilon)));
             } else {
                 // src/m3_op_execute_dense.c:128-141
-                const float squares = ordered_raw<EB, 1>(row, g.nvec, p.in_dtype, 0.0f);
+                const float squares = ordered_raw<EB, 1>(row, g.nvec, IN, 0.0f);
                 st.mean[r] = 0.0f;
                 st.sum[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(squares, channels), p.epsilon)));
             }
         }
         __syncthreads();
         // normalised outputs
-        unsigned char *out = static_cast<unsigned char *>(p.out);
-        for (int idx = static_cast<int>(threadIdx.x); idx < live * g.nvec; idx += TILE_THREADS) {
-            const int r = idx / g.nvec;
-            const int v = idx - r * g.nvec;
+        unsigned char *out = static_cast<unsigned char *>(p.out) + row0 * out_pitch;
+        for (int r = 0; r < live; ++r) {
             const float inverse = st.sum[r];
             const float mean = st.mean[r];
-            float x[EPV];
-            float y[EPV];
-            raw_vector<EB>(smem + r * g.raw_pitch, v, p.in_dtype, x);
+            const unsigned char *row = smem + r * g.raw_pitch;
+            for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
+                float x[EPV];
+                float y[EPV];
+                raw_vector<EB>(row, v, IN, x);
+                const float4 *w4 = reinterpret_cast<const float4 *>(scale + v * EPV);
+                const float4 *b4 = reinterpret_cast<const float4 *>(bias + v * EPV);
 #pragma unroll
-            for (int t = 0; t < EPV; ++t) {
-                const int j = v * EPV + t;
-                const float w = load_elem(p.scale, p.scale_dtype, j);
-                if (p.layer_norm) {
-                    // ((x - mean) * inv) * scale (+ bias), src/m3_op_execute_dense.c:195-213
-                    float o = __fmul_rn(__fmul_rn(__fsub_rn(x[t], mean), inverse), w);
-                    if (p.bias != nullptr) o = __fadd_rn(o, load_elem(p.bias, p.bias_dtype, j));
-                    y[t] = o;
-                } else {
-                    // round to the input dtype before scaling, src/m3_op_execute_dense.c:149-151
-                    y[t] = __fmul_rn(round_to(p.in_dtype, __fmul_rn(x[t], inverse)), w);
+                for (int q = 0; q < EPV / 4; ++q) {
+                    const float4 w = w4[q];
+                    const float ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int k = 4 * q + t;
+                        if (p.layer_norm) {
+                            // ((x - mean) * inv) * scale (+ bias), src/m3_op_execute_dense.c:195-213
+                            float o = __fmul_rn(__fmul_rn(__fsub_rn(x[k], mean), inverse), ws[t]);
+                            if (p.bias != nullptr) {
+                                const float4 bb = b4[q];
+                                const float bs[4] = {bb.x, bb.y, bb.z, bb.w};
+                                o = __fadd_rn(o, bs[t]);
+                            }
+                            y[k] = o;
+                        } else {
+                            // round to the input dtype before scaling,
+                            // src/m3_op_execute_dense.c:149-151
+                            y[k] = __fmul_rn(round_to(IN, __fmul_rn(x[k], inverse)), ws[t]);
+                        }
+                    }
                 }
+                store_vec<EPV>(out + r * out_pitch, OUT, static_cast<uint64_t>(v) * EPV, y);
             }
-            store_vec<EPV>(out + (row0 + r) * out_pitch, p.out_dtype, static_cast<uint64_t>(v) * EPV, y);
         }
         __syncthreads();
     }
@@ -743,11 +828,13 @@ bool aligned16(const void *p)
 }
 
 // Tile geometry, or rows = 0 when the tile path does not apply: rows must be
-// whole 16-byte vectors, and one tile (up to 8 rows, at least 1) must fit a
-// 48 KiB shared-memory budget so several CTAs share an SM.
-Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual)
+// whole 16-byte vectors, and one tile must fit a 48 KiB shared-memory budget
+// (so several CTAs share an SM) or, for very wide rows, one row must fit in
+// 200 KiB.  Softmax tiles hold 8, 4, 2 or 1 rows so that the 8 warps split
+// evenly over them.
+Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual, bool bias)
 {
-    Tile g{0, 0, 0, 0, 0, 0, 1};
+    Tile g{0, 0, 0, 0, 0, 0, 0, 0, 1};
     const uint64_t per_vec = 16u / static_cast<uint64_t>(eb);
     if (width == 0 || width % per_vec != 0 || width % 4 != 0 || width > 32768) {
         return g;
@@ -756,24 +843,40 @@ Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual)
     g.nvec = static_cast<int>(width / per_vec);
     g.raw_pitch = static_cast<int>(width) * eb + 16;
     g.f32_pitch = static_cast<int>(width) + 4;
-    g.stages = residual ? 2 : 1;
-    size_t row_bytes = static_cast<size_t>(g.raw_pitch) * g.stages;
-    if (softmax && eb != 4) {
-        row_bytes += static_cast<size_t>(g.f32_pitch) * 4u;  // separate exponentials
+    const size_t budget = 48u * 1024u;
+    if (softmax) {
+        const size_t row_bytes = static_cast<size_t>(g.raw_pitch) + (eb != 4 ? static_cast<size_t>(g.f32_pitch) * 4u : 0u);
+        int rows = TILE_MAX_ROWS;
+        while (rows > 1 && static_cast<size_t>(rows) * row_bytes > budget) rows >>= 1;
+        if (row_bytes > 200u * 1024u) return g;
+        g.rows = rows;
+        g.group = TILE_WARPS / rows;
+        g.f32_offset = eb != 4 ? rows * g.raw_pitch : 0;
+        return g;
     }
-    int rows = static_cast<int>((48u * 1024u) / row_bytes);
-    if (rows > TILE_MAX_ROWS) rows = TILE_MAX_ROWS;
-    if (rows < 1) rows = (row_bytes <= 200u * 1024u) ? 1 : 0;
+    const size_t areas = residual ? 2u : 1u;
+    const size_t row_bytes = static_cast<size_t>(g.raw_pitch) * areas;
+    const size_t params = static_cast<size_t>(width) * 4u * (bias ? 2u : 1u);
+    int rows = 0;
+    if (params + row_bytes <= budget) {
+        rows = static_cast<int>((budget - params) / row_bytes);
+        if (rows > TILE_MAX_ROWS) rows = TILE_MAX_ROWS;
+    } else if (params + row_bytes <= 200u * 1024u) {
+        rows = 1;
+    }
     g.rows = rows;
-    g.f32_offset = (softmax && eb != 4) ? rows * g.raw_pitch : 0;
+    g.b_offset = rows * g.raw_pitch;
+    g.param_offset = rows * g.raw_pitch * static_cast<int>(areas);
     return g;
 }
 
-size_t tile_smem(const Tile &g, bool softmax, int eb)
+size_t tile_smem(const Tile &g, bool softmax, int eb, bool bias)
 {
-    size_t bytes = static_cast<size_t>(g.rows) * g.raw_pitch * g.stages;
-    if (softmax && eb != 4) bytes += static_cast<size_t>(g.rows) * g.f32_pitch * 4u;
-    return bytes;
+    if (softmax) {
+        return static_cast<size_t>(g.rows) *
+               (static_cast<size_t>(g.raw_pitch) + (eb != 4 ? static_cast<size_t>(g.f32_pitch) * 4u : 0u));
+    }
+    return static_cast<size_t>(g.param_offset) + static_cast<size_t>(g.width) * 4u * (bias ? 2u : 1u);
 }
 
 template <typename Kernel, typename Params>
@@ -796,6 +899,59 @@ int launch_tile(Kernel kernel, const Params &params, const Tile &g, size_t smem,
     return static_cast<int>(cudaGetLastError());
 }
 
+// Tile kernels are compiled per (input, output) dtype pair so that every
+// codec folds to straight-line code.
+template <int IN, int OUT>
+int softmax_tile(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
+{
+    return launch_tile(softmax_tile_kernel<IN, OUT>, p, g, smem, p.rows, stream);
+}
+
+template <int IN>
+int softmax_tile_out(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
+{
+    switch (p.probs == nullptr ? IN : p.probs_dtype) {
+    case M3C_F16: return softmax_tile<IN, M3C_F16>(p, g, smem, stream);
+    case M3C_BF16: return softmax_tile<IN, M3C_BF16>(p, g, smem, stream);
+    default: return softmax_tile<IN, M3C_F32>(p, g, smem, stream);
+    }
+}
+
+int softmax_tile_dispatch(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
+{
+    switch (p.in_dtype) {
+    case M3C_F16: return softmax_tile_out<M3C_F16>(p, g, smem, stream);
+    case M3C_BF16: return softmax_tile_out<M3C_BF16>(p, g, smem, stream);
+    default: return softmax_tile_out<M3C_F32>(p, g, smem, stream);
+    }
+}
+
+template <int IN, int OUT>
+int norm_tile(const m3c_norm_params &p, const Tile &g, size_t smem, void *stream)
+{
+    return p.resid_b != nullptr ? launch_tile(norm_tile_kernel<IN, OUT, true>, p, g, smem, p.rows, stream)
+                                : launch_tile(norm_tile_kernel<IN, OUT, false>, p, g, smem, p.rows, stream);
+}
+
+template <int IN>
+int norm_tile_out(const m3c_norm_params &p, const Tile &g, size_t smem, void *stream)
+{
+    switch (p.out_dtype) {
+    case M3C_F16: return norm_tile<IN, M3C_F16>(p, g, smem, stream);
+    case M3C_BF16: return norm_tile<IN, M3C_BF16>(p, g, smem, stream);
+    default: return norm_tile<IN, M3C_F32>(p, g, smem, stream);
+    }
+}
+
+int norm_tile_dispatch(const m3c_norm_params &p, const Tile &g, size_t smem, void *stream)
+{
+    switch (p.in_dtype) {
+    case M3C_F16: return norm_tile_out<M3C_F16>(p, g, smem, stream);
+    case M3C_BF16: return norm_tile_out<M3C_BF16>(p, g, smem, stream);
+    default: return norm_tile_out<M3C_F32>(p, g, smem, stream);
+    }
+}
+
 // Rows per CTA and dynamic shared memory of the generic kernels.
 void row_shape(uint64_t width, int *rows_per_cta, size_t *smem_bytes, bool *fits)
 {
@@ -814,12 +970,11 @@ void row_shape(uint64_t width, int *rows_per_cta, size_t *smem_bytes, bool *fits
 extern "C" int m3c_launch_softmax(const m3c_softmax_params *params, void *stream)
 {
     const int eb = m3c::bytes_of(params->in_dtype);
-    const m3c::Tile g = m3c::tile_geometry(params->width, eb, true, false);
+    const m3c::Tile g = m3c::tile_geometry(params->width, eb, true, false, false);
     if (g.rows > 0 && params->rows > 0 && m3c::aligned16(params->input) &&
         (params->probs == nullptr || m3c::aligned16(params->probs))) {
-        const size_t smem = m3c::tile_smem(g, true, eb);
-        return eb == 4 ? m3c::launch_tile(m3c::softmax_tile_kernel<4>, *params, g, smem, params->rows, stream)
-                       : m3c::launch_tile(m3c::softmax_tile_kernel<2>, *params, g, smem, params->rows, stream);
+        const size_t smem = m3c::tile_smem(g, true, eb, false);
+        return m3c::softmax_tile_dispatch(*params, g, smem, stream);
     }
     int rows_per_cta = 4;
     size_t smem = 0;
@@ -842,17 +997,13 @@ extern "C" int m3c_launch_norm(const m3c_norm_params *params, void *stream)
 {
     const int eb = m3c::bytes_of(params->in_dtype);
     const bool resid = params->resid_b != nullptr;
-    const m3c::Tile g = m3c::tile_geometry(params->width, eb, false, resid);
+    const bool bias = params->bias != nullptr;
+    const m3c::Tile g = m3c::tile_geometry(params->width, eb, false, resid, bias);
     if (g.rows > 0 && params->rows > 0 && m3c::aligned16(params->x) && m3c::aligned16(params->out) &&
         (!resid || m3c::aligned16(params->resid_b)) &&
         (params->sum_out == nullptr || m3c::aligned16(params->sum_out))) {
-        const size_t smem = m3c::tile_smem(g, false, eb);
-        if (eb == 4) {
-            return resid ? m3c::launch_tile(m3c::norm_tile_kernel<4, true>, *params, g, smem, params->rows, stream)
-                         : m3c::launch_tile(m3c::norm_tile_kernel<4, false>, *params, g, smem, params->rows, stream);
-        }
-        return resid ? m3c::launch_tile(m3c::norm_tile_kernel<2, true>, *params, g, smem, params->rows, stream)
-                     : m3c::launch_tile(m3c::norm_tile_kernel<2, false>, *params, g, smem, params->rows, stream);
+        const size_t smem = m3c::tile_smem(g, false, eb, bias);
+        return m3c::norm_tile_dispatch(*params, g, smem, stream);
     }
     int rows_per_cta = 4;
     size_t smem = 0;
