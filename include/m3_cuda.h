@@ -446,8 +446,12 @@ typedef struct {
                               a non-blocking stream */
     bool fuse;             /* fuse element-wise chains and row prologues
                               (default true) */
-    bool cuda_graphs;      /* replay each run's launches as a CUDA graph
-                              (default true) */
+    bool cuda_graphs;      /* enqueue each run (or each run sequence of
+                              m3_cuda_session_run_steps_async) as one CUDA
+                              graph launch, captured on first use for each
+                              buffer assignment and kept (default true);
+                              falls back to single launches on a stream that
+                              cannot be captured */
 } m3_cuda_session_options;
 
 void m3_cuda_session_options_init(m3_cuda_session_options *options);
@@ -468,6 +472,20 @@ m3_status m3_cuda_session_create(m3_session **session, const m3_graph *graph,
  * m3_cuda_session_synchronize waits and returns the first failure since the
  * previous synchronise, with the reference's message. */
 m3_status m3_cuda_session_run_async(m3_session *session, m3_error *error);
+
+/* Enqueue `count` runs, exchanging the buffers of `input` and `output` (as
+ * m3_cuda_session_swap_values) between consecutive runs, so each run reads
+ * the previous run's output: the state of an iterative solver, e.g. the
+ * flow-matching Euler loop x <- x + dt * v that the reference's flow solver
+ * runs as repeated m3_session_run calls (src/m3_flow_solver_math.c:36-135).
+ * No exchange follows the last run.  Pass M3_GRAPH_VALUE_NONE for both to
+ * repeat runs without carrying state.  With cuda_graphs the whole sequence
+ * is one graph launch.  Failure semantics are those of `count` calls of
+ * m3_cuda_session_run_async. */
+m3_status m3_cuda_session_run_steps_async(m3_session *session, size_t count,
+                                          m3_graph_value_id input,
+                                          m3_graph_value_id output,
+                                          m3_error *error);
 m3_status m3_cuda_session_synchronize(m3_session *session, m3_error *error);
 
 /* Device address and byte size of a value's current storage (valid until the

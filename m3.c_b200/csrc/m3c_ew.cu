@@ -896,7 +896,7 @@ int sm_count()
 }  // namespace
 }  // namespace m3c
 
-extern "C" int m3c_launch_ew(const m3c_ew_params *params, void *stream)
+extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
 {
     const bool wide = params->count >= (1ull << 32);
     const m3c::Entry *entry = wide ? nullptr : m3c::find_program(*params);
@@ -904,15 +904,44 @@ extern "C" int m3c_launch_ew(const m3c_ew_params *params, void *stream)
                             ? entry->kernel
                             : (wide ? m3c::ew_kernel<m3c::Dynamic, true> : m3c::ew_kernel<m3c::Dynamic, false>);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, m3c::THREADS, 0) != cudaSuccess ||
-        per_sm < 1) {
+    const cudaError_t code =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, m3c::THREADS, 0);
+    if (code != cudaSuccess || per_sm < 1) {
+        (void)cudaGetLastError();
         per_sm = 1;
     }
     const uint64_t blocks_needed = (params->count / m3c::VEC + m3c::THREADS - 1) / m3c::THREADS;
-    // a persistent grid: every resident CTA of every SM, no more
-    const uint64_t cap = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(per_sm);
-    uint64_t grid = blocks_needed < cap ? blocks_needed : cap;
+    uint64_t grid;
+    if (params->reduce != nullptr) {
+        // a reduction ends with one atomic per CTA: a persistent grid, every
+        // resident CTA of every SM and no more
+        const uint64_t cap = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(per_sm);
+        grid = blocks_needed < cap ? blocks_needed : cap;
+    } else {
+        // otherwise one pass per thread (two blocks of VEC elements each):
+        // every load of the launch is issued as soon as its CTA is resident
+        // and the block scheduler keeps the SMs full to the end
+        grid = (blocks_needed + 1) / 2;
+        if (grid > 0x7fffffffull) grid = 0x7fffffffull;
+    }
     if (grid == 0) grid = 1;  // empty tensors still run the reduction epilogue
-    kernel<<<static_cast<unsigned>(grid), m3c::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(*params);
+    choice->kernel = reinterpret_cast<void *>(kernel);
+    choice->grid = grid;
+    return 0;
+}
+
+extern "C" int m3c_launch_ew_chosen(const m3c_ew_choice *choice, const m3c_ew_params *params,
+                                    void *stream)
+{
+    const m3c::ew_fn kernel = reinterpret_cast<m3c::ew_fn>(choice->kernel);
+    kernel<<<static_cast<unsigned>(choice->grid), m3c::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+        *params);
     return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int m3c_launch_ew(const m3c_ew_params *params, void *stream)
+{
+    m3c_ew_choice choice;
+    m3c_ew_choose(params, &choice);
+    return m3c_launch_ew_chosen(&choice, params, stream);
 }

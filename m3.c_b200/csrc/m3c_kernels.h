@@ -182,6 +182,17 @@ typedef struct {
     m3c_status *status;
 } m3c_norm_params;
 
+/* The kernel and grid m3c_launch_ew would use, chosen once (sessions keep it
+ * per launch so repeated runs skip the program search), and the launch with
+ * that choice. */
+typedef struct {
+    void *kernel;
+    uint64_t grid;
+} m3c_ew_choice;
+int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice);
+int m3c_launch_ew_chosen(const m3c_ew_choice *choice, const m3c_ew_params *params,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

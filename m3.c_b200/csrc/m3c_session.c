@@ -35,6 +35,20 @@ typedef struct {
     size_t slot_b;
 } session_event;
 
+/* A captured sequence of `runs` runs with slots swap_a/swap_b exchanged
+ * between consecutive runs (SIZE_MAX: none), valid for the buffer assignment
+ * it was captured from (kernel parameters hold buffer addresses). */
+#define M3C_RUN_GRAPHS 8
+
+typedef struct {
+    size_t runs;
+    size_t swap_a;
+    size_t swap_b;
+    unsigned char **start_buffer[2];
+    uint8_t *start_current;
+    cudaGraphExec_t exec;
+} run_graph;
+
 struct m3_session {
     m3c_plan plan;
     m3_graph_value_desc *descriptions;
@@ -59,10 +73,15 @@ struct m3_session {
     m3c_status *status_host;         /* pinned */
     m3c_reduce_scratch *reduce;      /* one per launch */
     m3c_ew_params *ew_templates;     /* one per launch (EW launches only) */
+    m3c_ew_choice *ew_choices;       /* kernel and grid of each EW launch */
     /* a failure found by an implicit synchronise, reported by the next
      * explicit one */
     m3_status sticky_status;
     m3_error sticky_error;
+    /* captured run sequences, replayed as one graph launch each */
+    run_graph graphs[M3C_RUN_GRAPHS];
+    size_t graph_count;
+    size_t graph_next;
 };
 
 static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, 0U};
@@ -120,6 +139,17 @@ static unsigned char *ref_pointer(const m3_session *s, m3c_ref ref)
 
 /* ---------------------------------------------------------- lifecycle */
 
+static void drop_graph(run_graph *g)
+{
+    if (g->exec != NULL) {
+        (void)cudaGraphExecDestroy(g->exec);
+    }
+    free(g->start_buffer[0]);
+    free(g->start_buffer[1]);
+    free(g->start_current);
+    memset(g, 0, sizeof(*g));
+}
+
 void m3_session_free(m3_session *session)
 {
     if (session == NULL) {
@@ -135,6 +165,9 @@ void m3_session_free(m3_session *session)
         if (session->stream != NULL) {
             (void)cudaStreamSynchronize(session->stream);
         }
+    }
+    for (size_t g = 0; g < session->graph_count; ++g) {
+        drop_graph(&session->graphs[g]);
     }
     if (session->arena != NULL) {
         (void)cudaFree(session->arena);
@@ -160,6 +193,7 @@ void m3_session_free(m3_session *session)
     free(session->sync_current);
     free(session->events);
     free(session->ew_templates);
+    free(session->ew_choices);
     free(session->descriptions);
     free(session->metadata);
     free(session->node_kinds);
@@ -224,6 +258,13 @@ static void build_templates(m3_session *s)
             t->outputs[k].raw = l->output_raw[k] ? 1 : 0;
         }
         t->absmax_command = l->absmax_command;
+        {
+            /* the choice depends on whether the launch reduces */
+            m3c_ew_params probe = *t;
+
+            probe.reduce = l->has_absmax ? &s->reduce[i] : NULL;
+            (void)m3c_ew_choose(&probe, &s->ew_choices[i]);
+        }
     }
 }
 
@@ -304,6 +345,8 @@ m3_status m3_cuda_session_create(m3_session **session_output,
     s->sync_current = calloc(count, 1U);
     s->ew_templates = calloc(s->plan.launch_count ? s->plan.launch_count : 1U,
                              sizeof(*s->ew_templates));
+    s->ew_choices = calloc(s->plan.launch_count ? s->plan.launch_count : 1U,
+                           sizeof(*s->ew_choices));
     s->node_kinds = calloc(graph->node_count ? graph->node_count : 1U,
                            sizeof(*s->node_kinds));
     if (s->node_kinds != NULL) {
@@ -316,7 +359,7 @@ m3_status m3_cuda_session_create(m3_session **session_output,
         s->buffer[0] == NULL || s->buffer[1] == NULL ||
         s->sync_buffer[0] == NULL || s->sync_buffer[1] == NULL ||
         s->current == NULL || s->sync_current == NULL ||
-        s->ew_templates == NULL) {
+        s->ew_templates == NULL || s->ew_choices == NULL) {
         m3_session_free(s);
         return m3c_error_set(error, M3_STATUS_OUT_OF_MEMORY,
                              "cannot allocate session plan arrays");
@@ -450,7 +493,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
             p.reduce = &s->reduce[index];
             p.absmax_out = ref_pointer(s, l->absmax_out);
         }
-        return m3c_launch_ew(&p, s->stream);
+        return m3c_launch_ew_chosen(&s->ew_choices[index], &p, s->stream);
     }
     if (l->kind == M3C_LAUNCH_SOFTMAX) {
         const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
@@ -505,45 +548,6 @@ static int launch_one(m3_session *s, size_t index, bool first)
     }
 }
 
-m3_status m3_cuda_session_run_async(m3_session *s, m3_error *error)
-{
-    size_t i;
-    m3_status status;
-
-    if (s == NULL) {
-        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                             "session is null");
-    }
-    if (s->plan.launch_count == 0U) {
-        m3_error_reset(error);
-        return M3_STATUS_OK;
-    }
-    status = use_device(s, error);
-    if (status != M3_STATUS_OK) {
-        return status;
-    }
-    status = push_event(s, EVENT_RUN, 0U, 0U, error);
-    if (status != M3_STATUS_OK) {
-        return status;
-    }
-    for (i = 0U; i < s->plan.launch_count; ++i) {
-        int code = launch_one(s, i, i == 0U);
-
-        if (code != 0) {
-            return m3c_error_set(error, M3_STATUS_INTERNAL,
-                                 "kernel launch failed: %s",
-                                 m3c_cuda_error_string(code));
-        }
-    }
-    /* assume success; a failure found at synchronise is replayed */
-    for (i = 0U; i < s->plan.flip_count; ++i) {
-        s->current[s->plan.flip_slot[i]] ^= 1U;
-    }
-    ++s->pending_runs;
-    m3_error_reset(error);
-    return M3_STATUS_OK;
-}
-
 static void apply_swap(m3_session *s, size_t a, size_t b)
 {
     unsigned char *held = s->buffer[s->current[a]][a];
@@ -551,6 +555,228 @@ static void apply_swap(m3_session *s, size_t a, size_t b)
     s->buffer[s->current[a]][a] = s->buffer[s->current[b]][b];
     s->buffer[s->current[b]][b] = held;
 }
+
+/* Host bookkeeping of one enqueued run: its event and the shadow flips a
+ * clean run commits (a failure found at synchronise is replayed). */
+static m3_status account_run(m3_session *s, m3_error *error)
+{
+    size_t i;
+    m3_status status = push_event(s, EVENT_RUN, 0U, 0U, error);
+
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    for (i = 0U; i < s->plan.flip_count; ++i) {
+        s->current[s->plan.flip_slot[i]] ^= 1U;
+    }
+    ++s->pending_runs;
+    return M3_STATUS_OK;
+}
+
+static m3_status account_swap(m3_session *s, size_t a, size_t b,
+                              m3_error *error)
+{
+    m3_status status = push_event(s, EVENT_SWAP, a, b, error);
+
+    if (status == M3_STATUS_OK) {
+        apply_swap(s, a, b);
+    }
+    return status;
+}
+
+/* The launches of one run with the buffer assignment as it stands. */
+static int launch_run(m3_session *s)
+{
+    size_t i;
+
+    for (i = 0U; i < s->plan.launch_count; ++i) {
+        int code = launch_one(s, i, i == 0U);
+
+        if (code != 0) {
+            return code;
+        }
+    }
+    return 0;
+}
+
+static bool graph_matches(const m3_session *s, const run_graph *g,
+                          size_t runs, size_t a, size_t b)
+{
+    size_t slots = s->plan.slot_count;
+
+    return g->exec != NULL && g->runs == runs && g->swap_a == a &&
+           g->swap_b == b &&
+           memcmp(g->start_current, s->current, slots) == 0 &&
+           memcmp(g->start_buffer[0], s->buffer[0],
+                  slots * sizeof(unsigned char *)) == 0 &&
+           memcmp(g->start_buffer[1], s->buffer[1],
+                  slots * sizeof(unsigned char *)) == 0;
+}
+
+/* Record the launches of `runs` runs (slots a/b exchanged between them) into
+ * a CUDA graph by stream capture, leaving the host state as it was.  NULL
+ * when capture is not possible on this stream; the caller then launches
+ * directly. */
+static cudaGraphExec_t capture_runs(m3_session *s, size_t runs, size_t a,
+                                    size_t b)
+{
+    size_t slots = s->plan.slot_count ? s->plan.slot_count : 1U;
+    run_graph entry;
+    cudaGraph_t graph = NULL;
+    cudaGraphExec_t exec = NULL;
+    cudaError_t code;
+    int launched = 0;
+    size_t r;
+    size_t i;
+
+    memset(&entry, 0, sizeof(entry));
+    entry.start_buffer[0] = malloc(slots * sizeof(unsigned char *));
+    entry.start_buffer[1] = malloc(slots * sizeof(unsigned char *));
+    entry.start_current = malloc(slots);
+    if (entry.start_buffer[0] == NULL || entry.start_buffer[1] == NULL ||
+        entry.start_current == NULL) {
+        drop_graph(&entry);
+        return NULL;
+    }
+    memcpy(entry.start_buffer[0], s->buffer[0], slots * sizeof(unsigned char *));
+    memcpy(entry.start_buffer[1], s->buffer[1], slots * sizeof(unsigned char *));
+    memcpy(entry.start_current, s->current, slots);
+    code = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeRelaxed);
+    if (code != cudaSuccess) {
+        (void)cudaGetLastError();
+        drop_graph(&entry);
+        return NULL;
+    }
+    for (r = 0U; r < runs && launched == 0; ++r) {
+        launched = launch_run(s);
+        for (i = 0U; i < s->plan.flip_count; ++i) {
+            s->current[s->plan.flip_slot[i]] ^= 1U;
+        }
+        if (r + 1U < runs && a != SIZE_MAX) {
+            apply_swap(s, a, b);
+        }
+    }
+    code = cudaStreamEndCapture(s->stream, &graph);
+    /* back to the state the runs start from */
+    memcpy(s->buffer[0], entry.start_buffer[0], slots * sizeof(unsigned char *));
+    memcpy(s->buffer[1], entry.start_buffer[1], slots * sizeof(unsigned char *));
+    memcpy(s->current, entry.start_current, slots);
+    if (code == cudaSuccess && launched == 0) {
+        code = cudaGraphInstantiate(&exec, graph, 0ULL);
+    }
+    if (graph != NULL) {
+        (void)cudaGraphDestroy(graph);
+    }
+    (void)cudaGetLastError();
+    if (code != cudaSuccess || launched != 0 || exec == NULL) {
+        drop_graph(&entry);
+        return NULL;
+    }
+    entry.runs = runs;
+    entry.swap_a = a;
+    entry.swap_b = b;
+    entry.exec = exec;
+    if (s->graph_count < M3C_RUN_GRAPHS) {
+        s->graphs[s->graph_count++] = entry;
+    } else {
+        drop_graph(&s->graphs[s->graph_next]);
+        s->graphs[s->graph_next] = entry;
+        s->graph_next = (s->graph_next + 1U) % M3C_RUN_GRAPHS;
+    }
+    return exec;
+}
+
+/* Enqueue `runs` runs, exchanging slots a and b between consecutive runs
+ * (SIZE_MAX: no exchange).  With cuda_graphs the whole sequence is one graph
+ * launch, captured on first use for each starting buffer assignment and kept
+ * (up to M3C_RUN_GRAPHS sequences); without it, or on a stream that cannot
+ * be captured (the legacy default stream, or one the caller is capturing
+ * already), the kernels are launched one by one. */
+static m3_status enqueue_runs(m3_session *s, size_t runs, size_t a, size_t b,
+                              m3_error *error)
+{
+    bool graphed = false;
+    m3_status status;
+    size_t r;
+
+    if (runs == 0U) {
+        m3_error_reset(error);
+        return M3_STATUS_OK;
+    }
+    if (s->plan.launch_count == 0U) {
+        /* nothing runs; only the exchanges take effect */
+        for (r = 0U; r + 1U < runs && a != SIZE_MAX; ++r) {
+            status = account_swap(s, a, b, error);
+            if (status != M3_STATUS_OK) {
+                return status;
+            }
+        }
+        m3_error_reset(error);
+        return M3_STATUS_OK;
+    }
+    status = use_device(s, error);
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    if (s->cuda.cuda_graphs) {
+        enum cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+
+        if (cudaStreamIsCapturing(s->stream, &capturing) == cudaSuccess &&
+            capturing == cudaStreamCaptureStatusNone) {
+            cudaGraphExec_t exec = NULL;
+            size_t g;
+
+            for (g = 0U; g < s->graph_count && exec == NULL; ++g) {
+                if (graph_matches(s, &s->graphs[g], runs, a, b)) {
+                    exec = s->graphs[g].exec;
+                }
+            }
+            if (exec == NULL) {
+                exec = capture_runs(s, runs, a, b);
+            }
+            if (exec != NULL) {
+                cudaError_t code = cudaGraphLaunch(exec, s->stream);
+
+                if (code != cudaSuccess) {
+                    return cuda_failure(error, code, "graph launch failed");
+                }
+                graphed = true;
+            }
+        }
+        (void)cudaGetLastError();
+    }
+    for (r = 0U; r < runs; ++r) {
+        if (!graphed) {
+            int code = launch_run(s);
+
+            if (code != 0) {
+                return m3c_error_set(error, M3_STATUS_INTERNAL,
+                                     "kernel launch failed: %s",
+                                     m3c_cuda_error_string(code));
+            }
+        }
+        /* assume success; a failure found at synchronise is replayed */
+        status = account_run(s, error);
+        if (status == M3_STATUS_OK && r + 1U < runs && a != SIZE_MAX) {
+            status = account_swap(s, a, b, error);
+        }
+        if (status != M3_STATUS_OK) {
+            return status;
+        }
+    }
+    m3_error_reset(error);
+    return M3_STATUS_OK;
+}
+
+m3_status m3_cuda_session_run_async(m3_session *s, m3_error *error)
+{
+    if (s == NULL) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "session is null");
+    }
+    return enqueue_runs(s, 1U, SIZE_MAX, SIZE_MAX, error);
+}
+
 
 /* The reference's data-check messages (src/m3_op_data_preflight.c:23,
  * :283-291). */
@@ -898,6 +1124,39 @@ m3_status m3_cuda_session_swap_values(m3_session *s, m3_graph_value_id input,
     apply_swap(s, a, b);
     m3_error_reset(error);
     return M3_STATUS_OK;
+}
+
+m3_status m3_cuda_session_run_steps_async(m3_session *s, size_t count,
+                                          m3_graph_value_id input,
+                                          m3_graph_value_id output,
+                                          m3_error *error)
+{
+    size_t a = SIZE_MAX;
+    size_t b = SIZE_MAX;
+
+    if (s == NULL) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "session is null");
+    }
+    if (input != M3_GRAPH_VALUE_NONE || output != M3_GRAPH_VALUE_NONE) {
+        m3_status status = value_check(s, input, M3_GRAPH_INPUT,
+                                       "carried input", error);
+
+        if (status == M3_STATUS_OK) {
+            status = value_check(s, output, M3_GRAPH_OUTPUT, "carried output",
+                                 error);
+        }
+        if (status != M3_STATUS_OK) {
+            return status;
+        }
+        if (s->metadata[input].byte_count != s->metadata[output].byte_count) {
+            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                                 "carried values differ in size");
+        }
+        a = s->plan.value_slot[input];
+        b = s->plan.value_slot[output];
+    }
+    return enqueue_runs(s, count, a, b, error);
 }
 
 void *m3_cuda_session_stream(const m3_session *s)

@@ -253,6 +253,9 @@ _CUDA_SIGNATURES = {
         ctypes.POINTER(M3Error)]),
     "m3_cuda_session_run_async": (ctypes.c_int, [ctypes.c_void_p,
                                                  ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_run_steps_async": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
+        ctypes.POINTER(M3Error)]),
     "m3_cuda_session_synchronize": (ctypes.c_int, [ctypes.c_void_p,
                                                    ctypes.POINTER(M3Error)]),
     "m3_cuda_session_value_device_pointer": (ctypes.c_int, [
@@ -467,7 +470,7 @@ class Session:
     def __init__(self, graph: Graph, allow_metal: bool = True,
                  allow_cpu: bool = True, allow_neural_engine: bool = True,
                  device: int = -1, stream: int | None = None,
-                 fuse: bool = True, cuda: bool = True):
+                 fuse: bool = True, cuda: bool = True, cuda_graphs: bool = True):
         self.lib = graph.lib
         self.values = list(graph.values)
         self.handle = ctypes.c_void_p()
@@ -480,6 +483,7 @@ class Session:
             extra.device = device
             extra.stream = stream
             extra.fuse = fuse
+            extra.cuda_graphs = cuda_graphs
             status = self.lib.m3_cuda_session_create(
                 ctypes.byref(self.handle), graph.handle, ctypes.byref(options),
                 ctypes.byref(extra), ctypes.byref(err))
@@ -530,6 +534,16 @@ class Session:
         err = M3Error()
         check(self.lib.m3_cuda_session_run_async(self.handle,
                                                  ctypes.byref(err)), err)
+
+    def run_steps(self, count: int, carried_in: int | None = None,
+                  carried_out: int | None = None) -> None:
+        """m3_cuda_session_run_steps_async: `count` runs, exchanging
+        carried_in and carried_out between consecutive runs."""
+        none = 0xFFFFFFFF
+        err = M3Error()
+        check(self.lib.m3_cuda_session_run_steps_async(
+            self.handle, count, none if carried_in is None else carried_in,
+            none if carried_out is None else carried_out, ctypes.byref(err)), err)
 
     def synchronize(self) -> None:
         err = M3Error()

@@ -480,9 +480,12 @@ def test_liveness_graph_and_plan_info(m3, gpu):
     assert failure.value.status == m3.INVALID_ARGUMENT
 
 
-def test_async_runs_and_swap_carry_state(m3, ref, gpu):
-    """Thirty Euler steps carried on the device (run_async + swap) equal
-    thirty synchronous runs with host round trips."""
+@pytest.mark.parametrize("mode", ["async", "async_no_graphs", "steps"])
+def test_async_runs_and_swap_carry_state(m3, ref, gpu, mode):
+    """Thirty Euler steps carried on the device equal thirty synchronous
+    runs with host round trips: run_async + swap (each run one graph launch,
+    or plain launches), and run_steps (the thirty runs as one graph launch).
+    The sequence runs twice so the second pass replays cached graphs."""
     rng = np.random.default_rng(3)
     shape = (2, 8, 96)
     x0, vc, vu = (rng.standard_normal(shape).astype(np.float32) for _ in range(3))
@@ -524,17 +527,21 @@ def test_async_runs_and_swap_carry_state(m3, ref, gpu):
 
     g = m3.Graph()
     x, c, u, xn, xb = build(g)
-    s = m3.Session(g)
+    s = m3.Session(g, cuda_graphs=mode != "async_no_graphs")
     s.write(c, vc)
     s.write(u, vu)
-    s.write(x, x0)
-    for step in range(30):
-        s.run_async()
-        if step != 29:
-            s.swap(x, xn)
-    s.synchronize()
-    assert np.array_equal(bits(s.read(xn)), bits(state))
-    assert np.array_equal(s.read(xb), ref_bf16)
+    for _ in range(2):
+        s.write(x, x0)
+        if mode == "steps":
+            s.run_steps(30, x, xn)
+        else:
+            for step in range(30):
+                s.run_async()
+                if step != 29:
+                    s.swap(x, xn)
+        s.synchronize()
+        assert np.array_equal(bits(s.read(xn)), bits(state))
+        assert np.array_equal(s.read(xb), ref_bf16)
 
 
 # ------------------------------------------------- backend plug-in path
