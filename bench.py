@@ -620,7 +620,7 @@ def main():
             for _ in range(config.runs_per_step):
                 session.run_async()
         if collective is not None:
-            session.read_device(outputs[0], collective.data_ptr(), 4)
+            session.read_device_async(outputs[0], collective.data_ptr(), 4)
             shardsmod().global_abs_max_bits(collective)
 
     for _ in range(args.warmup):

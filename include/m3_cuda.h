@@ -509,6 +509,16 @@ m3_status m3_cuda_session_read_output_device(const m3_session *session,
                                              size_t byte_count,
                                              m3_error *error);
 
+/* As m3_cuda_session_read_output_device, but enqueued on the session's
+ * stream without waiting: the copy reads the output as it stands after the
+ * runs already enqueued, assuming they succeed.  If one of them fails (as
+ * the next m3_cuda_session_synchronize reports), the copied bytes are
+ * unspecified.  For pipelines that hand an output to another stream-ordered
+ * consumer, such as a collective, without a host round trip. */
+m3_status m3_cuda_session_read_output_device_async(
+    m3_session *session, m3_graph_value_id value, void *device_destination,
+    size_t byte_count, m3_error *error);
+
 /* Exchange the storage of an INPUT and an OUTPUT value of equal byte size, in
  * O(1) and without copying: the next run reads as input what the last run
  * wrote as output.  Carries a solver state between runs (the flow solver's

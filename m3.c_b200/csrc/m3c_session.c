@@ -1067,6 +1067,38 @@ m3_status m3_cuda_session_read_output_device(const m3_session *session,
                       cudaMemcpyDeviceToDevice, error);
 }
 
+m3_status m3_cuda_session_read_output_device_async(
+    m3_session *s, m3_graph_value_id value, void *device_destination,
+    size_t byte_count, m3_error *error)
+{
+    cudaError_t code;
+    m3_status status = value_check(s, value, M3_GRAPH_OUTPUT, "output read",
+                                   error);
+
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    if (byte_count != s->metadata[value].byte_count ||
+        (byte_count != 0U && device_destination == NULL)) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "output read size does not match tensor");
+    }
+    status = use_device(s, error);
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    if (byte_count != 0U) {
+        /* the buffer the value occupies once the pending runs succeed */
+        code = cudaMemcpyAsync(device_destination, value_pointer(s, value, false),
+                               byte_count, cudaMemcpyDeviceToDevice, s->stream);
+        if (code != cudaSuccess) {
+            return cuda_failure(error, code, "session copy failed");
+        }
+    }
+    m3_error_reset(error);
+    return M3_STATUS_OK;
+}
+
 m3_status m3_cuda_session_value_device_pointer(const m3_session *session,
                                                m3_graph_value_id value,
                                                void **device_pointer,

@@ -267,6 +267,9 @@ _CUDA_SIGNATURES = {
     "m3_cuda_session_read_output_device": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
         ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_read_output_device_async": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.POINTER(M3Error)]),
     "m3_cuda_session_swap_values": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.POINTER(M3Error)]),
@@ -593,6 +596,13 @@ class Session:
         check(self.lib.m3_cuda_session_read_output_device(
             self.handle, vid, ctypes.c_void_p(pointer), nbytes,
             ctypes.byref(err)), err)
+
+    def read_device_async(self, vid: int, pointer: int, nbytes: int) -> None:
+        """m3_cuda_session_read_output_device_async: stream-ordered copy of
+        an output into device memory, no host wait."""
+        err = M3Error()
+        check(self.lib.m3_cuda_session_read_output_device_async(
+            self.handle, vid, ctypes.c_void_p(pointer), nbytes, ctypes.byref(err)), err)
 
     def swap(self, input_vid: int, output_vid: int) -> None:
         err = M3Error()

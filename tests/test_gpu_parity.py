@@ -319,6 +319,27 @@ def test_abs_max_nan_and_empty(m3, gpu):
     assert s.read(m)[0] == 0.0
 
 
+def test_async_device_read_follows_pending_runs(m3, gpu):
+    """read_device_async copies the output of the runs enqueued before it
+    (ABS_MAX writes a shadow buffer that only becomes current when its run
+    is committed), with no host wait in between."""
+    import torch
+
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (1000,))
+    m = g.inferred("ABS_MAX", [x], m3.OUTPUT, m3.F32)
+    g.node("ABS_MAX", [x], [m])
+    s = m3.Session(g)
+    data = np.linspace(-3, 2, 1000).astype(np.float32)
+    out = torch.zeros(2, dtype=torch.float32, device="cuda")
+    for k, scale in enumerate((1.0, 2.0)):
+        s.write(x, data * np.float32(scale))
+        s.run_async()
+        s.read_device_async(m, out.data_ptr() + 4 * k, 4)
+    s.synchronize()
+    assert out.cpu().tolist() == [3.0, 6.0]
+
+
 # ----------------------------------------------------------- row kernels
 
 
