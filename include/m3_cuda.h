@@ -486,6 +486,26 @@ m3_status m3_cuda_session_run_steps_async(m3_session *session, size_t count,
                                           m3_graph_value_id input,
                                           m3_graph_value_id output,
                                           m3_error *error);
+
+/* One run fed from and drained to host memory, enqueued without waiting.
+ * The inputs are uploaded on a copy stream of the session into one of two
+ * device staging areas and copied into their values on the session's stream
+ * ahead of the run; after the run the outputs are copied to the other side
+ * of the staging and downloaded on a second copy stream.  Consecutive
+ * submissions alternate staging areas, so one submission's upload overlaps
+ * the previous one's download (PCIe carries both directions at once) and the
+ * runs themselves.  Host buffers should be pinned (cudaHostAlloc) for the
+ * copies to be asynchronous; they must stay valid and untouched until the
+ * next m3_cuda_session_synchronize, which waits for the downloads too.  If a
+ * run fails (reported by that synchronise), the host outputs of its
+ * submission and of later ones are unspecified; the values in the session
+ * keep the reference's failure semantics.  The staging areas (twice the
+ * submitted bytes) are allocated on first use and grown when needed. */
+m3_status m3_cuda_session_submit_host_async(
+    m3_session *session, size_t input_count, const m3_graph_value_id *inputs,
+    const void *const *input_data, size_t output_count,
+    const m3_graph_value_id *outputs, void *const *output_data,
+    m3_error *error);
 m3_status m3_cuda_session_synchronize(m3_session *session, m3_error *error);
 
 /* Device address and byte size of a value's current storage (valid until the

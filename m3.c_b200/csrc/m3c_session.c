@@ -49,6 +49,24 @@ typedef struct {
     cudaGraphExec_t exec;
 } run_graph;
 
+/* Pipelined host submissions (m3_cuda_session_submit_host_async): uploads
+ * on one stream and downloads on another, through two staging areas used in
+ * turn, so one submission's upload overlaps the previous one's download. */
+typedef struct {
+    cudaStream_t upload;
+    cudaStream_t download;
+    unsigned char *stage_in[2];
+    unsigned char *stage_out[2];
+    size_t in_bytes;
+    size_t out_bytes;
+    cudaEvent_t uploaded[2];   /* staging input filled */
+    cudaEvent_t consumed[2];   /* staging input copied into the session */
+    cudaEvent_t produced[2];   /* staging output filled */
+    cudaEvent_t drained[2];    /* staging output copied to the host */
+    unsigned turn;
+    bool ready;
+} host_pipe;
+
 struct m3_session {
     m3c_plan plan;
     m3_graph_value_desc *descriptions;
@@ -82,6 +100,8 @@ struct m3_session {
     run_graph graphs[M3C_RUN_GRAPHS];
     size_t graph_count;
     size_t graph_next;
+    /* host submissions: copy streams, double-buffered staging, events */
+    host_pipe pipe;
 };
 
 static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, 0U};
@@ -150,6 +170,29 @@ static void drop_graph(run_graph *g)
     memset(g, 0, sizeof(*g));
 }
 
+static void drop_pipe(host_pipe *p)
+{
+    int k;
+
+    if (p->upload != NULL) {
+        (void)cudaStreamSynchronize(p->upload);
+        (void)cudaStreamDestroy(p->upload);
+    }
+    if (p->download != NULL) {
+        (void)cudaStreamSynchronize(p->download);
+        (void)cudaStreamDestroy(p->download);
+    }
+    for (k = 0; k < 2; ++k) {
+        (void)cudaFree(p->stage_in[k]);
+        (void)cudaFree(p->stage_out[k]);
+        if (p->uploaded[k] != NULL) (void)cudaEventDestroy(p->uploaded[k]);
+        if (p->consumed[k] != NULL) (void)cudaEventDestroy(p->consumed[k]);
+        if (p->produced[k] != NULL) (void)cudaEventDestroy(p->produced[k]);
+        if (p->drained[k] != NULL) (void)cudaEventDestroy(p->drained[k]);
+    }
+    memset(p, 0, sizeof(*p));
+}
+
 void m3_session_free(m3_session *session)
 {
     if (session == NULL) {
@@ -169,6 +212,7 @@ void m3_session_free(m3_session *session)
     for (size_t g = 0; g < session->graph_count; ++g) {
         drop_graph(&session->graphs[g]);
     }
+    drop_pipe(&session->pipe);
     if (session->arena != NULL) {
         (void)cudaFree(session->arena);
     }
@@ -812,6 +856,13 @@ static m3_status settle(m3_session *s, m3_error *error)
     if (code == cudaSuccess) {
         code = cudaStreamSynchronize(s->stream);
     }
+    if (code == cudaSuccess && s->pipe.ready) {
+        /* host submissions: their downloads finish after the runs */
+        code = cudaStreamSynchronize(s->pipe.upload);
+        if (code == cudaSuccess) {
+            code = cudaStreamSynchronize(s->pipe.download);
+        }
+    }
     if (code != cudaSuccess) {
         return cuda_failure(error, code, "device execution failed");
     }
@@ -1189,6 +1240,170 @@ m3_status m3_cuda_session_run_steps_async(m3_session *s, size_t count,
         b = s->plan.value_slot[output];
     }
     return enqueue_runs(s, count, a, b, error);
+}
+
+/* Copy streams, events and staging areas of at least the given sizes. */
+static m3_status pipe_ready(m3_session *s, size_t in_bytes, size_t out_bytes,
+                            m3_error *error)
+{
+    host_pipe *p = &s->pipe;
+    cudaError_t code = cudaSuccess;
+    int k;
+
+    if (p->ready && in_bytes <= p->in_bytes && out_bytes <= p->out_bytes) {
+        return M3_STATUS_OK;
+    }
+    if (p->ready) {
+        /* grow: earlier submissions may still use the old areas */
+        code = cudaStreamSynchronize(s->stream);
+        if (code == cudaSuccess) code = cudaStreamSynchronize(p->upload);
+        if (code == cudaSuccess) code = cudaStreamSynchronize(p->download);
+        for (k = 0; k < 2; ++k) {
+            (void)cudaFree(p->stage_in[k]);
+            (void)cudaFree(p->stage_out[k]);
+            p->stage_in[k] = NULL;
+            p->stage_out[k] = NULL;
+        }
+    } else {
+        code = cudaStreamCreateWithFlags(&p->upload, cudaStreamNonBlocking);
+        if (code == cudaSuccess) {
+            code = cudaStreamCreateWithFlags(&p->download, cudaStreamNonBlocking);
+        }
+        for (k = 0; k < 2 && code == cudaSuccess; ++k) {
+            code = cudaEventCreateWithFlags(&p->uploaded[k], cudaEventDisableTiming);
+            if (code == cudaSuccess) code = cudaEventCreateWithFlags(&p->consumed[k], cudaEventDisableTiming);
+            if (code == cudaSuccess) code = cudaEventCreateWithFlags(&p->produced[k], cudaEventDisableTiming);
+            if (code == cudaSuccess) code = cudaEventCreateWithFlags(&p->drained[k], cudaEventDisableTiming);
+        }
+    }
+    for (k = 0; k < 2 && code == cudaSuccess; ++k) {
+        code = cudaMalloc((void **)&p->stage_in[k], in_bytes ? in_bytes : 1U);
+        if (code == cudaSuccess) {
+            code = cudaMalloc((void **)&p->stage_out[k], out_bytes ? out_bytes : 1U);
+        }
+    }
+    if (code != cudaSuccess) {
+        drop_pipe(p);
+        return cuda_failure(error, code, "cannot set up host submissions");
+    }
+    p->in_bytes = in_bytes;
+    p->out_bytes = out_bytes;
+    p->ready = true;
+    return M3_STATUS_OK;
+}
+
+m3_status m3_cuda_session_submit_host_async(
+    m3_session *s, size_t input_count, const m3_graph_value_id *inputs,
+    const void *const *input_data, size_t output_count,
+    const m3_graph_value_id *outputs, void *const *output_data,
+    m3_error *error)
+{
+    host_pipe *p;
+    size_t in_bytes = 0U;
+    size_t out_bytes = 0U;
+    size_t offset;
+    size_t k;
+    unsigned t;
+    cudaError_t code = cudaSuccess;
+    m3_status status;
+
+    if (s == NULL || (input_count != 0U && (inputs == NULL || input_data == NULL)) ||
+        (output_count != 0U && (outputs == NULL || output_data == NULL))) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "session, values and host buffers are required");
+    }
+    for (k = 0U; k < input_count; ++k) {
+        status = value_check(s, inputs[k], M3_GRAPH_INPUT, "submitted input", error);
+        if (status != M3_STATUS_OK) {
+            return status;
+        }
+        if (input_data[k] == NULL && s->metadata[inputs[k]].byte_count != 0U) {
+            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                                 "submitted input %zu has no host buffer", k);
+        }
+        in_bytes += (s->metadata[inputs[k]].byte_count + 255U) & ~(size_t)255U;
+    }
+    for (k = 0U; k < output_count; ++k) {
+        status = value_check(s, outputs[k], M3_GRAPH_OUTPUT, "submitted output", error);
+        if (status != M3_STATUS_OK) {
+            return status;
+        }
+        if (output_data[k] == NULL && s->metadata[outputs[k]].byte_count != 0U) {
+            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                                 "submitted output %zu has no host buffer", k);
+        }
+        out_bytes += (s->metadata[outputs[k]].byte_count + 255U) & ~(size_t)255U;
+    }
+    status = use_device(s, error);
+    if (status == M3_STATUS_OK) {
+        status = pipe_ready(s, in_bytes, out_bytes, error);
+    }
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    p = &s->pipe;
+    t = p->turn;
+    /* upload into this turn's staging area once its last reader is done */
+    code = cudaStreamWaitEvent(p->upload, p->consumed[t], 0);
+    for (k = 0U, offset = 0U; k < input_count && code == cudaSuccess; ++k) {
+        size_t bytes = s->metadata[inputs[k]].byte_count;
+
+        if (bytes != 0U) {
+            code = cudaMemcpyAsync(p->stage_in[t] + offset, input_data[k], bytes,
+                                   cudaMemcpyHostToDevice, p->upload);
+        }
+        offset += (bytes + 255U) & ~(size_t)255U;
+    }
+    if (code == cudaSuccess) code = cudaEventRecord(p->uploaded[t], p->upload);
+    /* on the session stream: staging -> inputs, the run, outputs -> staging */
+    if (code == cudaSuccess) code = cudaStreamWaitEvent(s->stream, p->uploaded[t], 0);
+    for (k = 0U, offset = 0U; k < input_count && code == cudaSuccess; ++k) {
+        size_t bytes = s->metadata[inputs[k]].byte_count;
+
+        if (bytes != 0U) {
+            code = cudaMemcpyAsync(value_pointer(s, inputs[k], false), p->stage_in[t] + offset,
+                                   bytes, cudaMemcpyDeviceToDevice, s->stream);
+        }
+        offset += (bytes + 255U) & ~(size_t)255U;
+    }
+    if (code == cudaSuccess) code = cudaEventRecord(p->consumed[t], s->stream);
+    if (code != cudaSuccess) {
+        return cuda_failure(error, code, "host submission upload failed");
+    }
+    status = enqueue_runs(s, 1U, SIZE_MAX, SIZE_MAX, error);
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    code = cudaStreamWaitEvent(s->stream, p->drained[t], 0);
+    for (k = 0U, offset = 0U; k < output_count && code == cudaSuccess; ++k) {
+        size_t bytes = s->metadata[outputs[k]].byte_count;
+
+        if (bytes != 0U) {
+            /* the buffer the output occupies once this run succeeds */
+            code = cudaMemcpyAsync(p->stage_out[t] + offset, value_pointer(s, outputs[k], false),
+                                   bytes, cudaMemcpyDeviceToDevice, s->stream);
+        }
+        offset += (bytes + 255U) & ~(size_t)255U;
+    }
+    if (code == cudaSuccess) code = cudaEventRecord(p->produced[t], s->stream);
+    /* download once produced */
+    if (code == cudaSuccess) code = cudaStreamWaitEvent(p->download, p->produced[t], 0);
+    for (k = 0U, offset = 0U; k < output_count && code == cudaSuccess; ++k) {
+        size_t bytes = s->metadata[outputs[k]].byte_count;
+
+        if (bytes != 0U) {
+            code = cudaMemcpyAsync(output_data[k], p->stage_out[t] + offset, bytes,
+                                   cudaMemcpyDeviceToHost, p->download);
+        }
+        offset += (bytes + 255U) & ~(size_t)255U;
+    }
+    if (code == cudaSuccess) code = cudaEventRecord(p->drained[t], p->download);
+    if (code != cudaSuccess) {
+        return cuda_failure(error, code, "host submission download failed");
+    }
+    p->turn = t ^ 1U;
+    m3_error_reset(error);
+    return M3_STATUS_OK;
 }
 
 void *m3_cuda_session_stream(const m3_session *s)

@@ -253,6 +253,10 @@ _CUDA_SIGNATURES = {
         ctypes.POINTER(M3Error)]),
     "m3_cuda_session_run_async": (ctypes.c_int, [ctypes.c_void_p,
                                                  ctypes.POINTER(M3Error)]),
+    "m3_cuda_session_submit_host_async": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint32),
+        ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint32),
+        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(M3Error)]),
     "m3_cuda_session_run_steps_async": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
         ctypes.POINTER(M3Error)]),
@@ -547,6 +551,19 @@ class Session:
         check(self.lib.m3_cuda_session_run_steps_async(
             self.handle, count, none if carried_in is None else carried_in,
             none if carried_out is None else carried_out, ctypes.byref(err)), err)
+
+    def submit_host(self, inputs: dict, outputs: dict) -> None:
+        """m3_cuda_session_submit_host_async: {value id: host pointer} for
+        inputs and outputs (pinned memory for asynchronous copies); the
+        buffers must stay valid until synchronize()."""
+        ni, no = len(inputs), len(outputs)
+        in_ids = (ctypes.c_uint32 * max(ni, 1))(*inputs.keys())
+        in_ptr = (ctypes.c_void_p * max(ni, 1))(*inputs.values())
+        out_ids = (ctypes.c_uint32 * max(no, 1))(*outputs.keys())
+        out_ptr = (ctypes.c_void_p * max(no, 1))(*outputs.values())
+        err = M3Error()
+        check(self.lib.m3_cuda_session_submit_host_async(
+            self.handle, ni, in_ids, in_ptr, no, out_ids, out_ptr, ctypes.byref(err)), err)
 
     def synchronize(self) -> None:
         err = M3Error()

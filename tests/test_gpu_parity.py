@@ -340,6 +340,69 @@ def test_async_device_read_follows_pending_runs(m3, gpu):
     assert out.cpu().tolist() == [3.0, 6.0]
 
 
+def test_pipelined_host_submissions_match_synchronous_runs(m3, gpu):
+    """Five submissions with host buffers in flight at once (uploads of one
+    overlapping downloads of the previous) give each batch exactly the
+    outputs of a synchronous write/run/read; a NaN batch fails the
+    synchronise."""
+    import torch
+
+    rows, width = 64, 300
+
+    def build(g):
+        x = g.value(m3.INPUT, m3.F32, (rows, width))
+        b = g.value(m3.INPUT, m3.F32, (1, width))
+        t = g.inferred("ADD", [x, b], m3.TEMPORARY, m3.F32)
+        g.node("ADD", [x, b], [t])
+        p = g.inferred("SOFTMAX", [t], m3.OUTPUT, m3.F32)
+        g.node("SOFTMAX", [t], [p])
+        v = g.inferred("TOP_K", [t], m3.OUTPUT, m3.F32, k=1)
+        i = g.inferred("TOP_K", [t], m3.OUTPUT, m3.I32, output_index=1, k=1)
+        g.node("TOP_K", [t], [v, i], k=1)
+        return x, b, p, v, i
+
+    rng = np.random.default_rng(21)
+    batches = [((rng.standard_normal((rows, width)) * 3).astype(np.float32),
+                rng.standard_normal((1, width)).astype(np.float32)) for _ in range(5)]
+    g = m3.Graph()
+    x, b, p, v, i = build(g)
+    s = m3.Session(g)
+    expected = []
+    for xs, bs in batches:
+        s.write(x, xs)
+        s.write(b, bs)
+        s.run()
+        expected.append([s.read(p).copy(), s.read(v).copy(), s.read(i).copy()])
+
+    def pinned(a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        return t
+
+    ins = [(pinned(xs), pinned(bs)) for xs, bs in batches]
+    outs = [[torch.empty(e.shape, dtype=torch.from_numpy(e).dtype).pin_memory() for e in exp]
+            for exp in expected]
+    for (tx, tb), (tp, tv, ti) in zip(ins, outs):
+        s.submit_host({x: tx.data_ptr(), b: tb.data_ptr()},
+                      {p: tp.data_ptr(), v: tv.data_ptr(), i: ti.data_ptr()})
+    s.synchronize()
+    for got, exp in zip(outs, expected):
+        for t, e in zip(got, exp):
+            assert np.array_equal(bits(t.numpy()), bits(e))
+
+    poisoned = ins[2][0].clone().pin_memory()
+    poisoned[3, 7] = float("nan")
+    s.submit_host({x: ins[1][0].data_ptr(), b: ins[1][1].data_ptr()},
+                  {p: outs[0][0].data_ptr(), v: outs[0][1].data_ptr(), i: outs[0][2].data_ptr()})
+    s.submit_host({x: poisoned.data_ptr(), b: ins[2][1].data_ptr()},
+                  {p: outs[1][0].data_ptr(), v: outs[1][1].data_ptr(), i: outs[1][2].data_ptr()})
+    with pytest.raises(m3.M3Failure) as failure:
+        s.synchronize()
+    assert failure.value.status == m3.OUT_OF_RANGE
+    # the batch before the failure was delivered in full
+    for t, e in zip(outs[0], expected[1]):
+        assert np.array_equal(bits(t.numpy()), bits(e))
+
+
 # ----------------------------------------------------------- row kernels
 
 
