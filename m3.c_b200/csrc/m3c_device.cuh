@@ -161,6 +161,113 @@ __device__ __forceinline__ uint32_t narrow(int dtype, float value)
     return as_bits(value);
 }
 
+// ---------------------------------------------------------- vector codecs
+//
+// For every non-NaN value the hardware conversions above are the reference
+// codecs; only NaN payloads need the integer rules.  The vector forms below
+// test a whole vector for NaN once (a branch that is uniform in practice)
+// and then convert with packed hardware instructions, falling back to the
+// per-element forms when a NaN is present.  m3_cuda_codec_self_test checks
+// them against the per-element codecs.
+
+// Any F16 NaN among the two halves of each word: a half's magnitude m is a
+// NaN exactly when m + 0x3ff carries into bit 15.
+__device__ __forceinline__ bool f16_pairs_have_nan(const uint32_t *w, int words)
+{
+    uint32_t acc = 0u;
+#pragma unroll
+    for (int i = 0; i < words; ++i) acc |= (w[i] & 0x7fff7fffu) + 0x03ff03ffu;
+    return (acc & 0x80008000u) != 0u;
+}
+
+template <int N>
+__device__ __forceinline__ bool any_nan(const float (&x)[N])
+{
+    bool nan = false;
+#pragma unroll
+    for (int t = 0; t < N; ++t) nan |= x[t] != x[t];
+    return nan;
+}
+
+// Widen 2 * WORDS packed 16-bit values (element 2i in the low half of word i).
+template <int WORDS>
+__device__ __forceinline__ void widen_pairs(int dtype, const uint32_t (&w)[WORDS], float (&x)[2 * WORDS])
+{
+    if (dtype == M3C_BF16) {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+            x[2 * i] = as_float(w[i] << 16);
+            x[2 * i + 1] = as_float(w[i] & 0xffff0000u);
+        }
+    } else if (!f16_pairs_have_nan(w, WORDS)) {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+            x[2 * i] = f16_to_f32(w[i] & 0xffffu);
+            x[2 * i + 1] = f16_to_f32(w[i] >> 16);
+        }
+    }
+}
+
+// Narrow 2 * WORDS floats to packed 16-bit storage words.
+template <int WORDS>
+__device__ __forceinline__ void narrow_pairs(int dtype, const float (&x)[2 * WORDS], uint32_t (&w)[WORDS])
+{
+    if (!any_nan(x)) {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+            if (dtype == M3C_BF16) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+            } else {
+                const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+            const uint32_t lo = dtype == M3C_BF16 ? f32_to_bf16(x[2 * i]) : f32_to_f16(x[2 * i]);
+            const uint32_t hi = dtype == M3C_BF16 ? f32_to_bf16(x[2 * i + 1]) : f32_to_f16(x[2 * i + 1]);
+            w[i] = lo | (hi << 16);
+        }
+    }
+}
+
+// round_to on N values (N even) in place.
+template <int N>
+__device__ __forceinline__ void round_values(int dtype, float (&x)[N])
+{
+    if (dtype != M3C_F16 && dtype != M3C_BF16) {
+        return;
+    }
+    if (!any_nan(x)) {
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+            if (dtype == M3C_BF16) {
+                const float2 f = __bfloat1622float2(__floats2bfloat162_rn(x[2 * i], x[2 * i + 1]));
+                x[2 * i] = f.x;
+                x[2 * i + 1] = f.y;
+            } else {
+                const float2 f = __half22float2(__floats2half2_rn(x[2 * i], x[2 * i + 1]));
+                x[2 * i] = f.x;
+                x[2 * i + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < N; ++t) {
+            x[t] = dtype == M3C_BF16 ? bf16_to_f32(f32_to_bf16(x[t])) : f16_to_f32(f32_to_f16(x[t]));
+        }
+    }
+}
+
 // The correctly rounded quotient a / b from y = RN(1/b), after P. Markstein,
 // "Computation of elementary functions on the IBM RISC System/6000
 // processor", IBM J. Res. Develop. 34(1), 1990: q0 = RN(a y) is within one

@@ -307,12 +307,13 @@ __device__ __forceinline__ float snake(float x, float alpha)
     return __fadd_rn(x, scaled);
 }
 
-__device__ __forceinline__ float gated_silu(float gate, float up, int gate_dtype)
+// Round four F32 results to `rdtype` (the reference stores each statement in
+// its dtype) into register words.
+__device__ __forceinline__ void round_words(int rdtype, float (&f)[VEC], uint32_t (&d)[VEC])
 {
-    // src/m3_op_execute_basic.c:113-117
-    const float denominator = __fadd_rn(1.0f, expf(-gate));
-    const float activation = round_to(gate_dtype, __fdiv_rn(gate, denominator));
-    return __fmul_rn(activation, up);
+    round_values<VEC>(rdtype, f);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) d[j] = as_bits(f[j]);
 }
 
 struct Flags {
@@ -330,21 +331,35 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
     reg_get(rf, op.b, b);
     const int rdt = op.rdtype;
     switch (op.code) {
-    case M3C_OP_ADD:
+    case M3C_OP_ADD: {
+        float f[VEC];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-            d[j] = as_bits(round_to(rdt, __fadd_rn(as_float(a[j]), as_float(b[j]))));
+        for (int j = 0; j < VEC; ++j) f[j] = __fadd_rn(as_float(a[j]), as_float(b[j]));
+        round_words(rdt, f, d);
         break;
-    case M3C_OP_MUL:
+    }
+    case M3C_OP_MUL: {
+        float f[VEC];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-            d[j] = as_bits(round_to(rdt, __fmul_rn(as_float(a[j]), as_float(b[j]))));
+        for (int j = 0; j < VEC; ++j) f[j] = __fmul_rn(as_float(a[j]), as_float(b[j]));
+        round_words(rdt, f, d);
         break;
-    case M3C_OP_GSILU:
+    }
+    case M3C_OP_GSILU: {
+        // src/m3_op_execute_basic.c:113-117: the activation g / (1 + e^-g)
+        // is stored in the gate's dtype before the product
+        float f[VEC];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-            d[j] = as_bits(round_to(rdt, gated_silu(as_float(a[j]), as_float(b[j]), op.aux)));
+        for (int j = 0; j < VEC; ++j) {
+            const float gate = as_float(a[j]);
+            f[j] = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
+        }
+        round_values<VEC>(op.aux, f);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) f[j] = __fmul_rn(f[j], as_float(b[j]));
+        round_words(rdt, f, d);
         break;
+    }
     case M3C_OP_SNAKE:
         if (b[0] == b[1] && b[1] == b[2] && b[2] == b[3]) {
             // one channel per block (the common case): the reciprocal of
@@ -366,10 +381,13 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
 #pragma unroll
         for (int j = 0; j < VEC; ++j) d[j] = as_bits(tanhf(as_float(a[j])));
         break;
-    case M3C_OP_ROUND:
+    case M3C_OP_ROUND: {
+        float f[VEC];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) d[j] = as_bits(round_to(rdt, as_float(a[j])));
+        for (int j = 0; j < VEC; ++j) f[j] = as_float(a[j]);
+        round_words(rdt, f, d);
         break;
+    }
     case M3C_OP_F2I:
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
@@ -388,10 +406,19 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
         for (int j = 0; j < VEC; ++j)
             d[j] = as_bits(round_to(rdt, __int2float_rn(static_cast<int32_t>(a[j]))));
         break;
-    case M3C_OP_WIDEN:
+    case M3C_OP_WIDEN: {
+        if (op.aux == M3C_F16 || op.aux == M3C_BF16) {
+            const uint32_t pairs[2] = {(a[0] & 0xffffu) | (a[1] << 16), (a[2] & 0xffffu) | (a[3] << 16)};
+            float f[VEC];
+            widen_pairs<2>(op.aux, pairs, f);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) d[j] = as_bits(widen(op.aux, a[j]));
+            for (int j = 0; j < VEC; ++j) d[j] = as_bits(f[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) d[j] = a[j];
+        }
         break;
+    }
     case M3C_OP_CLAMP:
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
@@ -433,10 +460,15 @@ __device__ __forceinline__ void store_block(const m3c_ew_out &out, uint64_t f, c
 {
     unsigned char *p = static_cast<unsigned char *>(out.base);
     if (out.dtype == M3C_F16 || out.dtype == M3C_BF16) {
-        uint32_t h[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) h[j] = out.raw ? (w[j] & 0xffffu) : narrow(out.dtype, as_float(w[j]));
-        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16)));
+        uint32_t h[2];
+        if (out.raw) {
+            h[0] = (w[0] & 0xffffu) | (w[1] << 16);
+            h[1] = (w[2] & 0xffffu) | (w[3] << 16);
+        } else {
+            const float f[VEC] = {as_float(w[0]), as_float(w[1]), as_float(w[2]), as_float(w[3])};
+            narrow_pairs<2>(out.dtype, f, h);
+        }
+        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0], h[1]));
     } else {
         __stcs(reinterpret_cast<uint4 *>(p + f * 4u), make_uint4(w[0], w[1], w[2], w[3]));
     }
@@ -449,10 +481,15 @@ __device__ __forceinline__ void store_block_c(const m3c_ew_out &out, uint64_t f,
     constexpr bool RAW = ((SIG >> 5) & 1u) != 0u;
     unsigned char *p = static_cast<unsigned char *>(out.base);
     if constexpr (DT == M3C_F16 || DT == M3C_BF16) {
-        uint32_t h[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) h[j] = RAW ? (w[j] & 0xffffu) : narrow(DT, as_float(w[j]));
-        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16)));
+        uint32_t h[2];
+        if constexpr (RAW) {
+            h[0] = (w[0] & 0xffffu) | (w[1] << 16);
+            h[1] = (w[2] & 0xffffu) | (w[3] << 16);
+        } else {
+            const float f[VEC] = {as_float(w[0]), as_float(w[1]), as_float(w[2]), as_float(w[3])};
+            narrow_pairs<2>(DT, f, h);
+        }
+        __stcs(reinterpret_cast<uint2 *>(p + f * 2u), make_uint2(h[0], h[1]));
     } else {
         __stcs(reinterpret_cast<uint4 *>(p + f * 4u), make_uint4(w[0], w[1], w[2], w[3]));
     }

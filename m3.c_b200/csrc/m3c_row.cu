@@ -197,12 +197,11 @@ __device__ __forceinline__ void raw_vector(const unsigned char *row, int v, int 
 {
     const uint4 q = reinterpret_cast<const uint4 *>(row)[v];
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    if (EB == 4) {
+    if constexpr (EB == 4) {
 #pragma unroll
         for (int t = 0; t < 4; ++t) x[t] = as_float(w[t]);
     } else {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) x[t] = widen(dtype, (w[t >> 1] >> ((t & 1) * 16)) & 0xffffu);
+        widen_pairs<4>(dtype, w, x);
     }
 }
 
@@ -218,16 +217,13 @@ __device__ __forceinline__ void store_vec(void *row, int dtype, uint64_t j0, con
             __stcs(out + t, make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]));
         }
     } else {
-        uint32_t h[COUNT];
-#pragma unroll
-        for (int t = 0; t < COUNT; ++t) h[t] = narrow(dtype, v[t]);
+        uint32_t h[COUNT / 2];
+        narrow_pairs<COUNT / 2>(dtype, v, h);
         uint16_t *base = static_cast<uint16_t *>(row) + j0;
-        if (COUNT == 8) {
-            __stcs(reinterpret_cast<uint4 *>(base),
-                   make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                              h[6] | (h[7] << 16)));
+        if constexpr (COUNT == 8) {
+            __stcs(reinterpret_cast<uint4 *>(base), make_uint4(h[0], h[1], h[2], h[3]));
         } else {
-            __stcs(reinterpret_cast<uint2 *>(base), make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16)));
+            __stcs(reinterpret_cast<uint2 *>(base), make_uint2(h[0], h[1]));
         }
     }
 }
@@ -516,17 +512,17 @@ __global__ void __launch_bounds__(TILE_THREADS)
                 for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
                     float a[EPV];
                     float b[EPV];
-                    uint32_t raw[EPV];
                     raw_vector<EB>(reinterpret_cast<const unsigned char *>(arow), v, IN, a);
                     raw_vector<EB>(brow, v, IN, b);
 #pragma unroll
-                    for (int t = 0; t < EPV; ++t) raw[t] = narrow(IN, __fadd_rn(a[t], b[t]));
+                    for (int t = 0; t < EPV; ++t) a[t] = __fadd_rn(a[t], b[t]);
                     uint4 packed;
-                    if (EB == 4) {
-                        packed = make_uint4(raw[0], raw[1], raw[2], raw[3]);
+                    if constexpr (EB == 4) {
+                        packed = make_uint4(as_bits(a[0]), as_bits(a[1]), as_bits(a[2]), as_bits(a[3]));
                     } else {
-                        packed = make_uint4(raw[0] | (raw[1] << 16), raw[2] | (raw[3] << 16),
-                                            raw[4] | (raw[5] << 16), raw[6] | (raw[7] << 16));
+                        uint32_t h[4];
+                        narrow_pairs<4>(IN, a, h);
+                        packed = make_uint4(h[0], h[1], h[2], h[3]);
                     }
                     arow[v] = packed;
                     if (sum_out != nullptr) {
@@ -564,6 +560,13 @@ __global__ void __launch_bounds__(TILE_THREADS)
                 float x[EPV];
                 float y[EPV];
                 raw_vector<EB>(row, v, IN, x);
+                if (!p.layer_norm) {
+                    // x * inv rounded to the input dtype before scaling,
+                    // src/m3_op_execute_dense.c:149-151
+#pragma unroll
+                    for (int k = 0; k < EPV; ++k) x[k] = __fmul_rn(x[k], inverse);
+                    round_values<EPV>(IN, x);
+                }
                 const float4 *w4 = reinterpret_cast<const float4 *>(scale + v * EPV);
                 const float4 *b4 = reinterpret_cast<const float4 *>(bias + v * EPV);
 #pragma unroll
@@ -583,9 +586,7 @@ __global__ void __launch_bounds__(TILE_THREADS)
                             }
                             y[k] = o;
                         } else {
-                            // round to the input dtype before scaling,
-                            // src/m3_op_execute_dense.c:149-151
-                            y[k] = __fmul_rn(round_to(IN, __fmul_rn(x[k], inverse)), ws[t]);
+                            y[k] = __fmul_rn(x[k], ws[t]);
                         }
                     }
                 }

@@ -124,7 +124,9 @@ __global__ void scan_kernel(const void *data, int dtype, uint64_t count, int mod
 
 // Exhaustive agreement of the hardware-assisted codecs with the integer
 // restatement of the reference's encoders: every F32 bit pattern through
-// both F16 and BF16 narrowing, every F16 pattern through widening.
+// both F16 and BF16 narrowing, every F16 pattern through widening; and the
+// vector codecs on eight-value vectors built around every F32 pattern (so
+// both their NaN-free fast path and their NaN path are exercised).
 __global__ void codec_check_kernel(unsigned long long *mismatches)
 {
     unsigned long long local = 0;
@@ -141,6 +143,44 @@ __global__ void codec_check_kernel(unsigned long long *mismatches)
                              as_bits(f16_to_f32(static_cast<uint32_t>(i)))
                          ? 1u
                          : 0u;
+        }
+        {
+            // vector codecs: eight values around this pattern (a NaN in any
+            // lane sends the whole vector to the exact path)
+            const uint32_t b = static_cast<uint32_t>(i);
+            const uint32_t h = b * 2654435761u;
+            float x[8] = {v, as_float(b ^ 0x80000000u), as_float(b + 1u), as_float(h),
+                          as_float(h ^ 0x00400000u), as_float(b >> 3), as_float(~b), as_float(b << 7)};
+            uint32_t w16[4];
+            uint32_t wb[4];
+            narrow_pairs<4>(M3C_F16, x, w16);
+            narrow_pairs<4>(M3C_BF16, x, wb);
+            float r16[8];
+            float rb[8];
+            for (int t = 0; t < 8; ++t) {
+                r16[t] = x[t];
+                rb[t] = x[t];
+            }
+            round_values<8>(M3C_F16, r16);
+            round_values<8>(M3C_BF16, rb);
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t e16 = (w16[t >> 1] >> ((t & 1) * 16)) & 0xffffu;
+                const uint32_t eb = (wb[t >> 1] >> ((t & 1) * 16)) & 0xffffu;
+                local += e16 != f32_to_f16(x[t]) ? 1u : 0u;
+                local += eb != f32_to_bf16(x[t]) ? 1u : 0u;
+                local += as_bits(r16[t]) != as_bits(f16_to_f32(f32_to_f16(x[t]))) ? 1u : 0u;
+                local += as_bits(rb[t]) != as_bits(bf16_to_f32(f32_to_bf16(x[t]))) ? 1u : 0u;
+            }
+            const uint32_t pw[4] = {b, h, b ^ 0x7c007c00u, ~h};
+            float wide16[8];
+            float wideb[8];
+            widen_pairs<4>(M3C_F16, pw, wide16);
+            widen_pairs<4>(M3C_BF16, pw, wideb);
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t e = (pw[t >> 1] >> ((t & 1) * 16)) & 0xffffu;
+                local += as_bits(wide16[t]) != as_bits(f16_to_f32(e)) ? 1u : 0u;
+                local += as_bits(wideb[t]) != as_bits(bf16_to_f32(e)) ? 1u : 0u;
+            }
         }
     }
     if (local != 0) atomicAdd(mismatches, local);
