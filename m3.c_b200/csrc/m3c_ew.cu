@@ -438,16 +438,12 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
         for (int j = 0; j < VEC; ++j) d[j] = a[j];
         break;
     case M3C_OP_ABSMAX:
+        // the largest magnitude bit pattern; a NaN's pattern exceeds every
+        // other, so one test of the running maximum finds NaN inputs (at the
+        // end of the kernel: a failed abs-max publishes nothing)
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-            if (j < valid) {
-                const uint32_t magnitude = a[j] & 0x7fffffffu;
-                if (magnitude > 0x7f800000u) {
-                    flags.fail_command = min(flags.fail_command, static_cast<uint32_t>(op.command));
-                } else {
-                    flags.max_bits = max(flags.max_bits, magnitude);
-                }
-            }
+            flags.max_bits = max(flags.max_bits, j < valid ? (a[j] & 0x7fffffffu) : 0u);
         }
         return;  // no result register
     default:
@@ -695,6 +691,9 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
             Prog::run(p, rf, tail, flags);
             store_outputs(p, blocks * VEC, tail, rf);
         }
+    }
+    if (p.reduce != nullptr && flags.max_bits > 0x7f800000u) {
+        flags.fail_command = min(flags.fail_command, p.absmax_command);  // NaN input
     }
     if (flags.fail_command != 0xffffffffu) {
         record_failure(p.status, flags.fail_command);

@@ -718,3 +718,118 @@ def test_backend_plugin_strided_commands(m3, oracle, gpu):
     for key in list(storages):
         lib.m3_cuda_backend_free_storage(context, storages[key], storages[key])
     lib.m3_cuda_backend_destroy_context(context)
+
+
+class _Backend:
+    """The plug-in context with host-side storage bookkeeping, as the
+    reference's backend layer would hold it."""
+
+    def __init__(self, m3):
+        import ctypes
+
+        self.m3, self.ctypes = m3, ctypes
+        self.lib = m3.load()
+        self.storages = {}
+        self.err = m3.M3Error()
+
+        @m3.STORAGE_DATA
+        def storage_data(storage):
+            return self.storages[storage]
+
+        self._keep = storage_data
+        options = m3.BackendOptions(0, storage_data, False)
+        self.context = ctypes.c_void_p()
+        m3.check(self.lib.m3_cuda_backend_context_create(
+            ctypes.byref(options), ctypes.byref(self.context), ctypes.byref(self.err)), self.err)
+
+    def tensor(self, array):
+        ctypes = self.ctypes
+        handle, data = ctypes.c_void_p(), ctypes.c_void_p()
+        self.m3.check(self.lib.m3_cuda_backend_allocate(
+            self.context, array.nbytes, 64, ctypes.byref(handle), ctypes.byref(data),
+            ctypes.byref(self.err)), self.err)
+        key = len(self.storages) + 1
+        self.storages[key] = data.value
+        self.m3.check(self.lib.m3_cuda_backend_write(
+            self.context, data.value, 0, array.ctypes.data, array.nbytes,
+            ctypes.byref(self.err)), self.err)
+        return key
+
+    def view(self, key, shape, offset=0, dtype=None):
+        m3 = self.m3
+        v = m3.TensorView()
+        v.metadata.dtype = m3.F32 if dtype is None else dtype
+        v.metadata.rank = len(shape)
+        stride = 4
+        for i in reversed(range(len(shape))):
+            v.metadata.shape[i] = shape[i]
+            v.byte_strides[i] = stride
+            stride *= shape[i]
+        count = int(np.prod(shape))
+        v.metadata.element_count = count
+        v.metadata.byte_count = count * 4
+        v.byte_offset = offset
+        v.storage = key
+        return v
+
+    def read(self, key, count):
+        host = np.zeros(count, np.float32)
+        self.m3.check(self.lib.m3_cuda_backend_read(
+            self.context, self.storages[key], 0, host.ctypes.data, host.nbytes,
+            self.ctypes.byref(self.err)), self.err)
+        return host
+
+    def execute(self, commands):
+        cmd = (self.m3.Command * len(commands))()
+        keep = []
+        for i, (kind, a, b, out) in enumerate(commands):
+            cmd[i].kind = self.m3.OPS[kind]
+            keep += [a, b, out]
+            cmd[i].descriptor.add.left = self.ctypes.pointer(a)
+            cmd[i].descriptor.add.right = self.ctypes.pointer(b)
+            cmd[i].descriptor.add.output = self.ctypes.pointer(out)
+        return self.lib.m3_cuda_backend_execute(self.context, cmd, len(commands), None,
+                                                self.ctypes.byref(self.err))
+
+    def close(self):
+        for key in list(self.storages):
+            self.lib.m3_cuda_backend_free_storage(self.context, self.storages[key],
+                                                  self.storages[key])
+        self.lib.m3_cuda_backend_destroy_context(self.context)
+
+
+def test_flow_overlap_blend_through_backend_commands(m3, gpu):
+    """The flow solver's overlap blend as the reference issues it
+    (src/m3_flow_solver_math.c:137-205): MUL(noise_prompt, scalar) ->
+    arithmetic; MUL(previous_latent, scalar) -> the latent's first `overlap`
+    time steps (a view into the latent); ADD(arithmetic, that view) -> the
+    same view (exact alias).  Bit-exact with F32 statements; the rest of the
+    latent is untouched."""
+    rng = np.random.default_rng(31)
+    length, overlap, channels = 40, 12, 24
+    latent = rng.standard_normal((1, length, channels)).astype(np.float32)
+    prompt = rng.standard_normal((1, overlap, channels)).astype(np.float32)
+    previous = rng.standard_normal((1, overlap, channels)).astype(np.float32)
+    c_noise, c_prev = np.float32(0.3125), np.float32(0.6875)
+    be = _Backend(m3)
+    try:
+        k_lat = be.tensor(latent)
+        k_pr = be.tensor(prompt)
+        k_pv = be.tensor(previous)
+        k_s1 = be.tensor(np.array([c_noise], np.float32))
+        k_s2 = be.tensor(np.array([c_prev], np.float32))
+        k_ar = be.tensor(np.zeros((1, overlap, channels), np.float32))
+        head = be.view(k_lat, (1, overlap, channels))
+        status = be.execute([
+            ("MUL", be.view(k_pr, (1, overlap, channels)), be.view(k_s1, (1,)),
+             be.view(k_ar, (1, overlap, channels))),
+            ("MUL", be.view(k_pv, (1, overlap, channels)), be.view(k_s2, (1,)), head),
+            ("ADD", be.view(k_ar, (1, overlap, channels)), head, head),
+        ])
+        assert status == m3.OK
+        got = be.read(k_lat, latent.size).reshape(latent.shape)
+        expect = latent.copy()
+        expect[:, :overlap] = prompt * c_noise + previous * c_prev
+        assert np.array_equal(bits(got), bits(expect))
+    finally:
+        be.close()
