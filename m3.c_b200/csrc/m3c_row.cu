@@ -135,9 +135,7 @@ __device__ __forceinline__ void cp_async_wait_all()
 // the 16-byte pad puts the rows read by the ordered-sum lanes on different
 // banks).  Softmax keeps F32 exponentials `f32_pitch` floats apart, in place
 // over the raw rows for F32 input, else in a second area at `f32_offset`.
-// The residual norm stages its second operand in a second raw area at
-// `b_offset`; the norms keep the scale (and bias) widened to F32 at
-// `param_offset`.  With fewer than 8 rows, `group` warps share a row.
+// The norms keep the scale (and bias) widened to F32 at `param_offset`.  With fewer than 8 rows, `group` warps share a row.
 struct Tile {
     int rows;
     int width;
@@ -145,7 +143,6 @@ struct Tile {
     int raw_pitch;
     int f32_pitch;
     int f32_offset;
-    int b_offset;
     int param_offset;
     int group;
 };
@@ -486,7 +483,6 @@ __global__ void __launch_bounds__(TILE_THREADS)
     const uint4 *xa = static_cast<const uint4 *>(p.x);
     const uint4 *xb = static_cast<const uint4 *>(p.resid_b);
     uint4 *sum_out = static_cast<uint4 *>(p.sum_out);
-    unsigned char *bstage = smem + g.b_offset;
     float *scale = reinterpret_cast<float *>(smem + g.param_offset);
     float *bias = scale + g.width;
     for (int j = static_cast<int>(threadIdx.x); j < g.width; j += TILE_THREADS) {
@@ -500,7 +496,6 @@ __global__ void __launch_bounds__(TILE_THREADS)
         const uint64_t row0 = tile * g.rows;
         const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(g.rows) ? p.rows - row0 : g.rows);
         tile_copy(smem, xa, row0, live, g.nvec, g.raw_pitch);
-        if constexpr (RESID) tile_copy(bstage, xb, row0, live, g.nvec, g.raw_pitch);
         cp_async_wait_all();
         __syncthreads();
         if constexpr (RESID) {
@@ -508,12 +503,14 @@ __global__ void __launch_bounds__(TILE_THREADS)
             // sum's dtype; the stored bits replace x in shared memory
             for (int r = 0; r < live; ++r) {
                 uint4 *arow = reinterpret_cast<uint4 *>(smem + r * g.raw_pitch);
-                const unsigned char *brow = bstage + r * g.raw_pitch;
+                const uint4 *brow = xb + (row0 + r) * static_cast<uint64_t>(g.nvec);
                 for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
                     float a[EPV];
                     float b[EPV];
+                    // b is read once, straight from HBM (no staging)
+                    const uint4 bq = __ldcs(brow + v);
                     raw_vector<EB>(reinterpret_cast<const unsigned char *>(arow), v, IN, a);
-                    raw_vector<EB>(brow, v, IN, b);
+                    raw_vector<EB>(reinterpret_cast<const unsigned char *>(&bq), 0, IN, b);
 #pragma unroll
                     for (int t = 0; t < EPV; ++t) a[t] = __fadd_rn(a[t], b[t]);
                     uint4 packed;
@@ -835,7 +832,7 @@ bool aligned16(const void *p)
 // evenly over them.
 Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual, bool bias)
 {
-    Tile g{0, 0, 0, 0, 0, 0, 0, 0, 1};
+    Tile g{0, 0, 0, 0, 0, 0, 0, 1};
     const uint64_t per_vec = 16u / static_cast<uint64_t>(eb);
     if (width == 0 || width % per_vec != 0 || width % 4 != 0 || width > 32768) {
         return g;
@@ -855,7 +852,9 @@ Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual, bool bia
         g.f32_offset = eb != 4 ? rows * g.raw_pitch : 0;
         return g;
     }
-    const size_t areas = residual ? 2u : 1u;
+    // the residual's second operand is read from HBM in the add pass, not staged
+    (void)residual;
+    const size_t areas = 1u;
     const size_t row_bytes = static_cast<size_t>(g.raw_pitch) * areas;
     const size_t params = static_cast<size_t>(width) * 4u * (bias ? 2u : 1u);
     int rows = 0;
@@ -866,7 +865,6 @@ Tile tile_geometry(uint64_t width, int eb, bool softmax, bool residual, bool bia
         rows = 1;
     }
     g.rows = rows;
-    g.b_offset = rows * g.raw_pitch;
     g.param_offset = rows * g.raw_pitch * static_cast<int>(areas);
     return g;
 }
