@@ -510,14 +510,23 @@ m3_status m3_cuda_session_synchronize(m3_session *session, m3_error *error);
 
 /* Device address and byte size of a value's current storage (valid until the
  * next run, write or swap).  For zero-copy interoperation, e.g. handing an
- * output to a collective. */
+ * output to a collective.  A temporary that a fused launch keeps in registers
+ * has no storage (M3_STATUS_INVALID_ARGUMENT): the arena holds only the
+ * slots that launches store or read and those of inputs, outputs and
+ * constants, while m3_session_get_plan_info still reports the reference's
+ * liveness plan. */
 m3_status m3_cuda_session_value_device_pointer(const m3_session *session,
                                                m3_graph_value_id value,
                                                void **device_pointer,
                                                size_t *byte_count,
                                                m3_error *error);
 
-/* Device-to-device input write / output read (no host staging). */
+/* Device-to-device input write / output read (no host staging).  The copy
+ * runs on the session's stream after the runs enqueued there and the call
+ * returns once it is complete.  Work on other streams is not waited for: a
+ * source written on another stream (including the legacy default stream,
+ * which a session-owned non-blocking stream does not wait on) must be
+ * complete, or be ordered before the call with an event, by the caller. */
 m3_status m3_cuda_session_write_input_device(m3_session *session,
                                              m3_graph_value_id value,
                                              const void *device_source,

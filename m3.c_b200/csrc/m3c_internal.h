@@ -141,6 +141,10 @@ typedef struct {
     size_t *producers;
     size_t *last_uses;
     bool *slot_shadowed;           /* slot needs a second (shadow) buffer */
+    bool *slot_needed;             /* slot is stored or read by some launch or
+                                      holds an input, output or constant;
+                                      temporaries fused into registers get no
+                                      memory */
     /* launches */
     m3c_launch *launches;
     size_t launch_count;

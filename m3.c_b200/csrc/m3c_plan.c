@@ -1311,6 +1311,7 @@ void m3c_plan_free(m3c_plan *plan)
     free(plan->producers);
     free(plan->last_uses);
     free(plan->slot_shadowed);
+    free(plan->slot_needed);
     free(plan->launches);
     free(plan->flip_slot);
     free(plan->flip_command);
@@ -1321,6 +1322,64 @@ static size_t align_up(size_t value)
 {
     return (value + M3C_ARENA_ALIGNMENT - 1U) &
            ~(size_t)(M3C_ARENA_ALIGNMENT - 1U);
+}
+
+static void mark_ref(m3c_plan *plan, m3c_ref ref)
+{
+    if (ref.value != UINT32_MAX && ref.value < plan->value_count) {
+        plan->slot_needed[plan->value_slot[ref.value]] = true;
+    }
+}
+
+/* Slots that need memory: every slot holding an input, output or constant
+ * (the host writes or reads them) and every slot a launch reads or stores.
+ * A temporary that lives only in the registers of a fused launch needs
+ * none. */
+static m3_status mark_needed_slots(const m3_graph *graph, m3c_plan *plan,
+                                   m3_error *error)
+{
+    size_t v;
+    size_t l;
+    int k;
+
+    plan->slot_needed = calloc(plan->slot_count ? plan->slot_count : 1U, sizeof(bool));
+    if (plan->slot_needed == NULL) {
+        return m3c_error_set(error, M3_STATUS_OUT_OF_MEMORY,
+                             "cannot allocate slot plan");
+    }
+    for (v = 0U; v < plan->value_count; ++v) {
+        if (graph->values[v].description.role != M3_GRAPH_TEMPORARY) {
+            plan->slot_needed[plan->value_slot[v]] = true;
+        }
+    }
+    for (l = 0U; l < plan->launch_count; ++l) {
+        const m3c_launch *launch = &plan->launches[l];
+
+        if (launch->kind == M3C_LAUNCH_EW) {
+            for (k = 0; k < launch->n_operands; ++k) {
+                mark_ref(plan, launch->operands[k].ref);
+            }
+            for (k = 0; k < launch->n_outputs; ++k) {
+                mark_ref(plan, launch->outputs[k]);
+            }
+            if (launch->has_absmax) {
+                mark_ref(plan, launch->absmax_out);
+            }
+            continue;
+        }
+        mark_ref(plan, launch->row_in);
+        mark_ref(plan, launch->row_out);
+        if (launch->kind == M3C_LAUNCH_SOFTMAX) {
+            mark_ref(plan, launch->row_out2);
+            mark_ref(plan, launch->row_out3);
+        } else {
+            mark_ref(plan, launch->row_in_b);
+            mark_ref(plan, launch->row_sum_out);
+            mark_ref(plan, launch->norm_scale);
+            mark_ref(plan, launch->norm_bias);
+        }
+    }
+    return M3_STATUS_OK;
 }
 
 m3_status m3c_plan_build(const m3_graph *graph, bool fuse_enabled,
@@ -1382,9 +1441,17 @@ m3_status m3c_plan_build(const m3_graph *graph, bool fuse_enabled,
         m3c_plan_free(plan);
         return status;
     }
+    status = mark_needed_slots(graph, plan, error);
+    if (status != M3_STATUS_OK) {
+        m3c_plan_free(plan);
+        return status;
+    }
     plan->arena_bytes = 0U;
     plan->shadow_bytes = 0U;
     for (s = 0U; s < plan->slot_count; ++s) {
+        if (!plan->slot_needed[s]) {
+            continue;
+        }
         plan->arena_bytes += align_up(plan->slot_bytes[s]);
         if (plan->slot_shadowed[s]) {
             plan->shadow_bytes += align_up(plan->slot_bytes[s]);

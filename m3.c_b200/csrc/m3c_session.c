@@ -433,11 +433,15 @@ m3_status m3_cuda_session_create(m3_session **session_output,
     }
     offset = 0U;
     for (slot = 0U; slot < s->plan.slot_count; ++slot) {
+        if (!s->plan.slot_needed[slot]) {
+            s->buffer[0][slot] = NULL;   /* lives in registers only */
+            continue;
+        }
         s->buffer[0][slot] = s->arena + offset;
         offset += align_up(s->plan.slot_bytes[slot]);
     }
     for (slot = 0U; slot < s->plan.slot_count; ++slot) {
-        if (s->plan.slot_shadowed[slot]) {
+        if (s->plan.slot_shadowed[slot] && s->plan.slot_needed[slot]) {
             s->buffer[1][slot] = s->arena + offset;
             offset += align_up(s->plan.slot_bytes[slot]);
         } else {
@@ -1166,6 +1170,11 @@ m3_status m3_cuda_session_value_device_pointer(const m3_session *session,
     if ((size_t)value >= s->plan.value_count) {
         return m3c_error_set(error, M3_STATUS_OUT_OF_RANGE,
                              "value is out of range");
+    }
+    if (!s->plan.slot_needed[s->plan.value_slot[value]]) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "value has no device storage: it lives only in "
+                             "the registers of a fused launch");
     }
     status = settle_quietly(s, error);
     if (status != M3_STATUS_OK) {
