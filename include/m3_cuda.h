@@ -27,9 +27,9 @@
  * after the reference headers when both are used.
  *
  * Operators executed on the GPU: COPY, CAST, ADD, MUL, GATED_SILU, SOFTMAX,
- * TOP_K, RMS_NORM, LAYER_NORM, SNAKE1D, TANH, and the extensions
+ * TOP_K, CATEGORICAL, RMS_NORM, LAYER_NORM, SNAKE1D, TANH, and the extensions
  * M3_OP_ABS_MAX and M3_OP_CLAMP_UNIT.  Other m3.h kinds (contractions,
- * attention, convolutions, embedding, RoPE, categorical) are rejected with
+ * attention, convolutions, embedding, RoPE) are rejected with
  * M3_STATUS_UNSUPPORTED at session creation; there is no CPU fallback inside
  * this library.
  *

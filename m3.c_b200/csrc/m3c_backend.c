@@ -30,7 +30,7 @@ typedef struct {
     m3c_reduce_scratch *reduce;
 } cuda_backend;
 
-static const m3c_status clean = {UINT32_MAX, 0U, 0U, 0U};
+static const m3c_status clean = {UINT32_MAX, 0U, 0U, UINT32_MAX};
 
 static m3_status fail_cuda(m3_error *error, cudaError_t code, const char *what)
 {
@@ -252,6 +252,11 @@ static void to_vcommand(const m3_command *c, m3c_vcommand *v)
         vview_of(c->descriptor.top_k.values, &v->out[0]);
         vview_of(c->descriptor.top_k.indices, &v->out[1]);
         v->k = c->descriptor.top_k.k;
+        break;
+    case M3_OP_CATEGORICAL:
+        vview_of(c->descriptor.categorical.probabilities, &v->in[0]);
+        vview_of(c->descriptor.categorical.uniforms, &v->in[1]);
+        vview_of(c->descriptor.categorical.output, &v->out[0]);
         break;
     case M3_OP_SNAKE1D:
         vview_of(c->descriptor.snake1d.input, &v->in[0]);
@@ -515,6 +520,42 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         }
         return m3c_launch_softmax(&p, b->stream);
     }
+    case M3_OP_CATEGORICAL: {
+        const m3_tensor_view *probabilities = c->descriptor.categorical.probabilities;
+        const m3_tensor_view *uniforms = c->descriptor.categorical.uniforms;
+        m3c_categorical_params p;
+        const void *data;
+
+        if (!m3c_contiguous(&uniforms->metadata, uniforms->byte_strides)) {
+            return -1;  /* strided uniforms are not supported */
+        }
+        code = dense_input(b, probabilities, index, &data, temporary);
+        if (code != 0) {
+            return code;
+        }
+        memset(&p, 0, sizeof(p));
+        p.probabilities = data;
+        p.probabilities_dtype = (int32_t)probabilities->metadata.dtype;
+        p.uniforms = view_base(b, uniforms) + uniforms->byte_offset;
+        p.uniforms_dtype = (int32_t)uniforms->metadata.dtype;
+        p.output = (int32_t *)(view_base(b, c->descriptor.categorical.output) +
+                               c->descriptor.categorical.output->byte_offset);
+        p.width = probabilities->metadata.shape[probabilities->metadata.rank - 1U];
+        p.rows = p.width ? probabilities->metadata.element_count / p.width : 0U;
+        p.status = b->status;
+        p.command = index;
+        /* the checks of every row first, then the draws, which run only
+         * when no row failed: a failing command writes nothing */
+        p.skip_before = index;
+        p.check_only = 1;
+        code = m3c_launch_categorical(&p, b->stream);
+        if (code == 0) {
+            p.skip_before = index + 1U;
+            p.check_only = 0;
+            code = m3c_launch_categorical(&p, b->stream);
+        }
+        return code;
+    }
     case M3_OP_RMS_NORM:
     case M3_OP_LAYER_NORM: {
         bool layer = c->kind == M3_OP_LAYER_NORM;
@@ -563,9 +604,11 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
     }
 }
 
-static const char *check_message(m3_op_kind kind)
+static const char *check_message(m3_op_kind kind, uint32_t detail)
 {
     switch ((int)kind) {
+    case M3_OP_CATEGORICAL:
+        return m3c_categorical_message(detail);
     case M3_OP_SOFTMAX:
         return "softmax input contains NaN";
     case M3_OP_TOP_K:
@@ -643,7 +686,8 @@ m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
             return fail_cuda(error, code, "cannot reset backend status");
         }
         return m3c_error_set(error, M3_STATUS_OUT_OF_RANGE, "%s",
-                             check_message(commands[failing].kind));
+                             check_message(commands[failing].kind,
+                                           b->status_host->detail));
     }
     if (status == M3_STATUS_OK) {
         m3_error_reset(error);

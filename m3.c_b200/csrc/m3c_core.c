@@ -182,3 +182,15 @@ bool m3c_contiguous(const m3_tensor_metadata *metadata,
     }
     return true;
 }
+
+const char *m3c_categorical_message(uint32_t detail)
+{
+    switch (detail & 3U) {
+    case 1U:
+        return "categorical uniform is outside [0,1)";
+    case 2U:
+        return "categorical probability is invalid";
+    default:
+        return "categorical row sum is not positive finite";
+    }
+}

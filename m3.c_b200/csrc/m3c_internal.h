@@ -19,6 +19,9 @@
 
 m3_status m3c_error_set(m3_error *error, m3_status status, const char *format,
                         ...);
+/* The reference's preflight message for a failed categorical check, from the
+ * status detail word (row * 4 + reason; src/m3_op_data_preflight.c:246-265). */
+const char *m3c_categorical_message(uint32_t detail);
 
 /* ------------------------------------------------------------- tensors */
 
@@ -79,7 +82,9 @@ const char *m3c_kind_name(m3_op_kind kind);
 typedef enum {
     M3C_LAUNCH_EW = 0,
     M3C_LAUNCH_SOFTMAX,     /* softmax and/or top-k over the same rows */
-    M3C_LAUNCH_NORM         /* RMSNorm / LayerNorm, optional residual add */
+    M3C_LAUNCH_NORM,        /* RMSNorm / LayerNorm, optional residual add */
+    M3C_LAUNCH_CATEGORICAL  /* categorical sampling: row_in probabilities,
+                               row_in_b uniforms, row_out indices */
 } m3c_launch_kind;
 
 /* A reference to a value's device bytes at run time: slot + byte offset, and

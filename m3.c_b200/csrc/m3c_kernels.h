@@ -114,7 +114,8 @@ typedef struct {
     uint32_t fail_command;  /* UINT32_MAX when clean */
     uint32_t fail_code;
     uint32_t runs_started;
-    uint32_t reserved;
+    uint32_t detail;        /* categorical: smallest row * 4 + reason that
+                               failed (UINT32_MAX when clean) */
 } m3c_status;
 
 /* Reduction scratch of one launch: the running abs-max bit pattern and the
@@ -181,6 +182,25 @@ typedef struct {
     uint32_t skip_before;       /* skip when a command < this failed */
     m3c_status *status;
 } m3c_norm_params;
+
+/* Categorical sampling (reference src/m3_op_execute_sampling.c:90-137 with
+ * the checks of src/m3_op_data_preflight.c:231-268): one index per row. */
+typedef struct {
+    const void *probabilities;  /* dense [rows, width] */
+    int32_t probabilities_dtype;
+    const void *uniforms;       /* dense [rows] */
+    int32_t uniforms_dtype;
+    int32_t *output;            /* [rows] I32 */
+    uint64_t rows;
+    uint64_t width;
+    m3c_status *status;
+    uint32_t command;
+    uint32_t skip_before;
+    int32_t first_of_run;
+    int32_t check_only;         /* 1: record failures, write nothing */
+} m3c_categorical_params;
+
+int m3c_launch_categorical(const m3c_categorical_params *params, void *stream);
 
 /* The kernel and grid m3c_launch_ew would use, chosen once (sessions keep it
  * per launch so repeated runs skip the program search), and the launch with

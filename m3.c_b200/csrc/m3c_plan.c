@@ -372,6 +372,7 @@ static bool has_data_check(const m3_graph *graph,
     switch ((int)node->kind) {
     case M3_OP_SOFTMAX:
     case M3_OP_TOP_K:
+    case M3_OP_CATEGORICAL:
     case (int)M3_OP_ABS_MAX:
         return true;
     case M3_OP_CAST:
@@ -1114,6 +1115,36 @@ static m3_status plan_softmax(planner *p, size_t n, size_t count,
     return status;
 }
 
+/* Row launch for categorical sampling; its output is checked (written to
+ * the shadow buffer and committed only when the run is clean). */
+static m3_status plan_categorical(planner *p, size_t n, m3_error *error)
+{
+    const m3_graph_node_desc *node = &p->graph->nodes[n];
+    m3c_launch launch;
+    m3_status status;
+
+    memset(&launch, 0, sizeof(launch));
+    launch.kind = M3C_LAUNCH_CATEGORICAL;
+    launch.first_node = n;
+    launch.node_count = 1U;
+    launch.row_in = read_ref(p, node->inputs[0]);
+    launch.row_in_b = read_ref(p, node->inputs[1]);
+    launch.row_sum_out.value = NO_VALUE;
+    launch.row_out2.value = NO_VALUE;
+    launch.row_out3.value = NO_VALUE;
+    launch.norm_scale.value = NO_VALUE;
+    launch.norm_bias.value = NO_VALUE;
+    launch.command_a = (uint32_t)n;
+    launch.command_b = UINT32_MAX;
+    status = write_ref(p, node->outputs[0], true, (uint32_t)n, &launch.row_out,
+                       error);
+    (void)snprintf(launch.text, sizeof(launch.text), "row[CATEGORICAL]");
+    if (status == M3_STATUS_OK) {
+        status = push_launch(p, &launch, error);
+    }
+    return status;
+}
+
 /* Row launch for a norm; `residual` is the index of an ADD node whose output
  * is the norm input and that runs as the kernel's prologue (or SIZE_MAX). */
 static m3_status plan_norm(planner *p, size_t n, size_t residual,
@@ -1274,6 +1305,11 @@ static m3_status fuse(planner *p, bool fuse_enabled, m3_error *error)
         if (status != M3_STATUS_OK) {
             break;
         }
+        if (node->kind == M3_OP_CATEGORICAL) {
+            status = plan_categorical(p, n, error);
+            ++n;
+            continue;
+        }
         if (node->kind == M3_OP_SOFTMAX || node->kind == M3_OP_TOP_K) {
             size_t count = 1U;
 
@@ -1369,7 +1405,9 @@ static m3_status mark_needed_slots(const m3_graph *graph, m3c_plan *plan,
         }
         mark_ref(plan, launch->row_in);
         mark_ref(plan, launch->row_out);
-        if (launch->kind == M3C_LAUNCH_SOFTMAX) {
+        if (launch->kind == M3C_LAUNCH_CATEGORICAL) {
+            mark_ref(plan, launch->row_in_b);
+        } else if (launch->kind == M3C_LAUNCH_SOFTMAX) {
             mark_ref(plan, launch->row_out2);
             mark_ref(plan, launch->row_out3);
         } else {

@@ -104,7 +104,7 @@ struct m3_session {
     host_pipe pipe;
 };
 
-static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, 0U};
+static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, UINT32_MAX};
 
 /* ------------------------------------------------------------ helpers */
 
@@ -543,6 +543,24 @@ static int launch_one(m3_session *s, size_t index, bool first)
         }
         return m3c_launch_ew_chosen(&s->ew_choices[index], &p, s->stream);
     }
+    if (l->kind == M3C_LAUNCH_CATEGORICAL) {
+        const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
+        m3c_categorical_params p;
+
+        memset(&p, 0, sizeof(p));
+        p.probabilities = ref_pointer(s, l->row_in);
+        p.probabilities_dtype = (int32_t)in->dtype;
+        p.uniforms = ref_pointer(s, l->row_in_b);
+        p.uniforms_dtype = (int32_t)s->metadata[l->row_in_b.value].dtype;
+        p.output = (int32_t *)ref_pointer(s, l->row_out);
+        p.width = in->shape[in->rank - 1U];
+        p.rows = p.width ? in->element_count / p.width : 0U;
+        p.status = s->status_device;
+        p.command = l->command_a;
+        p.skip_before = (uint32_t)l->first_node;
+        p.first_of_run = first ? 1 : 0;
+        return m3c_launch_categorical(&p, s->stream);
+    }
     if (l->kind == M3C_LAUNCH_SOFTMAX) {
         const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
         m3c_softmax_params p;
@@ -828,12 +846,15 @@ m3_status m3_cuda_session_run_async(m3_session *s, m3_error *error)
 
 /* The reference's data-check messages (src/m3_op_data_preflight.c:23,
  * :283-291). */
-static const char *failure_message(const m3_session *s, uint32_t command)
+static const char *failure_message(const m3_session *s, uint32_t command,
+                                   uint32_t detail)
 {
     if (command >= s->plan.node_count) {
         return "data check failed";
     }
     switch ((int)s->node_kinds[command]) {
+    case M3_OP_CATEGORICAL:
+        return m3c_categorical_message(detail);
     case M3_OP_SOFTMAX:
         return "softmax input contains NaN";
     case M3_OP_TOP_K:
@@ -896,7 +917,8 @@ static m3_status settle(m3_session *s, m3_error *error)
             ++run;
         }
         status = m3c_error_set(error, M3_STATUS_OUT_OF_RANGE, "%s",
-                               failure_message(s, seen.fail_command));
+                               failure_message(s, seen.fail_command,
+                                               seen.detail));
         code = cudaMemcpyAsync(s->status_device, &clean_status,
                                sizeof(clean_status), cudaMemcpyHostToDevice,
                                s->stream);

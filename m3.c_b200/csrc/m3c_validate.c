@@ -453,6 +453,53 @@ static m3_status validate_top_k(const m3c_vcommand *c, m3_error *error)
     return status;
 }
 
+/* src/m3_op_validate_sampling.c:77-131 */
+static m3_status validate_categorical(const m3c_vcommand *c, m3_error *error)
+{
+    const m3_tensor_metadata *probabilities;
+    const m3_tensor_metadata *uniforms;
+    const m3_tensor_metadata *output;
+    uint8_t rank;
+    uint8_t axis;
+    bool shape_ok;
+    m3_status status = check_view(&c->in[0], false, "categorical probabilities",
+                                  error);
+
+    if (status == M3_STATUS_OK) {
+        status = check_view(&c->in[1], false, "categorical uniforms", error);
+    }
+    if (status == M3_STATUS_OK) {
+        status = check_view(&c->out[0], true, "categorical output", error);
+    }
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    probabilities = c->in[0].metadata;
+    uniforms = c->in[1].metadata;
+    output = c->out[0].metadata;
+    rank = probabilities->rank;
+    shape_ok = rank != 0U && probabilities->shape[rank - 1U] != 0U &&
+               probabilities->shape[rank - 1U] <= (uint64_t)INT32_MAX &&
+               uniforms->rank + 1U == rank && output->rank + 1U == rank &&
+               m3c_shape_equal(uniforms, output);
+    for (axis = 0U; shape_ok && axis + 1U < rank; ++axis) {
+        shape_ok = uniforms->shape[axis] == probabilities->shape[axis];
+    }
+    if (!m3c_dtype_float(probabilities->dtype) ||
+        !m3c_dtype_float(uniforms->dtype) || output->dtype != M3_DTYPE_I32 ||
+        !shape_ok) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "categorical dtype or shape is invalid");
+    }
+    status = check_alias(&c->out[0], &c->in[0], false,
+                         "categorical probabilities", error);
+    if (status == M3_STATUS_OK) {
+        status = check_alias(&c->out[0], &c->in[1], false,
+                             "categorical uniforms", error);
+    }
+    return status;
+}
+
 /* Extension: abs-max of any float tensor into one F32 element. */
 static m3_status validate_abs_max(const m3c_vcommand *c, m3_error *error)
 {
@@ -501,6 +548,7 @@ bool m3c_kind_supported(m3_op_kind kind)
     case M3_OP_GATED_SILU:
     case M3_OP_SOFTMAX:
     case M3_OP_TOP_K:
+    case M3_OP_CATEGORICAL:
     case M3_OP_RMS_NORM:
     case M3_OP_LAYER_NORM:
     case M3_OP_SNAKE1D:
@@ -523,6 +571,7 @@ const char *m3c_kind_name(m3_op_kind kind)
     case M3_OP_GATED_SILU: return "GATED_SILU";
     case M3_OP_SOFTMAX: return "SOFTMAX";
     case M3_OP_TOP_K: return "TOP_K";
+    case M3_OP_CATEGORICAL: return "CATEGORICAL";
     case M3_OP_RMS_NORM: return "RMS_NORM";
     case M3_OP_LAYER_NORM: return "LAYER_NORM";
     case M3_OP_SNAKE1D: return "SNAKE1D";
@@ -568,6 +617,9 @@ m3_status m3c_validate(const m3c_vcommand *command, m3_error *error)
         break;
     case M3_OP_TOP_K:
         status = validate_top_k(command, error);
+        break;
+    case M3_OP_CATEGORICAL:
+        status = validate_categorical(command, error);
         break;
     case (int)M3_OP_ABS_MAX:
         status = validate_abs_max(command, error);

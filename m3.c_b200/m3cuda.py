@@ -158,6 +158,10 @@ class _Snake(ctypes.Structure):
     _fields_ = [("input", _VP), ("alpha", _VP), ("output", _VP)]
 
 
+class _Categorical(ctypes.Structure):
+    _fields_ = [("probabilities", _VP), ("uniforms", _VP), ("output", _VP)]
+
+
 class _ConvTranspose(ctypes.Structure):
     # the largest member of the reference union (src/m3_op.h:105-116)
     _fields_ = [("input", _VP), ("weight", _VP), ("bias", _VP),
@@ -172,6 +176,7 @@ class _Descriptor(ctypes.Union):
                 ("layer_norm", _LayerNorm), ("gated_silu", _Binary),
                 ("softmax", _Unary), ("top_k", _TopKCommand),
                 ("snake1d", _Snake), ("tanh", _Unary),
+                ("categorical", _Categorical),
                 ("conv_transpose1d", _ConvTranspose)]
 
 
@@ -446,6 +451,8 @@ class Graph:
             return first[:-1] + (k,)
         if kind == OPS["ABS_MAX"]:
             return (1,)
+        if kind == OPS["CATEGORICAL"]:
+            return first[:-1]
         return first
 
     def inferred(self, kind: str | int, inputs: Iterable[int], role: int,
@@ -465,6 +472,8 @@ class Graph:
             dtype = self.values[inputs[0]][0]
         elif code == OPS["TOP_K"]:
             dtype = F32 if output_index == 0 else I32
+        elif code == OPS["CATEGORICAL"]:
+            dtype = I32
         self.values.append((dtype, self._shape_of(code, inputs,
                                                   params.get("k")), role))
         return out.value

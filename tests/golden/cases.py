@@ -1,4 +1,5 @@
-"""Golden cases: small graphs of every reference operator on the path, with
+"""Golden cases: small graphs of every reference operator on the path (and
+categorical sampling), with
 seeded inputs (test infrastructure).
 
 Each case is (builder, inputs, checks): `builder(m3, g)` adds the graph to
@@ -216,6 +217,32 @@ def casts():
     return build, inputs, ["bits", "bits", "bits", "bits"]
 
 
+def categorical(dt):
+    """Categorical sampling: rows with zeros, a single positive entry, a zero
+    uniform and the largest uniform below one."""
+    rows, vocab = 12, 257
+
+    def build(m3, g):
+        d = getattr(m3, dt)
+        p = g.value(m3.INPUT, d, (rows, vocab))
+        u = g.value(m3.INPUT, d, (rows,))
+        i = g.inferred("CATEGORICAL", [p, u], m3.OUTPUT, m3.I32)
+        g.node("CATEGORICAL", [p, u], [i])
+        return {"p": p, "u": u}, [i]
+
+    def inputs(m3, oracle):
+        r = np.random.default_rng(108)
+        p = r.random((rows, vocab)).astype(np.float32)
+        p[r.random((rows, vocab)) < 0.4] = 0.0
+        p[3] = 0.0
+        p[3, 100] = 0.5
+        u = r.random(rows).astype(np.float32)
+        u[0] = 0.0
+        u[1] = np.nextafter(np.float32(1.0), np.float32(0.0)) if dt == "F32" else np.float32(0.99609375)
+        return {"p": _enc(oracle, dt, p), "u": _enc(oracle, dt, u)}
+    return build, inputs, ["bits"]
+
+
 CASES = {
     "broadcast_mul_add_f32": broadcast_mul_add("F32"),
     "broadcast_mul_add_f16": broadcast_mul_add("F16"),
@@ -233,4 +260,6 @@ CASES = {
     "cfg_euler_bf16": cfg_euler_bf16(),
     "snake_tanh": snake_tanh(),
     "casts": casts(),
+    "categorical_f32": categorical("F32"),
+    "categorical_f16": categorical("F16"),
 }

@@ -833,3 +833,127 @@ def test_flow_overlap_blend_through_backend_commands(m3, gpu):
         assert np.array_equal(bits(got), bits(expect))
     finally:
         be.close()
+
+
+# ------------------------------------------------------ categorical sampling
+
+
+def _categorical_inputs(dtype_name, oracle, rows=37, vocab=1000, seed=41):
+    rng = np.random.default_rng(seed)
+    probs = rng.random((rows, vocab)).astype(np.float32)
+    probs[rng.random((rows, vocab)) < 0.3] = 0.0
+    probs[4] = 0.0
+    probs[4, 17] = 0.25                      # one positive entry
+    probs[6, -1] = 0.0                       # last positive is not the last
+    uniforms = rng.random(rows).astype(np.float32)
+    uniforms[0] = 0.0
+    uniforms[1] = (np.nextafter(np.float32(1.0), np.float32(0.0)) if dtype_name == "F32"
+                   else np.float32(0.99609375))  # largest below one in the dtype
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype_name]
+    return enc(probs), enc(uniforms)
+
+
+def _categorical_graph(m3, g, dt, rows, vocab):
+    p = g.value(m3.INPUT, dt, (rows, vocab))
+    u = g.value(m3.INPUT, dt, (rows,))
+    i = g.inferred("CATEGORICAL", [p, u], m3.OUTPUT, m3.I32)
+    g.node("CATEGORICAL", [p, u], [i])
+    return {"p": p, "u": u}, [i]
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+def test_categorical_matches_reference(m3, ref, oracle, gpu, dtype):
+    """Categorical sampling (src/m3_op_execute_sampling.c:90-137): the same
+    index as the reference CPU provider for every row, including a zero
+    uniform, the largest uniform below one and rows with few positives."""
+    probs, uniforms = _categorical_inputs(dtype, oracle)
+    dt = getattr(m3, dtype)
+    (mine,), (theirs,) = run_both(
+        m3, ref, lambda g: _categorical_graph(m3, g, dt, *probs.shape),
+        {"p": probs, "u": uniforms})
+    assert np.array_equal(mine, theirs)
+
+
+def test_categorical_checks_match_reference(m3, ref, oracle, gpu):
+    """Each failing check fails the run with the reference's message, picks
+    the failure of the earliest row, and leaves the output untouched."""
+    probs, uniforms = _categorical_inputs("F32", oracle)
+    rows, vocab = probs.shape
+    g = m3.Graph()
+    handles, (out,) = _categorical_graph(m3, g, m3.F32, rows, vocab)
+    s = m3.Session(g)
+    s.write(handles["p"], probs)
+    s.write(handles["u"], uniforms)
+    s.run()
+    good = s.read(out).copy()
+    rg = m3.Graph(lib=ref)
+    rhandles, _ = _categorical_graph(m3, rg, m3.F32, rows, vocab)
+    rs = m3.Session(rg, allow_metal=False, allow_neural_engine=False, cuda=False)
+
+    def poison(kind):
+        p, u = probs.copy(), uniforms.copy()
+        if kind == "uniform":
+            u[9] = 1.0
+        elif kind == "probability":
+            p[5, 7] = -1.0
+        elif kind == "nan":
+            p[8, 3] = np.nan
+        elif kind == "sum":
+            p[2] = 0.0
+        elif kind == "order":          # a probability failure in an earlier
+            p[3, 1] = np.inf           # row than a uniform failure
+            u[11] = -0.5
+        return p, u
+
+    for kind in ("uniform", "probability", "nan", "sum", "order"):
+        p, u = poison(kind)
+        for session, hs in ((s, handles), (rs, rhandles)):
+            session.write(hs["p"], p)
+            session.write(hs["u"], u)
+        status, message = s.run_status()
+        ref_status, ref_message = rs.run_status()
+        assert status == ref_status == m3.OUT_OF_RANGE, kind
+        assert message == ref_message, kind
+        assert np.array_equal(s.read(out), good), kind
+
+
+def test_categorical_through_backend_commands(m3, oracle, gpu):
+    """The plug-in path: checks first, then the draws; a failing command
+    writes nothing."""
+    probs, uniforms = _categorical_inputs("F32", oracle, rows=9, vocab=64, seed=5)
+    g = m3.Graph(lib=m3.load())
+    handles, (out,) = _categorical_graph(m3, g, m3.F32, *probs.shape)
+    s = m3.Session(g)
+    s.write(handles["p"], probs)
+    s.write(handles["u"], uniforms)
+    s.run()
+    expected = s.read(out).copy()
+    be = _Backend(m3)
+    try:
+        k_p = be.tensor(probs)
+        k_u = be.tensor(uniforms)
+        k_o = be.tensor(np.full(9, -3, np.int32).view(np.float32))
+        cmd = (m3.Command * 1)()
+        pv = be.view(k_p, probs.shape)
+        uv = be.view(k_u, (9,))
+        ov = be.view(k_o, (9,), dtype=m3.I32)
+        cmd[0].kind = m3.OPS["CATEGORICAL"]
+        cmd[0].descriptor.categorical.probabilities = be.ctypes.pointer(pv)
+        cmd[0].descriptor.categorical.uniforms = be.ctypes.pointer(uv)
+        cmd[0].descriptor.categorical.output = be.ctypes.pointer(ov)
+        status = be.lib.m3_cuda_backend_execute(be.context, cmd, 1, None, be.ctypes.byref(be.err))
+        assert status == m3.OK
+        assert np.array_equal(be.read(k_o, 9).view(np.int32), expected)
+        bad = uniforms.copy()
+        bad[4] = 2.0
+        be.lib.m3_cuda_backend_write(be.context, be.storages[k_u], 0, bad.ctypes.data, bad.nbytes,
+                                     be.ctypes.byref(be.err))
+        sentinel = np.full(9, -3, np.int32)
+        be.lib.m3_cuda_backend_write(be.context, be.storages[k_o], 0, sentinel.ctypes.data, 36,
+                                     be.ctypes.byref(be.err))
+        status = be.lib.m3_cuda_backend_execute(be.context, cmd, 1, None, be.ctypes.byref(be.err))
+        assert status == m3.OUT_OF_RANGE
+        assert be.err.message.decode() == "categorical uniform is outside [0,1)"
+        assert np.array_equal(be.read(k_o, 9).view(np.int32), sentinel)
+    finally:
+        be.close()

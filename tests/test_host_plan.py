@@ -278,3 +278,25 @@ def test_host_rng_matches_reference(m3, ref):
             uniform.append(value.value)
         mine = m3.fill_uniform(seed, sequence, 0.0, 1.0, 257)
         assert np.array_equal(mine, np.array(uniform, np.float32))
+
+
+def test_categorical_plans_as_checked_row_launch(m3):
+    """CATEGORICAL (src/m3_op_execute_sampling.c:90-137) is a row launch whose
+    I32 output is committed only by a clean run (a shadow buffer); shapes
+    and dtypes follow the reference's rules."""
+    g = m3.Graph()
+    p = g.value(m3.INPUT, m3.F32, (4, 100))
+    u = g.value(m3.INPUT, m3.F32, (4,))
+    i = g.inferred("CATEGORICAL", [p, u], m3.OUTPUT, m3.I32)
+    g.node("CATEGORICAL", [p, u], [i])
+    info, report, text = m3.graph_plan(g)
+    assert text == "row[CATEGORICAL]"
+    assert report.launch_count == 1 and report.shadow_bytes == 256
+    bad = m3.Graph()
+    p = bad.value(m3.INPUT, m3.F32, (4, 100))
+    u = bad.value(m3.INPUT, m3.F32, (5,))
+    o = bad.value(m3.OUTPUT, m3.I32, (5,))
+    bad.node("CATEGORICAL", [p, u], [o])
+    with pytest.raises(m3.M3Failure) as failure:
+        m3.graph_plan(bad)
+    assert failure.value.message == "categorical dtype or shape is invalid"
