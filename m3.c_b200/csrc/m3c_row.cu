@@ -302,7 +302,7 @@ __device__ __noinline__ float ieee_div(float a, float b) { return __fdiv_rn(a, b
 // the reference's left-to-right sums on the lanes of warp 0, one row each;
 // then the probabilities, e / sum, with Markstein's refinement of the
 // correctly rounded reciprocal.
-template <int IN, int OUT>
+template <int IN, int OUT, int VPL>
 __global__ void __launch_bounds__(TILE_THREADS, 6)
     softmax_tile_kernel(const __grid_constant__ m3c_softmax_params p, Tile g)
 {
@@ -319,26 +319,35 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
     float *ebuf = reinterpret_cast<float *>(smem + g.f32_offset);
     const float pos_inf = __int_as_float(0x7f800000);
     const uint32_t first_command = p.softmax_command < p.topk_command ? p.softmax_command : p.topk_command;
-    const uint64_t tiles = (p.rows + g.rows - 1) / g.rows;
-    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(OUT);
-    const int r = warp / g.group;      // this warp's row in the tile
-    const int sub = warp % g.group;    // and its place in the row's group
-    const int stride = g.group * WARP;
+    // VPL > 0: the width is a compile-time constant (VPL 16-byte vectors per
+    // lane, one warp per row, 8-row tiles), so every loop below has a fixed
+    // trip count and every shared-memory address a constant offset
+    const int group = VPL > 0 ? 1 : g.group;
+    const int nvec = VPL > 0 ? VPL * WARP : g.nvec;
+    const int width = nvec * EPV;
+    const int raw_pitch = width * EB + 16;
+    const int f32_pitch = width + 4;
+    const int tile_rows = VPL > 0 ? TILE_WARPS : g.rows;
+    const uint64_t tiles = (p.rows + tile_rows - 1) / tile_rows;
+    const uint64_t out_pitch = static_cast<uint64_t>(width) * bytes_of(OUT);
+    const int r = warp / group;      // this warp's row in the tile
+    const int sub = warp % group;    // and its place in the row's group
+    const int stride = group * WARP;
     for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        const uint64_t row0 = tile * g.rows;
-        const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(g.rows) ? p.rows - row0 : g.rows);
-        tile_copy(smem, in, row0, live, g.nvec, g.raw_pitch);
+        const uint64_t row0 = tile * tile_rows;
+        const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(tile_rows) ? p.rows - row0 : tile_rows);
+        tile_copy(smem, in, row0, live, nvec, raw_pitch);
         cp_async_wait_all();
         __syncthreads();
 
         // maximum, its first index and NaN, for the warp's share of its row
         const bool active = r < live;
-        const unsigned char *raw = smem + r * g.raw_pitch;
+        const unsigned char *raw = smem + r * raw_pitch;
         float best = -pos_inf;
         uint32_t best_i = 0xffffffffu;
         bool nan = false;
         if (active) {
-            for (int v = sub * WARP + lane; v < g.nvec; v += stride) {
+            for (int v = sub * WARP + lane; v < nvec; v += stride) {
                 float x[EPV];
                 raw_vector<EB>(raw, v, IN, x);
 #pragma unroll
@@ -352,15 +361,15 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
         }
         warp_best(best, best_i);
         nan = __any_sync(0xffffffffu, nan);
-        if (g.group > 1) {
+        if (group > 1) {
             if (lane == 0) {
                 st.part_max[warp] = best;
                 st.part_index[warp] = best_i;
                 st.part_nan[warp] = nan ? 1 : 0;
             }
             __syncthreads();
-            for (int s = 0; s < g.group; ++s) {
-                const int w = r * g.group + s;
+            for (int s = 0; s < group; ++s) {
+                const int w = r * group + s;
                 if (precedes(st.part_max[w], st.part_index[w], best, best_i)) {
                     best = st.part_max[w];
                     best_i = st.part_index[w];
@@ -386,7 +395,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
                         return EB == 4 ? reinterpret_cast<const float *>(raw)[j]
                                        : widen(IN, reinterpret_cast<const uint16_t *>(raw)[j]);
                     },
-                    static_cast<uint64_t>(g.width), p.k, best, best_i, p.top_values + row * p.k,
+                    static_cast<uint64_t>(width), p.k, best, best_i, p.top_values + row * p.k,
                     p.top_indices + row * p.k, lane);
             }
         }
@@ -394,13 +403,13 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
             if (p.k > 1 && p.top_values != nullptr) {
                 __syncthreads();  // the top-k passes read rows the exponentials overwrite
             }
-            float *erow = ebuf + r * g.f32_pitch;
+            float *erow = ebuf + r * f32_pitch;
             if (active && (best == -pos_inf || best == pos_inf)) {
                 // src/m3_op_execute_basic.c:165-170: final probabilities now,
                 // by the first warp of the row's group
                 if (sub == 0) {
                     uint32_t infinities = 0u;
-                    for (int v = lane; v < g.nvec; v += WARP) {
+                    for (int v = lane; v < nvec; v += WARP) {
                         float x[EPV];
                         raw_vector<EB>(raw, v, IN, x);
 #pragma unroll
@@ -412,7 +421,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
                     }
                     const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
                     __syncwarp();
-                    for (int v = lane; v < g.nvec; v += WARP) {
+                    for (int v = lane; v < nvec; v += WARP) {
                         float x[EPV];
                         raw_vector<EB>(raw, v, IN, x);
 #pragma unroll
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
                 }
             } else if (active) {
                 // each lane overwrites only the vector it has just read
-                for (int v = sub * WARP + lane; v < g.nvec; v += stride) {
+                for (int v = sub * WARP + lane; v < nvec; v += stride) {
                     float x[EPV];
                     raw_vector<EB>(raw, v, IN, x);
 #pragma unroll
@@ -435,16 +444,16 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
             __syncthreads();
             // the reference's left-to-right sums, one row per lane of warp 0
             if (threadIdx.x < static_cast<unsigned>(live) && !st.special[threadIdx.x]) {
-                const float sum = ordered_sum_f32(ebuf + threadIdx.x * g.f32_pitch, g.width);
+                const float sum = ordered_sum_f32(ebuf + threadIdx.x * f32_pitch, width);
                 st.sum[threadIdx.x] = sum;
                 st.reciprocal[threadIdx.x] = __frcp_rn(sum);
             }
             __syncthreads();
             // probabilities expf(x - max) / sum (src/m3_op_execute_basic.c:171-178)
             unsigned char *out = static_cast<unsigned char *>(p.probs) + row0 * out_pitch;
-            const int per_row = g.width / 4;
+            const int per_row = width / 4;
             for (int rr = 0; rr < live; ++rr) {
-                const float4 *e4 = reinterpret_cast<const float4 *>(ebuf + rr * g.f32_pitch);
+                const float4 *e4 = reinterpret_cast<const float4 *>(ebuf + rr * f32_pitch);
                 const bool special = st.special[rr] != 0;
                 const float sum = st.sum[rr];
                 const float y = st.reciprocal[rr];
@@ -903,7 +912,16 @@ int launch_tile(Kernel kernel, const Params &params, const Tile &g, size_t smem,
 template <int IN, int OUT>
 int softmax_tile(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
 {
-    return launch_tile(softmax_tile_kernel<IN, OUT>, p, g, smem, p.rows, stream);
+    // widths with a compiled geometry (8-row tiles, one warp per row)
+    if (IN == M3C_F32 && g.rows == TILE_WARPS && g.group == 1 && p.k <= 1) {
+        if (g.width == 1024) {
+            return launch_tile(softmax_tile_kernel<IN, OUT, 8>, p, g, smem, p.rows, stream);
+        }
+        if (g.width == 512) {
+            return launch_tile(softmax_tile_kernel<IN, OUT, 4>, p, g, smem, p.rows, stream);
+        }
+    }
+    return launch_tile(softmax_tile_kernel<IN, OUT, 0>, p, g, smem, p.rows, stream);
 }
 
 template <int IN>

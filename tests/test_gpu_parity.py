@@ -957,3 +957,47 @@ def test_categorical_through_backend_commands(m3, oracle, gpu):
         assert np.array_equal(be.read(k_o, 9).view(np.int32), sentinel)
     finally:
         be.close()
+
+
+def test_waveform_assembly_through_backend_commands(m3, gpu):
+    """Waveform assembly's per-channel crop-and-clamp copy
+    (src/m3_waveform.c:360-450) as CLAMP_UNIT commands on views: two decoded
+    chunks of a stereo signal, each cropped and written at its place in the
+    planar output.  Values beyond +-1 become +-1; NaN payloads, signed zeros
+    and subnormals are copied bit for bit."""
+    rng = np.random.default_rng(61)
+    chunks = [(rng.standard_normal((2, 100)) * 1.5).astype(np.float32) for _ in range(2)]
+    chunks[0][0, 12] = np.float32(-0.0)
+    chunks[0][1, 20] = np.uint32(0x7FC01234).view(np.float32)
+    chunks[1][0, 30] = np.float32(1e-42)
+    crops = [(10, 60), (5, 70)]          # (crop start, copy count) per chunk
+    total = sum(count for _, count in crops)
+    be = _Backend(m3)
+    try:
+        keys = [be.tensor(c) for c in chunks]
+        k_out = be.tensor(np.zeros((1, 2, total), np.float32))
+        commands = []
+        written = 0
+        for key, (start, count) in zip(keys, crops):
+            for ch in range(2):
+                src = be.view(key, (count,), offset=(ch * 100 + start) * 4)
+                dst = be.view(k_out, (count,), offset=(ch * total + written) * 4)
+                commands.append(("CLAMP_UNIT", src, dst))
+            written += count
+        cmd = (m3.Command * len(commands))()
+        for k, (kind, src, dst) in enumerate(commands):
+            cmd[k].kind = m3.OPS[kind]
+            cmd[k].descriptor.copy.input = be.ctypes.pointer(src)
+            cmd[k].descriptor.copy.output = be.ctypes.pointer(dst)
+        status = be.lib.m3_cuda_backend_execute(be.context, cmd, len(commands), None,
+                                                be.ctypes.byref(be.err))
+        assert status == m3.OK
+        got = be.read(k_out, 2 * total).reshape(2, total)
+        want = np.concatenate([c[:, s:s + n] for c, (s, n) in zip(chunks, crops)], axis=1)
+        w = want.view(np.uint32).copy()
+        mag = w & 0x7FFFFFFF
+        beyond = (mag > 0x3F800000) & (mag <= 0x7F800000)
+        w[beyond] = (w[beyond] & 0x80000000) | 0x3F800000
+        assert np.array_equal(got.view(np.uint32), w)
+    finally:
+        be.close()
