@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
 
 // RMSNorm / LayerNorm with an optional residual-add prologue (RESID: the
 // input is round_in(x + b), optionally stored to sum_out).
-template <int IN, int OUT, bool RESID>
+template <int IN, int OUT, bool RESID, int NVEC>
 __global__ void __launch_bounds__(TILE_THREADS)
     norm_tile_kernel(const __grid_constant__ m3c_norm_params p, Tile g)
 {
@@ -498,22 +498,27 @@ __global__ void __launch_bounds__(TILE_THREADS)
         scale[j] = load_elem(p.scale, p.scale_dtype, j);
         if (p.bias != nullptr) bias[j] = load_elem(p.bias, p.bias_dtype, j);
     }
+    // NVEC > 0: the row length in 16-byte vectors is a compile-time constant
+    // (fixed trip counts, constant shared-memory offsets)
+    const int nvec = NVEC > 0 ? NVEC : g.nvec;
+    const int width = nvec * EPV;
+    const int raw_pitch = width * EB + 16;
     const uint64_t tiles = (p.rows + g.rows - 1) / g.rows;
-    const float channels = __int2float_rn(g.width);
-    const uint64_t out_pitch = static_cast<uint64_t>(g.width) * bytes_of(OUT);
+    const float channels = __int2float_rn(width);
+    const uint64_t out_pitch = static_cast<uint64_t>(width) * bytes_of(OUT);
     for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint64_t row0 = tile * g.rows;
         const int live = static_cast<int>(p.rows - row0 < static_cast<uint64_t>(g.rows) ? p.rows - row0 : g.rows);
-        tile_copy(smem, xa, row0, live, g.nvec, g.raw_pitch);
+        tile_copy(smem, xa, row0, live, nvec, raw_pitch);
         cp_async_wait_all();
         __syncthreads();
         if constexpr (RESID) {
             // src/m3_op_execute_basic.c:61-77: one F32 add, stored in the
             // sum's dtype; the stored bits replace x in shared memory
             for (int r = 0; r < live; ++r) {
-                uint4 *arow = reinterpret_cast<uint4 *>(smem + r * g.raw_pitch);
-                const uint4 *brow = xb + (row0 + r) * static_cast<uint64_t>(g.nvec);
-                for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
+                uint4 *arow = reinterpret_cast<uint4 *>(smem + r * raw_pitch);
+                const uint4 *brow = xb + (row0 + r) * static_cast<uint64_t>(nvec);
+                for (int v = static_cast<int>(threadIdx.x); v < nvec; v += TILE_THREADS) {
                     float a[EPV];
                     float b[EPV];
                     // b is read once, straight from HBM (no staging)
@@ -532,7 +537,7 @@ __global__ void __launch_bounds__(TILE_THREADS)
                     }
                     arow[v] = packed;
                     if (sum_out != nullptr) {
-                        __stcs(sum_out + (row0 + r) * static_cast<uint64_t>(g.nvec) + v, packed);
+                        __stcs(sum_out + (row0 + r) * static_cast<uint64_t>(nvec) + v, packed);
                     }
                 }
             }
@@ -541,16 +546,16 @@ __global__ void __launch_bounds__(TILE_THREADS)
         // ordered sums, one row per lane of warp 0
         if (threadIdx.x < static_cast<unsigned>(live)) {
             const int r = static_cast<int>(threadIdx.x);
-            const unsigned char *row = smem + r * g.raw_pitch;
+            const unsigned char *row = smem + r * raw_pitch;
             if (p.layer_norm) {
                 // src/m3_op_execute_dense.c:175-194
-                const float mean = __fdiv_rn(ordered_raw<EB, 0>(row, g.nvec, IN, 0.0f), channels);
-                const float centred = ordered_raw<EB, 2>(row, g.nvec, IN, mean);
+                const float mean = __fdiv_rn(ordered_raw<EB, 0>(row, nvec, IN, 0.0f), channels);
+                const float centred = ordered_raw<EB, 2>(row, nvec, IN, mean);
                 st.mean[r] = mean;
                 st.sum[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(centred, channels), p.epsilon)));
             } else {
                 // src/m3_op_execute_dense.c:128-141
-                const float squares = ordered_raw<EB, 1>(row, g.nvec, IN, 0.0f);
+                const float squares = ordered_raw<EB, 1>(row, nvec, IN, 0.0f);
                 st.mean[r] = 0.0f;
                 st.sum[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(squares, channels), p.epsilon)));
             }
@@ -561,8 +566,8 @@ __global__ void __launch_bounds__(TILE_THREADS)
         for (int r = 0; r < live; ++r) {
             const float inverse = st.sum[r];
             const float mean = st.mean[r];
-            const unsigned char *row = smem + r * g.raw_pitch;
-            for (int v = static_cast<int>(threadIdx.x); v < g.nvec; v += TILE_THREADS) {
+            const unsigned char *row = smem + r * raw_pitch;
+            for (int v = static_cast<int>(threadIdx.x); v < nvec; v += TILE_THREADS) {
                 float x[EPV];
                 float y[EPV];
                 raw_vector<EB>(row, v, IN, x);
@@ -946,8 +951,15 @@ int softmax_tile_dispatch(const m3c_softmax_params &p, const Tile &g, size_t sme
 template <int IN, int OUT>
 int norm_tile(const m3c_norm_params &p, const Tile &g, size_t smem, void *stream)
 {
-    return p.resid_b != nullptr ? launch_tile(norm_tile_kernel<IN, OUT, true>, p, g, smem, p.rows, stream)
-                                : launch_tile(norm_tile_kernel<IN, OUT, false>, p, g, smem, p.rows, stream);
+    // 256 vectors per row (F16/BF16 width 2048, F32 width 1024): one vector
+    // per thread and row, with a compiled geometry
+    if (g.nvec == 256) {
+        return p.resid_b != nullptr
+                   ? launch_tile(norm_tile_kernel<IN, OUT, true, 256>, p, g, smem, p.rows, stream)
+                   : launch_tile(norm_tile_kernel<IN, OUT, false, 256>, p, g, smem, p.rows, stream);
+    }
+    return p.resid_b != nullptr ? launch_tile(norm_tile_kernel<IN, OUT, true, 0>, p, g, smem, p.rows, stream)
+                                : launch_tile(norm_tile_kernel<IN, OUT, false, 0>, p, g, smem, p.rows, stream);
 }
 
 template <int IN>
