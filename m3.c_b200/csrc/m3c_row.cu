@@ -476,6 +476,220 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
     }
 }
 
+// Softmax/TOP_K for the compiled F32 widths, pipelined across tiles.  Two
+// shared-memory stages of 8 rows; while warp 0 runs the ordered sums of tile
+// i, warps 1-7 write the probabilities of tile i-1 and then prefetch tile
+// i+1 into the stage tile i-1 has released, so the sequential sums, the
+// stores and the next loads overlap.  Then all warps find max/argmax/NaN and
+// the exponentials of tile i+1.
+struct PipeState {
+    float sum[2][TILE_WARPS];
+    float reciprocal[2][TILE_WARPS];
+    int special[2][TILE_WARPS];
+    int tiny[2][TILE_WARPS];
+    int skip;
+};
+
+// Copy `live` rows starting at row0 into a stage with threads [first, first + count).
+template <int NVEC>
+__device__ __forceinline__ void stage_copy(unsigned char *dst, const uint4 *src, uint64_t row0, int live,
+                                           int pitch, int thread, int count)
+{
+    for (int r = 0; r < live; ++r) {
+        const uint4 *row = src + (row0 + r) * static_cast<uint64_t>(NVEC);
+        for (int v = thread; v < NVEC; v += count) {
+            cp_async16(dst + r * pitch + v * 16, row + v);
+        }
+    }
+}
+
+template <int OUT, int VPL>
+__global__ void __launch_bounds__(TILE_THREADS, 3)
+    softmax_pipe_kernel(const __grid_constant__ m3c_softmax_params p)
+{
+    constexpr int NVEC = VPL * WARP;          // F32: 4 elements per vector
+    constexpr int WIDTH = NVEC * 4;
+    constexpr int PITCH = WIDTH * 4 + 16;     // bytes (and 4 * the F32 pitch)
+    constexpr int STAGE = TILE_WARPS * PITCH;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ PipeState st;
+    const int warp = static_cast<int>(threadIdx.x) / WARP;
+    const int lane = static_cast<int>(threadIdx.x) % WARP;
+    if (threadIdx.x == 0) {
+        st.skip = failed_before(p.status, p.skip_before) ? 1 : 0;
+        if (!st.skip && p.first_of_run && blockIdx.x == 0) {
+            atomicAdd(const_cast<uint32_t *>(&p.status->runs_started), 1u);
+        }
+    }
+    __syncthreads();
+    const uint64_t tiles = (p.rows + TILE_WARPS - 1) / TILE_WARPS;
+    if (st.skip || blockIdx.x >= tiles) {
+        return;
+    }
+    const uint4 *in = static_cast<const uint4 *>(p.input);
+    const float pos_inf = __int_as_float(0x7f800000);
+    const uint32_t first_command = p.softmax_command < p.topk_command ? p.softmax_command : p.topk_command;
+    const uint64_t out_pitch = static_cast<uint64_t>(WIDTH) * bytes_of(OUT);
+    auto live_rows = [&](uint64_t tile) {
+        const uint64_t row0 = tile * TILE_WARPS;
+        return static_cast<int>(p.rows - row0 < static_cast<uint64_t>(TILE_WARPS) ? p.rows - row0 : TILE_WARPS);
+    };
+
+    // max, first argmax and NaN of row `warp`, then its exponentials in place
+    auto row_pass = [&](int stage, uint64_t tile) {
+        const int live = live_rows(tile);
+        const int r = warp;
+        if (r >= live) return;
+        float *erow = reinterpret_cast<float *>(smem + stage * STAGE + r * PITCH);
+        const float4 *x4 = reinterpret_cast<const float4 *>(erow);
+        float best = -pos_inf;
+        uint32_t best_i = 0xffffffffu;
+        bool nan = false;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int v = lane + j * WARP;
+            const float4 q = x4[v];
+            const float x[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const bool greater = x[t] > best;
+                best = greater ? x[t] : best;
+                best_i = greater ? static_cast<uint32_t>(v * 4 + t) : best_i;
+                nan |= x[t] != x[t];
+            }
+        }
+        warp_best(best, best_i);
+        nan = __any_sync(0xffffffffu, nan);
+        if (best_i == 0xffffffffu) best_i = 0u;  // a row of -inf only
+        if (nan && lane == 0) record_failure(p.status, first_command);
+        const uint64_t row = tile * TILE_WARPS + r;
+        if (p.top_values != nullptr && lane == 0) {
+            p.top_values[row] = best;
+            p.top_indices[row] = static_cast<int32_t>(best_i);
+        }
+        if (p.probs == nullptr) return;
+        if (best == -pos_inf || best == pos_inf) {
+            // src/m3_op_execute_basic.c:165-170: final probabilities now
+            uint32_t infinities = 0u;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const float4 q = x4[lane + j * WARP];
+                infinities += (q.x == pos_inf) + (q.y == pos_inf) + (q.z == pos_inf) + (q.w == pos_inf);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) infinities += __shfl_xor_sync(0xffffffffu, infinities, off);
+            const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int v = lane + j * WARP;
+                const float4 q = x4[v];
+                const bool plus = best == pos_inf;
+                reinterpret_cast<float4 *>(erow)[v] =
+                    make_float4(plus && q.x == pos_inf ? share : 0.0f, plus && q.y == pos_inf ? share : 0.0f,
+                                plus && q.z == pos_inf ? share : 0.0f, plus && q.w == pos_inf ? share : 0.0f);
+            }
+            if (lane == 0) {
+                st.special[stage][r] = 1;
+                st.tiny[stage][r] = 0;
+            }
+            return;
+        }
+        bool tiny = false;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int v = lane + j * WARP;
+            const float4 q = x4[v];
+            const float4 e = make_float4(expf(__fsub_rn(q.x, best)), expf(__fsub_rn(q.y, best)),
+                                         expf(__fsub_rn(q.z, best)), expf(__fsub_rn(q.w, best)));
+            tiny |= (e.x < 0x1p-100f) | (e.y < 0x1p-100f) | (e.z < 0x1p-100f) | (e.w < 0x1p-100f);
+            reinterpret_cast<float4 *>(erow)[v] = e;
+        }
+        tiny = __any_sync(0xffffffffu, tiny);
+        if (lane == 0) {
+            st.special[stage][r] = 0;
+            st.tiny[stage][r] = tiny ? 1 : 0;
+        }
+    };
+
+    // probabilities e / sum (src/m3_op_execute_basic.c:171-178) of a tile,
+    // by threads [first, first + count)
+    auto store_tile = [&](int stage, uint64_t tile, int thread, int count) {
+        const int live = live_rows(tile);
+        unsigned char *out = static_cast<unsigned char *>(p.probs) + tile * TILE_WARPS * out_pitch;
+        for (int rr = 0; rr < live; ++rr) {
+            const float4 *e4 = reinterpret_cast<const float4 *>(smem + stage * STAGE + rr * PITCH);
+            unsigned char *orow = out + rr * out_pitch;
+            const float sum = st.sum[stage][rr];
+            const float y = st.reciprocal[stage][rr];
+            const bool special = st.special[stage][rr] != 0;
+            const bool tiny = st.tiny[stage][rr] != 0;
+            for (int j4 = thread; j4 < NVEC; j4 += count) {
+                const float4 e = e4[j4];
+                float pr[4] = {e.x, e.y, e.z, e.w};
+                if (!special) {
+                    if (!tiny) {
+                        // e in [2^-100, 1] and sum >= 1: Markstein's quotient
+                        // is the IEEE one
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) pr[t] = div_markstein(pr[t], sum, y);
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            pr[t] = pr[t] >= 0x1p-100f ? div_markstein(pr[t], sum, y) : ieee_div(pr[t], sum);
+                        }
+                    }
+                }
+                store_vec<4>(orow, OUT, static_cast<uint64_t>(j4) * 4u, pr);
+            }
+        }
+    };
+
+    uint64_t tile = blockIdx.x;
+    int stage = 0;
+    stage_copy<NVEC>(smem, in, tile * TILE_WARPS, live_rows(tile), PITCH, threadIdx.x, TILE_THREADS);
+    cp_async_wait_all();
+    __syncthreads();
+    row_pass(stage, tile);
+    __syncthreads();
+    bool have_previous = false;
+    uint64_t previous = 0;
+    for (;;) {
+        const uint64_t next = tile + gridDim.x;
+        const bool has_next = next < tiles;
+        if (warp == 0) {
+            // the reference's left-to-right sums, one row per lane
+            if (p.probs != nullptr && lane < live_rows(tile) && !st.special[stage][lane]) {
+                const float sum =
+                    ordered_sum_f32(reinterpret_cast<const float *>(smem + stage * STAGE + lane * PITCH), WIDTH);
+                st.sum[stage][lane] = sum;
+                st.reciprocal[stage][lane] = __frcp_rn(sum);
+            }
+        } else {
+            if (have_previous && p.probs != nullptr) {
+                store_tile(stage ^ 1, previous, static_cast<int>(threadIdx.x) - WARP, TILE_THREADS - WARP);
+            }
+            // every read of the other stage is done before it is refilled
+            asm volatile("bar.sync 1, %0;" ::"r"(TILE_THREADS - WARP) : "memory");
+            if (has_next) {
+                stage_copy<NVEC>(smem + (stage ^ 1) * STAGE, in, next * TILE_WARPS, live_rows(next), PITCH,
+                                 static_cast<int>(threadIdx.x) - WARP, TILE_THREADS - WARP);
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        have_previous = true;
+        previous = tile;
+        if (!has_next) break;
+        tile = next;
+        stage ^= 1;
+        row_pass(stage, tile);
+        __syncthreads();
+    }
+    if (p.probs != nullptr) {
+        store_tile(stage, previous, static_cast<int>(threadIdx.x), TILE_THREADS);
+    }
+}
+
 // RMSNorm / LayerNorm with an optional residual-add prologue (RESID: the
 // input is round_in(x + b), optionally stored to sum_out).
 template <int IN, int OUT, bool RESID, int NVEC>
@@ -912,19 +1126,37 @@ int launch_tile(Kernel kernel, const Params &params, const Tile &g, size_t smem,
     return static_cast<int>(cudaGetLastError());
 }
 
+template <typename Kernel>
+int launch_pipe(Kernel kernel, const m3c_softmax_params &params, size_t smem, void *stream)
+{
+    if (smem > 48u * 1024u) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, TILE_THREADS, smem) != cudaSuccess ||
+        per_sm < 1) {
+        per_sm = 1;
+    }
+    const uint64_t tiles = (params.rows + TILE_WARPS - 1) / TILE_WARPS;
+    const uint64_t cap = static_cast<uint64_t>(sm_count_current()) * static_cast<uint64_t>(per_sm);
+    const unsigned grid = static_cast<unsigned>(tiles == 0 ? 1 : (tiles < cap ? tiles : cap));
+    kernel<<<grid, TILE_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(params);
+    return static_cast<int>(cudaGetLastError());
+}
+
 // Tile kernels are compiled per (input, output) dtype pair so that every
 // codec folds to straight-line code.
 template <int IN, int OUT>
 int softmax_tile(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
 {
-    // widths with a compiled geometry (8-row tiles, one warp per row)
-    if (IN == M3C_F32 && g.rows == TILE_WARPS && g.group == 1 && p.k <= 1) {
+    // widths with a compiled geometry: 8-row tiles in two stages
+    if (IN == M3C_F32 && g.rows == TILE_WARPS && g.group == 1 && p.k <= 1 &&
+        (g.width == 1024 || g.width == 512)) {
+        const size_t stages = 2u * static_cast<size_t>(TILE_WARPS) * static_cast<size_t>(g.raw_pitch);
         if (g.width == 1024) {
-            return launch_tile(softmax_tile_kernel<IN, OUT, 8>, p, g, smem, p.rows, stream);
+            return launch_pipe(softmax_pipe_kernel<OUT, 8>, p, stages, stream);
         }
-        if (g.width == 512) {
-            return launch_tile(softmax_tile_kernel<IN, OUT, 4>, p, g, smem, p.rows, stream);
-        }
+        return launch_pipe(softmax_pipe_kernel<OUT, 4>, p, stages, stream);
     }
     return launch_tile(softmax_tile_kernel<IN, OUT, 0>, p, g, smem, p.rows, stream);
 }
