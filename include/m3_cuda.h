@@ -670,6 +670,16 @@ m3_status m3_cuda_codec_self_test(int device, uint64_t *mismatches,
 m3_status m3_cuda_division_self_test(int device, uint64_t samples,
                                      uint64_t *mismatches, m3_error *error);
 
+/* Diagnostics: gated SiLU with F16 or BF16 results evaluates e^-g with the
+ * PTX base-2 approximation after a Cody-Waite reduction (for |g| <= 80;
+ * other gates, and F32 results, take the IEEE path), since a few F32 ulps
+ * are far below the half-ulp of the 16-bit result.  This runs every F32
+ * argument in [-87, 87] on `device` against the correctly rounded e^d and
+ * reports the largest distance in ulps (`max_ulp`) and `violations`, the
+ * count of wrong special values (e^0 must be exactly 1). */
+m3_status m3_cuda_exp_self_test(int device, uint32_t *max_ulp,
+                                uint64_t *violations, m3_error *error);
+
 /* ------------------------------------------------------------------------
  * Abs-max without allocation.  No counterpart in the reference: m3.c has no
  * device memory to manage, so it has no allocation-free variant either.

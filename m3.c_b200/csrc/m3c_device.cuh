@@ -283,6 +283,41 @@ __device__ __forceinline__ float div_markstein(float a, float b, float y)
     return __fmaf_rn(r, y, q0);
 }
 
+// e^d for |d| <= EXP_MODERATE_LIMIT, where e^d is a normal F32 number, from
+// the hardware base-2 approximation (PTX ex2.approx) after an additive
+// Cody-Waite reduction (W. J. Cody and W. Waite, Software Manual for the
+// Elementary Functions, 1980):
+//   e^d = 2^h * e^c,  h = RN(d log2 e),  c = d - h ln 2,
+// where c, the part of d that h misses, is evaluated with two FMAs against a
+// two-piece ln 2 (|c| < 2^-16, accurate to about 2^-31) and e^c = 1 + c to
+// within c^2 / 2 < 2^-33.  A few ulps from the correctly rounded value
+// (m3_cuda_exp_self_test measures every F32 argument of the range): for
+// results that are then rounded to F16 or BF16 only, not where the
+// reference's F32 value is kept.
+constexpr float EXP_MODERATE_LIMIT = 87.0f;  // e^-87 = 1.6e-38 > 2^-126
+
+__device__ __forceinline__ float exp_moderate(float d)
+{
+    const float h = __fmul_rn(d, 0x1.715476p+0f);     // RN(log2 e)
+    float c = __fmaf_rn(-h, 0x1.62e000p-1f, d);       // ln 2, leading 12 bits
+    c = __fmaf_rn(-h, 0x1.0bfbe8p-15f, c);            // ln 2, the rest
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(h));
+    return __fmaf_rn(r, c, r);
+}
+
+// a / b within about one ulp for normal a / b and b: the hardware reciprocal
+// approximation refined by one step of the Markstein correction.  Like
+// exp_moderate, only for results rounded to F16 or BF16 afterwards.
+__device__ __forceinline__ float div_approx(float a, float b)
+{
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    const float q0 = __fmul_rn(a, y);
+    const float r = __fmaf_rn(-q0, b, a);
+    return __fmaf_rn(r, y, q0);
+}
+
 // Granlund-Montgomery division by an invariant 32-bit divisor.
 __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const m3c_fastdiv &d)
 {

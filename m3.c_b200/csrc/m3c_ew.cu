@@ -349,10 +349,25 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
         // src/m3_op_execute_basic.c:113-117: the activation g / (1 + e^-g)
         // is stored in the gate's dtype before the product
         float f[VEC];
+        bool moderate = op.aux == M3C_F16 || op.aux == M3C_BF16;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-            const float gate = as_float(a[j]);
-            f[j] = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
+        for (int j = 0; j < VEC; ++j) moderate &= fabsf(as_float(a[j])) <= 80.0f;  // false for NaN
+        if (moderate) {
+            // The activation is rounded to 16 bits, whose half ulp (2^-12
+            // relative or more) dwarfs the few F32 ulps of the approximate
+            // exponential and quotient; e^-g and 1 + e^-g stay normal and
+            // finite for |g| <= 80.
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) {
+                const float gate = as_float(a[j]);
+                f[j] = div_approx(gate, __fadd_rn(1.0f, exp_moderate(-gate)));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) {
+                const float gate = as_float(a[j]);
+                f[j] = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
+            }
         }
         round_values<VEC>(op.aux, f);
 #pragma unroll

@@ -214,6 +214,32 @@ __global__ void division_check_kernel(uint64_t samples, unsigned long long *mism
     if (local != 0) atomicAdd(mismatches, local);
 }
 
+// exp_moderate against the correctly rounded e^d (the double-precision exp
+// rounded to F32) for every F32 argument d in [-87, 87]: the largest distance
+// in ulps, and the count of wrong special values (e^+-0 must be exactly 1).
+__global__ void exp_check_kernel(unsigned int *worst, unsigned long long *violations)
+{
+    constexpr uint32_t last = 0x42ae0000u;  // |87.0|
+    unsigned int local = 0u;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i <= last; i += stride) {
+#pragma unroll
+        for (int sign = 0; sign < 2; ++sign) {
+            const float d = as_float((sign ? 0x80000000u : 0u) | i);
+            const float got = exp_moderate(d);
+            const float want = __double2float_rn(exp(static_cast<double>(d)));
+            const int32_t distance = static_cast<int32_t>(as_bits(got)) - static_cast<int32_t>(as_bits(want));
+            const unsigned int ulps = static_cast<unsigned int>(distance < 0 ? -distance : distance);
+            local = ulps > local ? ulps : local;
+        }
+    }
+    atomicMax(worst, local);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const bool ok = exp_moderate(0.0f) == 1.0f && exp_moderate(-0.0f) == 1.0f;
+        if (!ok) atomicAdd(violations, 1ull);
+    }
+}
+
 }  // namespace
 }  // namespace m3c
 
@@ -240,6 +266,40 @@ extern "C" m3_status m3_cuda_division_self_test(int device, uint64_t samples, ui
         return M3_STATUS_INTERNAL;
     }
     if (mismatches != nullptr) *mismatches = host;
+    if (error != nullptr) {
+        error->status = M3_STATUS_OK;
+        error->message[0] = '\0';
+    }
+    return M3_STATUS_OK;
+}
+
+extern "C" m3_status m3_cuda_exp_self_test(int device, uint32_t *max_ulp, uint64_t *violations, m3_error *error)
+{
+    struct Result {
+        unsigned int worst;
+        unsigned int pad;
+        unsigned long long violations;
+    };
+    Result *result = nullptr;
+    Result host = {};
+    cudaError_t code = cudaSetDevice(device);
+    if (code == cudaSuccess) code = cudaMalloc(&result, sizeof(*result));
+    if (code == cudaSuccess) code = cudaMemset(result, 0, sizeof(*result));
+    if (code == cudaSuccess) {
+        m3c::exp_check_kernel<<<148 * 16, 256>>>(&result->worst, &result->violations);
+        code = cudaGetLastError();
+    }
+    if (code == cudaSuccess) code = cudaMemcpy(&host, result, sizeof(host), cudaMemcpyDeviceToHost);
+    if (result != nullptr) cudaFree(result);
+    if (code != cudaSuccess) {
+        if (error != nullptr) {
+            error->status = M3_STATUS_INTERNAL;
+            snprintf(error->message, sizeof(error->message), "exp self-test failed: %s", cudaGetErrorString(code));
+        }
+        return M3_STATUS_INTERNAL;
+    }
+    if (max_ulp != nullptr) *max_ulp = host.worst;
+    if (violations != nullptr) *violations = host.violations;
     if (error != nullptr) {
         error->status = M3_STATUS_OK;
         error->message[0] = '\0';

@@ -95,6 +95,25 @@ def test_markstein_division_matches_ieee_on_softmax_domain(m3, gpu):
     assert mismatches.value == 0
 
 
+def test_moderate_exponential_error_bound(m3, gpu):
+    """The exponential of the 16-bit gated SiLU path: every F32 argument in
+    [-87, 87] within 4 ulps (4 * 2^-23 = 4.8e-7 relative) of the correctly
+    rounded e^d, and exactly 1 at 0.  A 16-bit result's half ulp is 2^-12
+    (F16) or 2^-9 (BF16) relative, so such an error moves the rounded
+    result only when the exact value lies within 4.8e-7 of a rounding
+    boundary, and then by one ulp."""
+    import ctypes
+
+    worst = ctypes.c_uint32(99)
+    violations = ctypes.c_uint64(99)
+    err = m3.M3Error()
+    m3.check(m3.load().m3_cuda_exp_self_test(0, ctypes.byref(worst), ctypes.byref(violations),
+                                             ctypes.byref(err)), err)
+    print("exp_moderate: max ulp", worst.value)
+    assert violations.value == 0
+    assert worst.value <= 4
+
+
 # ------------------------------------------------------------ element-wise
 
 
@@ -234,6 +253,41 @@ def test_gated_silu(m3, ref, oracle, gpu, dtype):
         assert close_abs_or_rel(mine, theirs, 2.0 ** -20)
     else:
         assert ulp_distance(mine, theirs).max() <= 1
+
+
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+def test_gated_silu_16_bit_across_gate_range(m3, ref, oracle, gpu, dtype):
+    """16-bit gated SiLU over a million elements whose gates cover every
+    binade the 16-bit type has, both sides of the |g| = 80 switch between the
+    approximate and the IEEE evaluation, infinities, zeros and subnormals:
+    within 1 ulp of the reference everywhere."""
+    dt = getattr(m3, dtype)
+    enc = {"F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+    rng = np.random.default_rng(17)
+    shape = (4096, 257)
+    top = 15 if dtype == "F16" else 100
+    mags = np.exp2(rng.uniform(-24 if dtype == "F16" else -120, top, shape))
+    g32 = (mags * rng.choice([-1.0, 1.0], shape)).astype(np.float32)
+    g32[0, :16] = [0.0, -0.0, 79.9, -79.9, 80.0, -80.0, 80.5, -80.5, 90.0, -90.0,
+                   np.inf, -np.inf, 1e-7, -1e-7, 6e-8, 3.0]
+    u32 = (rng.standard_normal(shape) * 2).astype(np.float32)
+
+    def build(g):
+        a = g.value(m3.INPUT, dt, shape)
+        b = g.value(m3.INPUT, dt, shape)
+        y = g.inferred("GATED_SILU", [a, b], m3.OUTPUT, dt)
+        g.node("GATED_SILU", [a, b], [y])
+        return {"g": a, "u": b}, [y]
+
+    (mine,), (theirs,) = run_both(m3, ref, build, {"g": enc(g32), "u": enc(u32)})
+    # -inf / inf makes a NaN from non-NaN operands, whose bits are the
+    # platform's default NaN (x86 and ARM differ; the GPU has its own): both
+    # sides must be NaN there, and within 1 ulp everywhere else
+    exponent = 0x7C00 if dtype == "F16" else 0x7F80
+    nan = lambda b: ((b & 0x7FFF) > exponent)
+    both_nan = nan(mine) & nan(theirs)
+    assert np.array_equal(nan(mine), nan(theirs))
+    assert ulp_distance(mine[~both_nan], theirs[~both_nan]).max() <= 1
 
 
 def test_snake_tanh_clamp_absmax(m3, ref, oracle, gpu):
@@ -433,6 +487,69 @@ def test_softmax_top_k(m3, ref, gpu, width, k):
     rel = np.abs(p.astype(np.float64) - rp) / np.maximum(np.abs(rp), 1e-30)
     assert rel.max() <= 1e-6, rel.max()
     assert np.array_equal(p[0], rp[0]) and np.array_equal(p[1], rp[1])
+
+
+@pytest.mark.parametrize("width", [512, 1024])
+@pytest.mark.parametrize("mode", ["both", "softmax", "top_k"])
+def test_softmax_compiled_widths_many_tiles(m3, ref, gpu, width, mode):
+    """The compiled-width F32 kernel runs a ring of tile stages per CTA:
+    enough rows for several tiles per CTA, a ragged last tile, special rows
+    (all -inf, +inf entries, ties, exponentials below 2^-100) spread over
+    the tensor, and each of the three output combinations."""
+    rows = 8 * 2500 + 5
+    rng = np.random.default_rng(width + len(mode))
+    x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
+    for r in rng.choice(rows, 40, replace=False):
+        kind = r % 4
+        if kind == 0:
+            x[r, :] = -np.inf
+        elif kind == 1:
+            x[r, rng.choice(width, 3, replace=False)] = np.inf
+        elif kind == 2:
+            x[r, :] = 5.0
+        else:
+            x[r, rng.choice(width, 5, replace=False)] = 90.0   # the rest underflow past 2^-100
+    x[-1, :] = -np.inf
+
+    def build(g):
+        v = g.value(m3.INPUT, m3.F32, x.shape)
+        outs = []
+        if mode != "top_k":
+            p = g.inferred("SOFTMAX", [v], m3.OUTPUT, m3.F32)
+            g.node("SOFTMAX", [v], [p])
+            outs.append(p)
+        if mode != "softmax":
+            tv = g.inferred("TOP_K", [v], m3.OUTPUT, m3.F32, 0, k=1)
+            ti = g.inferred("TOP_K", [v], m3.OUTPUT, m3.I32, 1, k=1)
+            g.node("TOP_K", [v], [tv, ti], k=1)
+            outs += [tv, ti]
+        return {"x": v}, outs
+
+    got, want = run_both(m3, ref, build, {"x": x})
+    if mode != "top_k":
+        p, rp = got.pop(0), want.pop(0)
+        rel = np.abs(p.astype(np.float64) - rp) / np.maximum(np.abs(rp), 1e-30)
+        assert rel.max() <= 1e-6, rel.max()
+    if mode != "softmax":
+        assert np.array_equal(bits(got[0]), bits(want[0])) and np.array_equal(got[1], want[1])
+
+
+def test_softmax_compiled_width_nan_deep_in_tensor(m3, gpu):
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (20000, 1024))
+    p = g.inferred("SOFTMAX", [x], m3.OUTPUT, m3.F32)
+    g.node("SOFTMAX", [x], [p])
+    s = m3.Session(g)
+    good = np.random.default_rng(4).standard_normal((20000, 1024)).astype(np.float32)
+    s.write(x, good)
+    s.run()
+    before = s.read(p).copy()
+    bad = good.copy()
+    bad[17771, 1000] = np.nan
+    s.write(x, bad)
+    status, message = s.run_status()
+    assert status == m3.OUT_OF_RANGE and message == "softmax input contains NaN"
+    assert np.array_equal(s.read(p), before)
 
 
 @pytest.mark.parametrize("dtype", ["F16", "BF16"])
