@@ -349,25 +349,10 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
         // src/m3_op_execute_basic.c:113-117: the activation g / (1 + e^-g)
         // is stored in the gate's dtype before the product
         float f[VEC];
-        bool moderate = op.aux == M3C_F16 || op.aux == M3C_BF16;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) moderate &= fabsf(as_float(a[j])) <= 80.0f;  // false for NaN
-        if (moderate) {
-            // The activation is rounded to 16 bits, whose half ulp (2^-12
-            // relative or more) dwarfs the few F32 ulps of the approximate
-            // exponential and quotient; e^-g and 1 + e^-g stay normal and
-            // finite for |g| <= 80.
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                const float gate = as_float(a[j]);
-                f[j] = div_approx(gate, __fadd_rn(1.0f, exp_moderate(-gate)));
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                const float gate = as_float(a[j]);
-                f[j] = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
-            }
+        for (int j = 0; j < VEC; ++j) {
+            const float gate = as_float(a[j]);
+            f[j] = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
         }
         round_values<VEC>(op.aux, f);
 #pragma unroll
@@ -550,6 +535,7 @@ __device__ __forceinline__ m3c_ew_op decode(uint64_t e, uint16_t command)
 
 template <int NOPERANDS, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
 struct Fixed {
+    static constexpr bool custom_loop = false;
     static constexpr int unroll = 2;
     static constexpr int operands = NOPERANDS;
     static constexpr uint64_t opsig = OPSIG;
@@ -563,6 +549,7 @@ struct Fixed {
 };
 
 struct Dynamic {
+    static constexpr bool custom_loop = false;
     static constexpr int unroll = 1;
     static constexpr int operands = M3C_EW_MAX_OPERANDS;
     static constexpr uint64_t opsig = ANY_OPERANDS;
@@ -669,16 +656,12 @@ __device__ __forceinline__ void store_block_all(const m3c_ew_params &p, uint64_t
     }
 }
 
+// The grid-stride loop of a program over all blocks, then the tail.
 template <class Prog, bool WIDE>
-__global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c_ew_params p)
+__device__ __forceinline__ void program_loop(const m3c_ew_params &p, Flags &flags)
 {
     constexpr int U = Prog::unroll;
-    const bool skip = failed_before(p.status, p.skip_before);
-    if (p.first_of_run && !skip && blockIdx.x == 0 && threadIdx.x == 0) {
-        atomicAdd(&p.status->runs_started, 1u);
-    }
-    Flags flags{0xffffffffu, 0u};
-    if (!skip) {
+    {
         const uint64_t blocks = p.count / VEC;
         const uint64_t threads = static_cast<uint64_t>(gridDim.x) * THREADS;
         for (uint64_t v = static_cast<uint64_t>(blockIdx.x) * THREADS + threadIdx.x; v < blocks;
@@ -705,6 +688,154 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
             load_operands<WIDE, Prog::operands>(p, blocks * VEC, tail, rf);
             Prog::run(p, rf, tail, flags);
             store_outputs(p, blocks * VEC, tail, rf);
+        }
+    }
+}
+
+// Gated SiLU of 16-bit gate and up with a 16-bit result (the benchmark's
+// MLP activation), as its own loop over packed words: two 8-byte loads and
+// one 8-byte store per four elements.  One test of the raw words finds the
+// blocks whose gates and ups are all finite with |gate| <= 80; those take a
+// straight path: hardware widening, the approximate exponential and quotient
+// (a few F32 ulps, far below the result's half ulp), the activation rounded
+// to 16 bits as the reference stores it, the product, and one packed
+// narrowing, with no NaN to carry.  Every other block, the tail and outputs
+// stored element by element run the table's op-by-op program.
+template <int DT, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
+struct Gsilu16 {
+    using Generic = Fixed<2, OPSIG, OUTSIG, OPS...>;
+    static_assert(!Generic::custom_loop && Generic::unroll > 0, "the fallback is the table's own program");
+    static constexpr bool custom_loop = true;
+    static constexpr int unroll = 4;
+    static constexpr int operands = Generic::operands;
+    static constexpr uint64_t opsig = Generic::opsig;
+    static constexpr uint64_t outsig = Generic::outsig;
+
+    __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid, Flags &flags)
+    {
+        Generic::run(p, rf, valid, flags);
+    }
+
+    __device__ __forceinline__ static void widen2(uint32_t w, float &lo, float &hi)
+    {
+        if constexpr (DT == M3C_F16) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+            lo = f.x;
+            hi = f.y;
+        } else {
+            lo = as_float(w << 16);
+            hi = as_float(w & 0xffff0000u);
+        }
+    }
+
+    __device__ __forceinline__ static uint32_t narrow2(float lo, float hi)
+    {
+        if constexpr (DT == M3C_F16) {
+            const __half2 h = __floats2half2_rn(lo, hi);
+            return *reinterpret_cast<const uint32_t *>(&h);
+        } else {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+            return *reinterpret_cast<const uint32_t *>(&h);
+        }
+    }
+
+    // four results (two packed words) from four gates and ups
+    __device__ __forceinline__ static uint2 block(const m3c_ew_params &p, uint2 gw, uint2 uw, Flags &flags)
+    {
+        // a half is infinite or NaN when its magnitude reaches the all-ones
+        // exponent, i.e. when magnitude + (0x8000 - that) carries into bit 15
+        constexpr uint32_t CARRY = DT == M3C_F16 ? 0x04000400u : 0x00800080u;
+        const uint32_t special = (((gw.x & 0x7fff7fffu) + CARRY) | ((gw.y & 0x7fff7fffu) + CARRY) |
+                                  ((uw.x & 0x7fff7fffu) + CARRY) | ((uw.y & 0x7fff7fffu) + CARRY)) &
+                                 0x80008000u;
+        float g[VEC];
+        float u[VEC];
+        widen2(gw.x, g[0], g[1]);
+        widen2(gw.y, g[2], g[3]);
+        widen2(uw.x, u[0], u[1]);
+        widen2(uw.y, u[2], u[3]);
+        const float largest = fmaxf(fmaxf(fabsf(g[0]), fabsf(g[1])), fmaxf(fabsf(g[2]), fabsf(g[3])));
+        if (special == 0u && largest <= 80.0f) {
+            // src/m3_op_execute_basic.c:113-117: the activation is stored in
+            // the gate's dtype before the product
+            float s[VEC];
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) s[j] = div_approx(g[j], __fadd_rn(1.0f, exp_moderate(-g[j])));
+            widen2(narrow2(s[0], s[1]), s[0], s[1]);
+            widen2(narrow2(s[2], s[3]), s[2], s[3]);
+            return make_uint2(narrow2(__fmul_rn(s[0], u[0]), __fmul_rn(s[1], u[1])),
+                              narrow2(__fmul_rn(s[2], u[2]), __fmul_rn(s[3], u[3])));
+        }
+        RegisterFile rf;
+        rf.w[0][0] = gw.x & 0xffffu;
+        rf.w[0][1] = gw.x >> 16;
+        rf.w[0][2] = gw.y & 0xffffu;
+        rf.w[0][3] = gw.y >> 16;
+        rf.w[1][0] = uw.x & 0xffffu;
+        rf.w[1][1] = uw.x >> 16;
+        rf.w[1][2] = uw.y & 0xffffu;
+        rf.w[1][3] = uw.y >> 16;
+        Generic::run(p, rf, VEC, flags);
+        const float f[VEC] = {as_float(rf.w[0][0]), as_float(rf.w[0][1]), as_float(rf.w[0][2]),
+                              as_float(rf.w[0][3])};
+        uint32_t h[2];
+        narrow_pairs<2>(DT, f, h);  // the reference's NaN rules
+        return make_uint2(h[0], h[1]);
+    }
+
+    __device__ __forceinline__ static void loop(const m3c_ew_params &p, Flags &flags)
+    {
+        if (p.outputs[0].scalar_only) {
+            program_loop<Gsilu16, false>(p, flags);
+            return;
+        }
+        constexpr int U = unroll;
+        const uint2 *gate = static_cast<const uint2 *>(p.operands[0].base);
+        const uint2 *up = static_cast<const uint2 *>(p.operands[1].base);
+        uint2 *out = static_cast<uint2 *>(p.outputs[0].base);
+        const uint64_t blocks = p.count / VEC;
+        const uint64_t threads = static_cast<uint64_t>(gridDim.x) * THREADS;
+        for (uint64_t v = static_cast<uint64_t>(blockIdx.x) * THREADS + threadIdx.x; v < blocks;
+             v += threads * U) {
+            uint2 gw[U];
+            uint2 uw[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const uint64_t b = v + static_cast<uint64_t>(k) * threads;
+                if (b < blocks) {
+                    gw[k] = __ldcs(gate + b);
+                    uw[k] = __ldcs(up + b);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const uint64_t b = v + static_cast<uint64_t>(k) * threads;
+                if (b < blocks) __stcs(out + b, block(p, gw[k], uw[k], flags));
+            }
+        }
+        const int tail = static_cast<int>(p.count - blocks * VEC);
+        if (tail != 0 && blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+            RegisterFile rf;
+            load_operands<false, operands>(p, blocks * VEC, tail, rf);
+            Generic::run(p, rf, tail, flags);
+            store_outputs(p, blocks * VEC, tail, rf);
+        }
+    }
+};
+
+template <class Prog, bool WIDE>
+__global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c_ew_params p)
+{
+    const bool skip = failed_before(p.status, p.skip_before);
+    if (p.first_of_run && !skip && blockIdx.x == 0 && threadIdx.x == 0) {
+        atomicAdd(&p.status->runs_started, 1u);
+    }
+    Flags flags{0xffffffffu, 0u};
+    if (!skip) {
+        if constexpr (Prog::custom_loop) {
+            Prog::loop(p, flags);
+        } else {
+            program_loop<Prog, WIDE>(p, flags);
         }
     }
     if (p.reduce != nullptr && flags.max_bits > 0x7f800000u) {
@@ -808,8 +939,6 @@ constexpr uint64_t output_sig(std::initializer_list<uint32_t> bytes)
     X(6, (operand_sig({C32, I32C, C32, I32C, I32C, C32})),                                \
       (output_sig({OUT(0, M3C_F32), OUT(1, M3C_BF16)})), OPS_CFG_EULER_BF16)             \
     X(2, (operand_sig({C32, C32})), (output_sig({OUT(0, M3C_F32)})), OPS_GSILU_F32)        \
-    X(2, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_GSILU_F16)        \
-    X(2, (operand_sig({CB16, CB16})), (output_sig({OUT(0, M3C_BF16)})), OPS_GSILU_BF16)    \
     X(2, (operand_sig({C32, U32_2})), (output_sig({OUT(0, M3C_F32)})), OPS_SNAKE_ABSMAX_CLAMP) \
     X(2, (operand_sig({C32, U32_2})), (output_sig({OUT(0, M3C_F32)})), OPS_SNAKE)          \
     X(1, (operand_sig({C32})), (output_sig({OUT(0, M3C_F32)})), OPS_TANH)                  \
@@ -861,6 +990,7 @@ struct Entry {
     int count;
     uint64_t ops[M3C_EW_MAX_OPS];
     ew_fn kernel;
+    int unroll;  // blocks of VEC elements per thread and pass
 };
 
 constexpr int count_of(std::initializer_list<uint64_t> ops)
@@ -870,10 +1000,21 @@ constexpr int count_of(std::initializer_list<uint64_t> ops)
 
 // Fixed programs cover index spaces below 2^32 elements; larger ones use the
 // generic kernel's 64-bit addressing.
-#define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS) \
-    {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>},
+#define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS)                                                  \
+    {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>, \
+     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll},
 
-const Entry PROGRAMS[] = {M3C_PROGRAMS(M3C_ENTRY)};
+// the dedicated 16-bit gated SiLU programs, matched like the table's own
+#define M3C_GSILU16_ENTRY(DT, OPSIG, OUTSIG, OPS)                                                  \
+    {2, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Gsilu16<DT, OPSIG, OUTSIG, OPS>, false>,    \
+     Gsilu16<DT, OPSIG, OUTSIG, OPS>::unroll},
+
+const Entry PROGRAMS[] = {
+    M3C_GSILU16_ENTRY(M3C_F16, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_GSILU_F16)
+    M3C_GSILU16_ENTRY(M3C_BF16, (operand_sig({CB16, CB16})), (output_sig({OUT(0, M3C_BF16)})), OPS_GSILU_BF16)
+    M3C_PROGRAMS(M3C_ENTRY)};
+
+#undef M3C_GSILU16_ENTRY
 
 #undef M3C_ENTRY
 #undef E
@@ -969,10 +1110,11 @@ extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
         const uint64_t cap = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(per_sm);
         grid = blocks_needed < cap ? blocks_needed : cap;
     } else {
-        // otherwise one pass per thread (two blocks of VEC elements each):
-        // every load of the launch is issued as soon as its CTA is resident
-        // and the block scheduler keeps the SMs full to the end
-        grid = (blocks_needed + 1) / 2;
+        // otherwise one pass per thread (`unroll` blocks of VEC elements
+        // each): every load of the launch is issued as soon as its CTA is
+        // resident and the block scheduler keeps the SMs full to the end
+        const uint64_t unroll = entry != nullptr ? static_cast<uint64_t>(entry->unroll) : 2u;
+        grid = (blocks_needed + unroll - 1) / unroll;
         if (grid > 0x7fffffffull) grid = 0x7fffffffull;
     }
     if (grid == 0) grid = 1;  // empty tensors still run the reduction epilogue
