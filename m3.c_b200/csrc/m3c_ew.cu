@@ -536,7 +536,7 @@ __device__ __forceinline__ m3c_ew_op decode(uint64_t e, uint16_t command)
 template <int NOPERANDS, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
 struct Fixed {
     static constexpr bool custom_loop = false;
-    static constexpr int unroll = 2;
+    static constexpr int unroll = 4;  // blocks per thread and pass, loads all in flight
     static constexpr int operands = NOPERANDS;
     static constexpr uint64_t opsig = OPSIG;
     static constexpr uint64_t outsig = OUTSIG;
