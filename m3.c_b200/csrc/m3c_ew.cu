@@ -579,32 +579,43 @@ __device__ __forceinline__ void load_operands(const m3c_ew_params &p, uint64_t f
     }
 }
 
-template <class Prog, int I>
+// Which operands a load pass covers: the streamed ones (read once, from
+// HBM: their loads go out first for all of a thread's blocks), the cached
+// ones (broadcast rows and elements, immediates: loaded just before their
+// block runs, so they hold no registers while the streamed loads are in
+// flight), or all of them.
+enum LoadPass { LOAD_STREAMED, LOAD_CACHED, LOAD_ALL };
+
+template <class Prog, int I, LoadPass PASS>
 __device__ __forceinline__ void load_operand_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
 {
     constexpr uint32_t sig = static_cast<uint32_t>((Prog::opsig >> (8 * I)) & 0xffu);
-    if constexpr (sig == 0xffu) {
-        load_block<false>(p.operands[I], f, rf.w[I]);
-    } else {
-        load_block_c<sig>(p.operands[I], f, rf.w[I]);
+    constexpr bool streamed = sig != 0xffu && (sig & 7u) == M3C_V_CONTIG;
+    if constexpr (PASS == LOAD_ALL || (PASS == LOAD_STREAMED) == streamed) {
+        if constexpr (sig == 0xffu) {
+            load_block<false>(p.operands[I], f, rf.w[I]);
+        } else {
+            load_block_c<sig>(p.operands[I], f, rf.w[I]);
+        }
     }
 }
 
-template <class Prog, int... I>
+template <class Prog, LoadPass PASS, int... I>
 __device__ __forceinline__ void load_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf,
                                           std::integer_sequence<int, I...>)
 {
-    (load_operand_full<Prog, I>(p, f, rf), ...);
+    (load_operand_full<Prog, I, PASS>(p, f, rf), ...);
 }
 
-// All operands of a full block: through the program's signature when it has
-// one (narrow index only), else the run-time dispatch.
-template <class Prog, bool WIDE>
+// The operands of a full block that a load pass covers: through the
+// program's signature when it has one (narrow index only), else the
+// run-time dispatch (which loads everything in the first pass).
+template <class Prog, bool WIDE, LoadPass PASS>
 __device__ __forceinline__ void load_block_all(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
 {
     if constexpr (Prog::opsig != ANY_OPERANDS && !WIDE) {
-        load_full<Prog>(p, f, rf, std::make_integer_sequence<int, Prog::operands>{});
-    } else {
+        load_full<Prog, PASS>(p, f, rf, std::make_integer_sequence<int, Prog::operands>{});
+    } else if constexpr (PASS != LOAD_CACHED) {
         load_operands<WIDE, Prog::operands>(p, f, VEC, rf);
     }
 }
@@ -666,17 +677,19 @@ __device__ __forceinline__ void program_loop(const m3c_ew_params &p, Flags &flag
         const uint64_t threads = static_cast<uint64_t>(gridDim.x) * THREADS;
         for (uint64_t v = static_cast<uint64_t>(blockIdx.x) * THREADS + threadIdx.x; v < blocks;
              v += threads * U) {
-            // all loads of the U blocks first, so they are in flight together
+            // the streamed loads of the U blocks first, so they are in
+            // flight together
             RegisterFile rf[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const uint64_t b = v + static_cast<uint64_t>(u) * threads;
-                if (b < blocks) load_block_all<Prog, WIDE>(p, b * VEC, rf[u]);
+                if (b < blocks) load_block_all<Prog, WIDE, LOAD_STREAMED>(p, b * VEC, rf[u]);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const uint64_t b = v + static_cast<uint64_t>(u) * threads;
                 if (b < blocks) {
+                    load_block_all<Prog, WIDE, LOAD_CACHED>(p, b * VEC, rf[u]);
                     Prog::run(p, rf[u], VEC, flags);
                     store_block_all<Prog>(p, b * VEC, rf[u]);
                 }
