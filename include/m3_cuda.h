@@ -680,6 +680,15 @@ m3_status m3_cuda_division_self_test(int device, uint64_t samples,
 m3_status m3_cuda_exp_self_test(int device, uint32_t *max_ulp,
                                 uint64_t *violations, m3_error *error);
 
+/* Diagnostics: SNAKE1D evaluates sin^2(alpha x) with its own reduction and
+ * series for |alpha x| <= 8192 (other arguments take sinf), within the
+ * activation's 0x1p-19 tolerance.  This runs every F32 argument in
+ * [-8192, 8192] on `device` against sin(t)^2 in double precision and reports
+ * the largest absolute error and the largest distance in ulps where
+ * sin(t)^2 >= 2^-10. */
+m3_status m3_cuda_sin_squared_self_test(int device, float *max_abs_error,
+                                        uint32_t *max_ulp, m3_error *error);
+
 /* ------------------------------------------------------------------------
  * Abs-max without allocation.  No counterpart in the reference: m3.c has no
  * device memory to manage, so it has no allocation-free variant either.

@@ -306,6 +306,36 @@ __device__ __forceinline__ float exp_moderate(float d)
     return __fmaf_rn(r, c, r);
 }
 
+// sin^2(t) for |t| <= SIN_SQUARED_LIMIT, the snake activation's square of a
+// sine.  t = k pi/2 + r with |r| <= pi/4 (k the nearest integer to
+// t 2/pi; r by a three-part Cody-Waite split of pi/2, W. J. Cody and W.
+// Waite, Software Manual for the Elementary Functions, 1980), then
+// sin^2(t) = sin^2(r) for even k and 1 - sin^2(r) for odd k, with
+// sin^2(r) = u Q(u), u = r^2, Q the Taylor series of sin^2(r) / r^2,
+// sum over n >= 1 of (-1)^(n+1) 2^(2n-1) u^(n-1) / (2n)!, to n = 7 (the
+// next term is below 4e-11 on |r| <= pi/4).  m3_cuda_sin_squared_self_test
+// measures the error over every F32 argument of the range.
+constexpr float SIN_SQUARED_LIMIT = 8192.0f;
+
+__device__ __forceinline__ float sin_squared(float t)
+{
+    const int k = __float2int_rn(__fmul_rn(t, 0x1.45f306p-1f));  // 2/pi
+    const float kf = __int2float_rn(k);
+    float r = __fmaf_rn(-kf, 0x1.921fb6p+0f, t);                   // pi/2 in three parts
+    r = __fmaf_rn(-kf, -0x1.777a5cp-25f, r);
+    r = __fmaf_rn(-kf, -0x1.ee59dap-50f, r);
+    const float u = __fmul_rn(r, r);
+    float q = 0x1.93974ap-24f;                                     // 2^13 / 14!
+    q = __fmaf_rn(q, u, -0x1.1eed8ep-18f);                         // -2^11 / 12!
+    q = __fmaf_rn(q, u, 0x1.27e4fcp-13f);                          // 2^9 / 10!
+    q = __fmaf_rn(q, u, -0x1.a01a02p-9f);                          // -2^7 / 8!
+    q = __fmaf_rn(q, u, 0x1.6c16c2p-5f);                           // 2^5 / 6!
+    q = __fmaf_rn(q, u, -0x1.555556p-2f);                          // -2^3 / 4!
+    q = __fmaf_rn(q, u, 1.0f);                                     // 2 / 2!
+    const float s = __fmul_rn(u, q);
+    return (k & 1) != 0 ? __fsub_rn(1.0f, s) : s;
+}
+
 // a / b within about one ulp for normal a / b and b: the hardware reciprocal
 // approximation refined by one step of the Markstein correction.  Like
 // exp_moderate, only for results rounded to F16 or BF16 afterwards.

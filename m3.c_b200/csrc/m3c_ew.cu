@@ -366,11 +366,24 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
             // (alpha + eps) is the same statement for all four elements
             const float alpha = as_float(b[0]);
             const float inverse = __fdiv_rn(1.0f, __fadd_rn(alpha, 0x1.12e0bep-30f));
+            float angle[VEC];
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                const float x = as_float(a[j]);
-                const float sine = sinf(__fmul_rn(alpha, x));
-                d[j] = as_bits(__fadd_rn(x, __fmul_rn(inverse, __fmul_rn(sine, sine))));
+            for (int j = 0; j < VEC; ++j) angle[j] = __fmul_rn(alpha, as_float(a[j]));
+            const float largest =
+                fmaxf(fmaxf(fabsf(angle[0]), fabsf(angle[1])), fmaxf(fabsf(angle[2]), fabsf(angle[3])));
+            if (largest <= SIN_SQUARED_LIMIT) {  // false for NaN
+                // the square of the sine straight from sin_squared: a few
+                // F32 ulps, far inside the activation's 0x1p-19 tolerance
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    d[j] = as_bits(__fadd_rn(as_float(a[j]), __fmul_rn(inverse, sin_squared(angle[j]))));
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    const float sine = sinf(angle[j]);
+                    d[j] = as_bits(__fadd_rn(as_float(a[j]), __fmul_rn(inverse, __fmul_rn(sine, sine))));
+                }
             }
         } else {
 #pragma unroll

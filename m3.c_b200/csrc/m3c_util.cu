@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 #include <cstdio>
 
 #include "m3_cuda.h"
@@ -240,6 +241,36 @@ __global__ void exp_check_kernel(unsigned int *worst, unsigned long long *violat
     }
 }
 
+// sin_squared against sin(t)^2 in double precision for every F32 argument t
+// in [-8192, 8192]: the largest absolute error (as F32 bits of a
+// non-negative float, so integer maxima order them) and the largest distance
+// in ulps of RN(sin(t)^2) where that is at least 2^-10.
+__global__ void sin_squared_check_kernel(unsigned int *worst_abs_bits, unsigned int *worst_ulps)
+{
+    constexpr uint32_t last = 0x46000000u;  // |8192.0|
+    unsigned int abs_bits = 0u;
+    unsigned int ulps = 0u;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i <= last; i += stride) {
+#pragma unroll
+        for (int sign = 0; sign < 2; ++sign) {
+            const float t = as_float((sign ? 0x80000000u : 0u) | i);
+            const float got = sin_squared(t);
+            const double sine = sin(static_cast<double>(t));
+            const double exact = sine * sine;
+            const float error = __double2float_ru(fabs(static_cast<double>(got) - exact));
+            abs_bits = max(abs_bits, as_bits(error));
+            const float want = __double2float_rn(exact);
+            if (want >= 0x1p-10f) {
+                const int32_t d = static_cast<int32_t>(as_bits(got)) - static_cast<int32_t>(as_bits(want));
+                ulps = max(ulps, static_cast<unsigned int>(d < 0 ? -d : d));
+            }
+        }
+    }
+    atomicMax(worst_abs_bits, abs_bits);
+    atomicMax(worst_ulps, ulps);
+}
+
 }  // namespace
 }  // namespace m3c
 
@@ -300,6 +331,37 @@ extern "C" m3_status m3_cuda_exp_self_test(int device, uint32_t *max_ulp, uint64
     }
     if (max_ulp != nullptr) *max_ulp = host.worst;
     if (violations != nullptr) *violations = host.violations;
+    if (error != nullptr) {
+        error->status = M3_STATUS_OK;
+        error->message[0] = '\0';
+    }
+    return M3_STATUS_OK;
+}
+
+extern "C" m3_status m3_cuda_sin_squared_self_test(int device, float *max_abs_error, uint32_t *max_ulp,
+                                                   m3_error *error)
+{
+    unsigned int *result = nullptr;
+    unsigned int host[2] = {0u, 0u};
+    cudaError_t code = cudaSetDevice(device);
+    if (code == cudaSuccess) code = cudaMalloc(&result, sizeof(host));
+    if (code == cudaSuccess) code = cudaMemset(result, 0, sizeof(host));
+    if (code == cudaSuccess) {
+        m3c::sin_squared_check_kernel<<<148 * 16, 256>>>(result, result + 1);
+        code = cudaGetLastError();
+    }
+    if (code == cudaSuccess) code = cudaMemcpy(host, result, sizeof(host), cudaMemcpyDeviceToHost);
+    if (result != nullptr) cudaFree(result);
+    if (code != cudaSuccess) {
+        if (error != nullptr) {
+            error->status = M3_STATUS_INTERNAL;
+            snprintf(error->message, sizeof(error->message), "sin^2 self-test failed: %s",
+                     cudaGetErrorString(code));
+        }
+        return M3_STATUS_INTERNAL;
+    }
+    if (max_abs_error != nullptr) memcpy(max_abs_error, &host[0], sizeof(float));
+    if (max_ulp != nullptr) *max_ulp = host[1];
     if (error != nullptr) {
         error->status = M3_STATUS_OK;
         error->message[0] = '\0';

@@ -114,6 +114,23 @@ def test_moderate_exponential_error_bound(m3, gpu):
     assert worst.value <= 4
 
 
+def test_sin_squared_error_bound(m3, gpu):
+    """The snake activation's sin^2 for |alpha x| <= 8192, every F32 argument
+    of that range: absolute error below 2^-22 (so the output x + sin^2/alpha
+    moves by under 5 * 2^-22 < 0x1p-19 for alpha >= 0.2) and within 4 ulps
+    where sin^2 >= 2^-10."""
+    import ctypes
+
+    abs_error = ctypes.c_float(99.0)
+    worst = ctypes.c_uint32(99)
+    err = m3.M3Error()
+    m3.check(m3.load().m3_cuda_sin_squared_self_test(0, ctypes.byref(abs_error), ctypes.byref(worst),
+                                                     ctypes.byref(err)), err)
+    print("sin_squared: max abs error", abs_error.value, "max ulp", worst.value)
+    assert abs_error.value < 2.0 ** -22
+    assert worst.value <= 4
+
+
 # ------------------------------------------------------------ element-wise
 
 
