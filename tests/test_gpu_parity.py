@@ -307,6 +307,28 @@ def test_gated_silu_16_bit_across_gate_range(m3, ref, oracle, gpu, dtype):
     assert ulp_distance(mine[~both_nan], theirs[~both_nan]).max() <= 1
 
 
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+@pytest.mark.parametrize("shape", [(33, 257), (3,), (1, 5)])
+def test_gated_silu_16_bit_ragged(m3, ref, oracle, gpu, dtype, shape):
+    """Element counts that are not a multiple of four: the dedicated 16-bit
+    loop's full blocks and its element-wise tail."""
+    dt = getattr(m3, dtype)
+    enc = {"F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+    rng = np.random.default_rng(sum(shape))
+    g32 = (rng.standard_normal(shape) * 6).astype(np.float32)
+    u32 = rng.standard_normal(shape).astype(np.float32)
+
+    def build(g):
+        a = g.value(m3.INPUT, dt, shape)
+        b = g.value(m3.INPUT, dt, shape)
+        y = g.inferred("GATED_SILU", [a, b], m3.OUTPUT, dt)
+        g.node("GATED_SILU", [a, b], [y])
+        return {"g": a, "u": b}, [y]
+
+    (mine,), (theirs,) = run_both(m3, ref, build, {"g": enc(g32), "u": enc(u32)})
+    assert ulp_distance(mine, theirs).max() <= 1
+
+
 def test_snake_tanh_clamp_absmax(m3, ref, oracle, gpu):
     rng = np.random.default_rng(4)
     x = (rng.standard_normal((2, 24, 1000)) * 0.5).astype(np.float32)
