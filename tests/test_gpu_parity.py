@@ -1115,6 +1115,40 @@ def test_categorical_through_backend_commands(m3, oracle, gpu):
         be.close()
 
 
+def test_wave_interleave_through_backend_copy(m3, gpu):
+    """The WAVE writer's sample layout (src/m3_wav.c:232-276): IEEE float32
+    stereo, frame by frame the left sample's bits then the right's.  From the
+    assembled planar [1, 2, N] signal that is one COPY whose input view walks
+    frames with a 4-byte stride and channels with a 4N-byte stride, into a
+    contiguous [N, 2] tensor: bit for bit, NaN payloads included."""
+    rng = np.random.default_rng(67)
+    n = 1001                                   # not a multiple of the vector width
+    planar = rng.uniform(-1.0, 1.0, (1, 2, n)).astype(np.float32)
+    planar[0, 0, 3] = np.float32(-0.0)
+    planar[0, 1, 4] = np.uint32(0x7FC0BEEF).view(np.float32)
+    planar[0, 0, 5] = np.float32(1e-42)
+    planar[0, 1, 6] = np.float32(np.inf)
+    be = _Backend(m3)
+    try:
+        k_planar = be.tensor(planar)
+        k_wave = be.tensor(np.zeros((n, 2), np.float32))
+        src = be.view(k_planar, (n, 2))
+        src.byte_strides[0] = 4                # next frame
+        src.byte_strides[1] = 4 * n            # next channel plane
+        dst = be.view(k_wave, (n, 2))
+        cmd = (m3.Command * 1)()
+        cmd[0].kind = m3.OPS["COPY"]
+        cmd[0].descriptor.copy.input = be.ctypes.pointer(src)
+        cmd[0].descriptor.copy.output = be.ctypes.pointer(dst)
+        status = be.lib.m3_cuda_backend_execute(be.context, cmd, 1, None, be.ctypes.byref(be.err))
+        assert status == m3.OK
+        got = be.read(k_wave, 2 * n).view(np.uint32)
+        want = np.stack([planar[0, 0], planar[0, 1]], axis=1).reshape(-1).view(np.uint32)
+        assert np.array_equal(got, want)
+    finally:
+        be.close()
+
+
 def test_waveform_assembly_through_backend_commands(m3, gpu):
     """Waveform assembly's per-channel crop-and-clamp copy
     (src/m3_waveform.c:360-450) as CLAMP_UNIT commands on views: two decoded
