@@ -244,9 +244,8 @@ __device__ __forceinline__ float ordered_sum_f32(const float *row, int width)
 // Plain widening for the ordered sums: a NaN anywhere makes the sum NaN
 // whatever its payload, so the hardware conversion is enough here.
 template <int EB>
-__device__ __forceinline__ void sum_vector(const unsigned char *row, int v, int dtype, float (&x)[16 / EB])
+__device__ __forceinline__ void sum_vector_value(const uint4 &q, int dtype, float (&x)[16 / EB])
 {
-    const uint4 q = reinterpret_cast<const uint4 *>(row)[v];
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     if (EB == 4) {
 #pragma unroll
@@ -262,6 +261,12 @@ __device__ __forceinline__ void sum_vector(const unsigned char *row, int v, int 
     }
 }
 
+template <int EB>
+__device__ __forceinline__ void sum_vector(const unsigned char *row, int v, int dtype, float (&x)[16 / EB])
+{
+    sum_vector_value<EB>(reinterpret_cast<const uint4 *>(row)[v], dtype, x);
+}
+
 // Ordered sums over a raw row: KIND 0 sum of x, 1 sum of x*x, 2 sum of
 // (x - mean)^2, each product and difference rounded to F32 on its own (the
 // statements of src/m3_op_execute_dense.c:128-140 and :175-191).  For F16 the
@@ -271,23 +276,39 @@ template <int EB, int KIND>
 __device__ __forceinline__ float ordered_raw(const unsigned char *row, int nvec, int dtype, float mean)
 {
     constexpr int EPV = 16 / EB;
+    constexpr int AHEAD = 2;  // vectors loaded while the chain runs over the current ones
+    const uint4 *v4 = reinterpret_cast<const uint4 *>(row);
     float s = 0.0f;
     const bool exact_squares = EB == 2 && dtype == M3C_F16;
-#pragma unroll 2
-    for (int v = 0; v < nvec; ++v) {
-        float x[EPV];
-        sum_vector<EB>(row, v, dtype, x);
+    uint4 cur[AHEAD];
 #pragma unroll
-        for (int t = 0; t < EPV; ++t) {
-            if (KIND == 0) {
-                s = __fadd_rn(s, x[t]);
-            } else if (KIND == 1) {
-                s = exact_squares ? __fmaf_rn(x[t], x[t], s) : __fadd_rn(s, __fmul_rn(x[t], x[t]));
-            } else {
-                const float c = __fsub_rn(x[t], mean);
-                s = __fadd_rn(s, __fmul_rn(c, c));
+    for (int k = 0; k < AHEAD; ++k) cur[k] = k < nvec ? v4[k] : make_uint4(0u, 0u, 0u, 0u);
+    for (int v = 0; v < nvec; v += AHEAD) {
+        uint4 next[AHEAD];
+#pragma unroll
+        for (int k = 0; k < AHEAD; ++k) {
+            next[k] = v + AHEAD + k < nvec ? v4[v + AHEAD + k] : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < AHEAD; ++k) {
+            if (v + k < nvec) {
+                float x[EPV];
+                sum_vector_value<EB>(cur[k], dtype, x);
+#pragma unroll
+                for (int t = 0; t < EPV; ++t) {
+                    if (KIND == 0) {
+                        s = __fadd_rn(s, x[t]);
+                    } else if (KIND == 1) {
+                        s = exact_squares ? __fmaf_rn(x[t], x[t], s) : __fadd_rn(s, __fmul_rn(x[t], x[t]));
+                    } else {
+                        const float c = __fsub_rn(x[t], mean);
+                        s = __fadd_rn(s, __fmul_rn(c, c));
+                    }
+                }
             }
         }
+#pragma unroll
+        for (int k = 0; k < AHEAD; ++k) cur[k] = next[k];
     }
     return s;
 }
