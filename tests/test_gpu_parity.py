@@ -1001,7 +1001,8 @@ def _categorical_inputs(dtype_name, oracle, rows=37, vocab=1000, seed=41):
     probs[4] = 0.0
     probs[4, 17] = 0.25                      # one positive entry
     probs[6, -1] = 0.0                       # last positive is not the last
-    uniforms = rng.random(rows).astype(np.float32)
+    # at most 0.99, so rounding to a 16-bit dtype cannot reach 1.0
+    uniforms = np.minimum(rng.random(rows), 0.99).astype(np.float32)
     uniforms[0] = 0.0
     uniforms[1] = (np.nextafter(np.float32(1.0), np.float32(0.0)) if dtype_name == "F32"
                    else np.float32(0.99609375))  # largest below one in the dtype
@@ -1017,12 +1018,15 @@ def _categorical_graph(m3, g, dt, rows, vocab):
     return {"p": p, "u": u}, [i]
 
 
+@pytest.mark.parametrize("vocab", [1000, 1024])
 @pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
-def test_categorical_matches_reference(m3, ref, oracle, gpu, dtype):
+def test_categorical_matches_reference(m3, ref, oracle, gpu, dtype, vocab):
     """Categorical sampling (src/m3_op_execute_sampling.c:90-137): the same
     index as the reference CPU provider for every row, including a zero
-    uniform, the largest uniform below one and rows with few positives."""
-    probs, uniforms = _categorical_inputs(dtype, oracle)
+    uniform, the largest uniform below one and rows with few positives.
+    Rows of whole 128-byte chunks (vocab 1024) take the warp-group kernel,
+    others the thread-per-row kernel."""
+    probs, uniforms = _categorical_inputs(dtype, oracle, vocab=vocab)
     dt = getattr(m3, dtype)
     (mine,), (theirs,) = run_both(
         m3, ref, lambda g: _categorical_graph(m3, g, dt, *probs.shape),
@@ -1030,10 +1034,27 @@ def test_categorical_matches_reference(m3, ref, oracle, gpu, dtype):
     assert np.array_equal(mine, theirs)
 
 
-def test_categorical_checks_match_reference(m3, ref, oracle, gpu):
+@pytest.mark.parametrize("dtype,rows,vocab", [("F32", 20000, 1024), ("F16", 3000, 2048),
+                                              ("BF16", 45, 4096), ("F32", 70, 2048),
+                                              ("F32", 50, 1001), ("F32", 9, 3000)])
+def test_categorical_shapes_match_reference(m3, ref, oracle, gpu, dtype, rows, vocab):
+    """Warp groups of 32 rows over 128-byte chunks (rows of 2 to 8 KiB, a
+    ragged last group), and widths that are not whole chunks or exceed
+    8 KiB (read straight from global memory): the reference's index for
+    every row."""
+    probs, uniforms = _categorical_inputs(dtype, oracle, rows=rows, vocab=vocab, seed=rows + vocab)
+    dt = getattr(m3, dtype)
+    (mine,), (theirs,) = run_both(
+        m3, ref, lambda g: _categorical_graph(m3, g, dt, *probs.shape),
+        {"p": probs, "u": uniforms})
+    assert np.array_equal(mine, theirs)
+
+
+@pytest.mark.parametrize("vocab", [1000, 1024])
+def test_categorical_checks_match_reference(m3, ref, oracle, gpu, vocab):
     """Each failing check fails the run with the reference's message, picks
     the failure of the earliest row, and leaves the output untouched."""
-    probs, uniforms = _categorical_inputs("F32", oracle)
+    probs, uniforms = _categorical_inputs("F32", oracle, vocab=vocab)
     rows, vocab = probs.shape
     g = m3.Graph()
     handles, (out,) = _categorical_graph(m3, g, m3.F32, rows, vocab)
