@@ -637,6 +637,39 @@ def test_softmax_nan_leaves_outputs_untouched(m3, gpu):
 
 
 @pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+@pytest.mark.parametrize("rows,width", [(70, 1024), (33, 64), (5, 4096)])
+@pytest.mark.parametrize("residual", ["none", "temporary"])
+def test_rms_norm_row_groups_bit_exact(m3, ref, oracle, gpu, dtype, rows, width, residual):
+    """RMSNorm without a residual (the lane-per-row kernel reads the input
+    twice) and with a residual sum that is not an output (the row-tile
+    kernel), over ragged row counts: bit-exact against the reference."""
+    dt = getattr(m3, dtype)
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+    rng = np.random.default_rng(rows * width)
+    h = enc(rng.standard_normal((rows, width)).astype(np.float32))
+    r = enc(rng.standard_normal((rows, width)).astype(np.float32))
+    w = enc(rng.normal(1, 0.05, width).astype(np.float32))
+
+    def build(g):
+        vh = g.value(m3.INPUT, dt, h.shape)
+        vw = g.constant(dt, w)
+        handles = {"h": vh}
+        x = vh
+        if residual == "temporary":
+            vr = g.value(m3.INPUT, dt, r.shape)
+            handles["r"] = vr
+            x = g.inferred("ADD", [vh, vr], m3.TEMPORARY, dt)
+            g.node("ADD", [vh, vr], [x])
+        n = g.inferred("RMS_NORM", [x, vw], m3.OUTPUT, dt, epsilon=1e-6)
+        g.node("RMS_NORM", [x, vw], [n], epsilon=1e-6)
+        return handles, [n]
+
+    inputs = {"h": h, "r": r}
+    (mine,), (theirs,) = run_both(m3, ref, build, inputs)
+    assert np.array_equal(bits(mine), bits(theirs))
+
+
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
 @pytest.mark.parametrize("width", [5, 64, 2048, 3000])
 def test_residual_rms_norm_bit_exact(m3, ref, oracle, gpu, dtype, width):
     dt = getattr(m3, dtype)
