@@ -44,7 +44,7 @@ namespace m3c {
 namespace {
 
 constexpr int VEC = 4;
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;
 constexpr int REGS = M3C_EW_MAX_REGS;
 
 struct RegisterFile {
