@@ -1,23 +1,34 @@
 """Benchmark of the CUDA provider on BASELINE.json's configurations.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5]
     python bench.py --impl reference ...      # the reference CPU provider
 
-Default workload: configs[1] of BASELINE.json, softmax + row max/argmax
-(TOP_K k=1) over F32 [32768,1024], logits N(0,3^2) with 1% set to +20, as
-one m3 graph (SOFTMAX and TOP_K of one input).  One step = one session run
-over one batch.  Multi-GPU runs shard by independent batches (rows) with no
-data-path collective: every rank runs a full batch ("weak" scaling) and
-`value` is the whole-job throughput.  --config c1..c5 select the other
-configurations (c5 all-reduces its abs-max across ranks with NCCL).
+Headline workload (`--config`, default c5): BASELINE.json's largest
+configuration, the vocoder activation on stereo F32 [2,512,1572864] (snake,
+global abs-max, clamp), 12.9 GB per run.  Every other configuration (c1-c4)
+is measured the same way in the same run and reported under `per_config`,
+each with its own value, roofline, CPU baseline and end-to-end figure.
+
+One step = one session run over one batch (C4: its 30 carried Euler runs).
+With N ranks (torchrun, one process per GPU) every configuration's FIXED
+tensor is split N ways by the library's sharding layer
+(m3_cuda_shard_session_create): rows for C1-C3, the time axis for C4 and C5,
+one arena per GPU, constants replicated; C5's global abs-max is one NCCL
+all-reduce issued by the library on the session's stream.  Scaling is
+"strong": `value` = the whole tensor's algorithmic bytes / the slowest
+rank's step time.
 
 Metric: achieved HBM GB/s = algorithmic bytes (each input read once, each
-graph output written once) / device time.  Inputs are generated on the device
-from the reference's seeded PCG32 streams and are resident in HBM before the
-timed region; a 256 MiB buffer is overwritten between timed steps so no step
-starts from a warm L2.  `e2e` repeats the measurement through the public C
-API with host buffers: pinned host -> device input writes, the run, and
-device -> pinned host output reads inside the timed region.
+graph output written once) / device time, inputs resident in HBM, L2 evicted
+between timed steps.  `e2e` is the same metric through the public C API with
+pinned host buffers: every step uploads its inputs and downloads its outputs
+inside the timed region.
+
+The reference arm (--impl reference) runs the reference's own CPU provider
+(oracle/_ref/libm3ref.so, compiled from the reference sources) on all host
+threads over bounded samples of the same workloads.  Its inputs come from the
+reference's RNG (m3_rng_normal_f32_fill) and the restated PCG32 word stream of
+oracle/; the product library is never loaded in that process.
 """
 
 from __future__ import annotations
@@ -49,6 +60,8 @@ def _module(name: str, path: str):
 
 
 def m3mod():
+    """The ctypes binding (m3.c_b200/m3cuda.py).  Importing it loads nothing;
+    only `load()` maps libm3cuda.so."""
     return _module("m3cuda", os.path.join(ROOT, "m3.c_b200", "m3cuda.py"))
 
 
@@ -60,28 +73,82 @@ def shardsmod():
     return _module("m3_shards", os.path.join(ROOT, "m3.c_b200", "shards.py"))
 
 
-# this process's rank: its input slab is drawn from its own PCG32 streams
-RANK = int(os.environ.get("RANK", "0"))
-
-
 METRIC = ("achieved HBM GB/s (fraction of B200 peak) per op; "
           "elems/s at 1/2/4/8 GPUs vs CPU")
+L2_NOTE = "256 MiB buffer written, then another 256 MiB read, between timed steps"
+
+F32, F16, BF16 = 0, 1, 2
+
+
+# ----------------------------------------------------------------- RNGs
+
+class ProductRng:
+    """Seeded inputs from libm3cuda.so's restatement of the reference RNG."""
+
+    def __init__(self, m3):
+        self.m3 = m3
+
+    def uniform(self, seed, sequence, low, high, count):
+        return self.m3.fill_uniform(seed, sequence, low, high, count)
+
+    def normal(self, seed, sequence, mean, deviation, count):
+        return self.m3.fill_normal(seed, sequence, mean, deviation, count)
+
+
+class _RefRng(ctypes.Structure):
+    # src/m3_rng.h:10-15
+    _fields_ = [("state", ctypes.c_uint64), ("increment", ctypes.c_uint64),
+                ("spare_normal", ctypes.c_float), ("has_spare_normal", ctypes.c_bool)]
+
+
+class ReferenceRng:
+    """Seeded inputs from the reference itself: m3_rng_seed and
+    m3_rng_normal_f32_fill of libm3ref.so (src/m3_rng.c:22-110) for normals,
+    the restated PCG32 word stream (oracle/, pinned against m3_rng_u32) for
+    uniforms.  mean + deviation * z and low + (high - low) * u are separate
+    F32 statements, as in the product's fills."""
+
+    def __init__(self, reference_lib, oracle):
+        self.lib = reference_lib
+        self.oracle = oracle
+
+    def uniform(self, seed, sequence, low, high, count):
+        return self.oracle.uniform(seed, sequence, low, high, count)
+
+    def normal(self, seed, sequence, mean, deviation, count):
+        rng = _RefRng()
+        err = (ctypes.c_char * 264)()
+        out = np.empty(count, dtype=np.float32)
+        if self.lib.m3_rng_seed(ctypes.byref(rng), ctypes.c_uint64(seed),
+                                ctypes.c_uint64(sequence), err) != 0:
+            raise RuntimeError("m3_rng_seed failed")
+        if self.lib.m3_rng_normal_f32_fill(ctypes.byref(rng), out.ctypes.data_as(ctypes.c_void_p),
+                                           ctypes.c_size_t(count), err) != 0:
+            raise RuntimeError("m3_rng_normal_f32_fill failed")
+        scaled = (np.float32(deviation) * out).astype(np.float32)
+        return (np.float32(mean) + scaled).astype(np.float32)
 
 
 # ---------------------------------------------------------------- configs
 
 class Config:
-    """One benchmark graph: builder, seeded inputs, algorithmic bytes."""
+    """One benchmark graph: builder, seeded inputs, algorithmic bytes.
+
+    `scale` shrinks the configuration along its shard axis (rows, or time
+    for C4/C5): CPU samples and profiling cases use it; reported GPU
+    numbers use 1.0."""
 
     name = ""
     workload = ""
     dtype = "f32"
     runs_per_step = 1
+    shard_axis = 0
+    shard_axis_name = "rows"
 
-    def build(self, m3, g, scale: float = 1.0):  # -> (inputs {name: vid}, outputs [vid])
+    def build(self, m3, g, rng, scale: float = 1.0):  # -> ({name: vid}, [vid])
         raise NotImplementedError
 
-    def inputs_host(self, m3, oracle, scale: float = 1.0):  # -> {name: ndarray}
+    def inputs_host(self, rng, scale: float = 1.0):  # -> {name: ndarray}
         raise NotImplementedError
 
     def algorithmic_bytes(self, scale: float = 1.0) -> int:
@@ -91,18 +158,63 @@ class Config:
         raise NotImplementedError
 
 
+def _rows(full, scale):
+    return max(1, int(round(full * scale)))
+
+
+def _length(full, scale):
+    return max(4, int(full * scale) // 4 * 4)
+
+
+class C1(Config):
+    name = "c1"
+    workload = "y = (x * c) + b F32 [1024,4096], c [4096] / b [1,4096] constants, seed 0"
+    rows, width = 1024, 4096
+
+    def shape(self, scale=1.0):
+        return (_rows(self.rows, scale), self.width)
+
+    def build(self, m3, g, rng, scale=1.0):
+        c = rng.uniform(0, 1, 0.5, 2.0, self.width)
+        b = rng.normal(0, 2, 0.0, 1.0, self.width).reshape(1, self.width)
+        x = g.value(m3.INPUT, m3.F32, self.shape(scale))
+        vc = g.constant(m3.F32, c)
+        vb = g.constant(m3.F32, b)
+        t = g.inferred("MUL", [x, vc], m3.TEMPORARY, m3.F32)
+        g.node("MUL", [x, vc], [t])
+        y = g.inferred("ADD", [t, vb], m3.OUTPUT, m3.F32)
+        g.node("ADD", [t, vb], [y])
+        return {"x": x}, [y]
+
+    def inputs_host(self, rng, scale=1.0):
+        shape = self.shape(scale)
+        return {"x": rng.uniform(0, 0, -1.0, 1.0, shape[0] * shape[1]).reshape(shape)}
+
+    def inputs_device(self, m3, torch, device, scale=1.0):
+        shape = self.shape(scale)
+        x = torch.empty(shape[0] * shape[1], dtype=torch.float32, device=device)
+        fill(m3, "uniform", 0, 0, -1.0, 1.0, x, torch.cuda.current_stream(device).cuda_stream)
+        return {"x": x.view(shape)}
+
+    def algorithmic_bytes(self, scale=1.0):
+        rows = self.shape(scale)[0]
+        return rows * self.width * 8 + 2 * self.width * 4
+
+    def elements(self, scale=1.0):
+        return self.shape(scale)[0] * self.width
+
+
 class C2(Config):
     name = "c2"
     workload = ("softmax + row max/argmax (TOP_K k=1) F32 [32768,1024], "
                 "N(0,3^2) logits with 1% = +20, seed 1")
     rows, width = 32768, 1024
 
-    def shape(self, scale):
-        return (max(1, int(self.rows * scale)), self.width)
+    def shape(self, scale=1.0):
+        return (_rows(self.rows, scale), self.width)
 
-    def build(self, m3, g, scale=1.0):
-        shape = self.shape(scale)
-        x = g.value(m3.INPUT, m3.F32, shape)
+    def build(self, m3, g, rng, scale=1.0):
+        x = g.value(m3.INPUT, m3.F32, self.shape(scale))
         p = g.inferred("SOFTMAX", [x], m3.OUTPUT, m3.F32)
         g.node("SOFTMAX", [x], [p])
         v = g.inferred("TOP_K", [x], m3.OUTPUT, m3.F32, 0, k=1)
@@ -110,12 +222,11 @@ class C2(Config):
         g.node("TOP_K", [x], [v, i], k=1)
         return {"x": x}, [p, v, i]
 
-    def inputs_host(self, m3, oracle, scale=1.0):
+    def inputs_host(self, rng, scale=1.0):
         shape = self.shape(scale)
         n = shape[0] * shape[1]
-        x = m3.fill_normal(1, 0, 0.0, 3.0, n)
-        spikes = m3.fill_uniform(1, 1, 0.0, 1.0, n) < 0.01
-        x[spikes] = 20.0
+        x = rng.normal(1, 0, 0.0, 3.0, n)
+        x[rng.uniform(1, 1, 0.0, 1.0, n) < 0.01] = 20.0
         return {"x": x.reshape(shape)}
 
     def inputs_device(self, m3, torch, device, scale=1.0):
@@ -138,42 +249,6 @@ class C2(Config):
         return rows * width
 
 
-class C1(Config):
-    name = "c1"
-    workload = "y = (x * c) + b F32 [1024,4096], c [4096] / b [1,4096] constants, seed 0"
-    rows, width = 1024, 4096
-
-    def build(self, m3, g, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        c = m3.fill_uniform(0, 1, 0.5, 2.0, self.width)
-        b = m3.fill_normal(0, 2, 0.0, 1.0, self.width).reshape(1, self.width)
-        x = g.value(m3.INPUT, m3.F32, (rows, self.width))
-        vc = g.constant(m3.F32, c)
-        vb = g.constant(m3.F32, b)
-        t = g.inferred("MUL", [x, vc], m3.TEMPORARY, m3.F32)
-        g.node("MUL", [x, vc], [t])
-        y = g.inferred("ADD", [t, vb], m3.OUTPUT, m3.F32)
-        g.node("ADD", [t, vb], [y])
-        return {"x": x}, [y]
-
-    def inputs_host(self, m3, oracle, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        return {"x": m3.fill_uniform(0, 0, -1.0, 1.0, rows * self.width).reshape(rows, self.width)}
-
-    def inputs_device(self, m3, torch, device, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        x = torch.empty(rows * self.width, dtype=torch.float32, device=device)
-        fill(m3, "uniform", 0, 0, -1.0, 1.0, x, torch.cuda.current_stream(device).cuda_stream)
-        return {"x": x.view(rows, self.width)}
-
-    def algorithmic_bytes(self, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        return rows * self.width * 8 + 2 * self.width * 4
-
-    def elements(self, scale=1.0):
-        return max(1, int(self.rows * scale)) * self.width
-
-
 class C3(Config):
     name = "c3"
     dtype = "f16"
@@ -181,9 +256,14 @@ class C3(Config):
                 "and SiLU(gate)*up [8192,5632], seed 2")
     rows, width, ffn = 8192, 2048, 5632
 
-    def build(self, m3, g, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        w = f16_bits(m3.fill_normal(2, 2, 1.0, 0.05, self.width))
+    def _sizes(self, scale):
+        rows = _rows(self.rows, scale)
+        return {"h": (rows, self.width, 0), "r": (rows, self.width, 1),
+                "gate": (rows, self.ffn, 3), "up": (rows, self.ffn, 4)}
+
+    def build(self, m3, g, rng, scale=1.0):
+        rows = _rows(self.rows, scale)
+        w = f16_bits(rng.normal(2, 2, 1.0, 0.05, self.width))
         h = g.value(m3.INPUT, m3.F16, (rows, self.width))
         r = g.value(m3.INPUT, m3.F16, (rows, self.width))
         vw = g.constant(m3.F16, w)
@@ -197,15 +277,10 @@ class C3(Config):
         g.node("GATED_SILU", [gate, up], [y])
         return {"h": h, "r": r, "gate": gate, "up": up}, [s, n, y]
 
-    def _sizes(self, scale):
-        rows = max(1, int(self.rows * scale))
-        return {"h": (rows, self.width, 0), "r": (rows, self.width, 1),
-                "gate": (rows, self.ffn, 3), "up": (rows, self.ffn, 4)}
-
-    def inputs_host(self, m3, oracle, scale=1.0):
+    def inputs_host(self, rng, scale=1.0):
         out = {}
         for name, (rows, cols, seq) in self._sizes(scale).items():
-            out[name] = f16_bits(m3.fill_normal(2, seq, 0.0, 1.0, rows * cols)).reshape(rows, cols)
+            out[name] = f16_bits(rng.normal(2, seq, 0.0, 1.0, rows * cols)).reshape(rows, cols)
         return out
 
     def inputs_device(self, m3, torch, device, scale=1.0):
@@ -219,23 +294,27 @@ class C3(Config):
         return out
 
     def algorithmic_bytes(self, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        return (rows * self.width * 2 * 4 + self.width * 2 + rows * self.ffn * 2 * 3)
+        rows = _rows(self.rows, scale)
+        return rows * self.width * 2 * 4 + self.width * 2 + rows * self.ffn * 2 * 3
 
     def elements(self, scale=1.0):
-        rows = max(1, int(self.rows * scale))
-        return rows * (self.width + self.ffn)
+        return _rows(self.rows, scale) * (self.width + self.ffn)
 
 
 class C4(Config):
     name = "c4"
     workload = ("flow-matching CFG + Euler step, F32 [2,64,8192], g = 4, dt = 1/30, "
                 "then BF16 cast; 30 steps carried on device; seed 3")
-    shape3 = (2, 64, 8192)
+    batch, channels, length = 2, 64, 8192
     runs_per_step = 30
+    shard_axis = 2
+    shard_axis_name = "time"
 
-    def build(self, m3, g, scale=1.0):
-        shape = self.shape3
+    def shape(self, scale=1.0):
+        return (self.batch, self.channels, _length(self.length, scale))
+
+    def build(self, m3, g, rng, scale=1.0):
+        shape = self.shape(scale)
         x = g.value(m3.INPUT, m3.F32, shape)
         vc = g.value(m3.INPUT, m3.F32, shape)
         vu = g.value(m3.INPUT, m3.F32, shape)
@@ -259,40 +338,45 @@ class C4(Config):
         self.carry = (x, xn)
         return {"x": x, "vc": vc, "vu": vu}, [xn, xb]
 
-    def inputs_host(self, m3, oracle, scale=1.0):
-        n = int(np.prod(self.shape3))
-        return {name: m3.fill_normal(3, seq, 0.0, 1.0, n).reshape(self.shape3)
+    def inputs_host(self, rng, scale=1.0):
+        shape = self.shape(scale)
+        n = int(np.prod(shape))
+        return {name: rng.normal(3, seq, 0.0, 1.0, n).reshape(shape)
                 for seq, name in enumerate(("x", "vc", "vu"))}
 
     def inputs_device(self, m3, torch, device, scale=1.0):
-        n = int(np.prod(self.shape3))
+        shape = self.shape(scale)
+        n = int(np.prod(shape))
         stream = torch.cuda.current_stream(device).cuda_stream
         out = {}
         for seq, name in enumerate(("x", "vc", "vu")):
             t = torch.empty(n, dtype=torch.float32, device=device)
             fill(m3, "normal", 3, seq, 0.0, 1.0, t, stream)
-            out[name] = t.view(self.shape3)
+            out[name] = t.view(shape)
         return out
 
     def algorithmic_bytes(self, scale=1.0):
-        n = int(np.prod(self.shape3))
+        n = int(np.prod(self.shape(scale)))
         return 30 * (n * 4 * 3 + n * 4 + n * 2)
 
     def elements(self, scale=1.0):
-        return 30 * int(np.prod(self.shape3))
+        return 30 * int(np.prod(self.shape(scale)))
 
 
 class C5(Config):
     name = "c5"
     workload = ("snake x + sin^2(a x)/a on stereo F32 [2,512,1572864], a U[0.2,2], "
-                "x N(0,0.5); global abs-max (NCCL all-reduce across ranks) and clamp "
-                "to [-1,1]; seed 4")
+                "x N(0,0.5); global abs-max and clamp to [-1,1]; seed 4")
     batch, channels, length = 2, 512, 1572864
+    shard_axis = 2
+    shard_axis_name = "time"
 
-    def build(self, m3, g, scale=1.0):
-        length = max(4, int(self.length * scale) // 4 * 4)
-        alpha = m3.fill_uniform(4, 1, 0.2, 2.0, self.channels).reshape(1, self.channels, 1)
-        x = g.value(m3.INPUT, m3.F32, (self.batch, self.channels, length))
+    def shape(self, scale=1.0):
+        return (self.batch, self.channels, _length(self.length, scale))
+
+    def build(self, m3, g, rng, scale=1.0):
+        alpha = rng.uniform(4, 1, 0.2, 2.0, self.channels).reshape(1, self.channels, 1)
+        x = g.value(m3.INPUT, m3.F32, self.shape(scale))
         va = g.constant(m3.F32, alpha)
         z = g.inferred("SNAKE1D", [x, va], m3.TEMPORARY, m3.F32)
         g.node("SNAKE1D", [x, va], [z])
@@ -302,29 +386,36 @@ class C5(Config):
         g.node("CLAMP_UNIT", [z], [y])
         return {"x": x}, [m, y]
 
-    def _length(self, scale):
-        return max(4, int(self.length * scale) // 4 * 4)
-
-    def inputs_host(self, m3, oracle, scale=1.0):
-        n = self.batch * self.channels * self._length(scale)
-        return {"x": m3.fill_normal(4, 0, 0.0, 0.5, n).reshape(
-            self.batch, self.channels, self._length(scale))}
+    def inputs_host(self, rng, scale=1.0):
+        shape = self.shape(scale)
+        return {"x": rng.normal(4, 0, 0.0, 0.5, int(np.prod(shape))).reshape(shape)}
 
     def inputs_device(self, m3, torch, device, scale=1.0):
-        n = self.batch * self.channels * self._length(scale)
-        x = torch.empty(n, dtype=torch.float32, device=device)
+        shape = self.shape(scale)
+        x = torch.empty(int(np.prod(shape)), dtype=torch.float32, device=device)
         fill(m3, "normal", 4, 0, 0.0, 0.5, x, torch.cuda.current_stream(device).cuda_stream)
-        return {"x": x.view(self.batch, self.channels, self._length(scale))}
+        return {"x": x.view(shape)}
 
     def algorithmic_bytes(self, scale=1.0):
-        n = self.batch * self.channels * self._length(scale)
+        n = int(np.prod(self.shape(scale)))
         return n * 8 + self.channels * 4 + 4
 
     def elements(self, scale=1.0):
-        return self.batch * self.channels * self._length(scale)
+        return int(np.prod(self.shape(scale)))
 
 
 CONFIGS = {c.name: c for c in (C1(), C2(), C3(), C4(), C5())}
+
+
+def config_dict(cfg, world: int) -> dict:
+    """The `config` object of both arms' JSON lines (identical by design)."""
+    return {"workload": cfg.workload, "name": cfg.name, "scale": 1.0,
+            "shards": world, "shard_axis": cfg.shard_axis_name,
+            "split": "one fixed tensor split across the ranks (strong scaling)",
+            "l2": L2_NOTE,
+            "parallelism": (f"{world}-way {cfg.shard_axis_name} shards" +
+                            (", NCCL all-reduce(max) of the abs-max" if cfg.name == "c5" else
+                             ", no data-path collective"))}
 
 
 # ------------------------------------------------------------- helpers
@@ -362,12 +453,11 @@ def f16_bits(values: np.ndarray) -> np.ndarray:
 
 
 def fill(m3, kind, seed, sequence, a, b, tensor, stream):
-    """Device fill from the reference RNG; rank r > 0 draws its slab from the
-    rank's own streams (rank 0 uses the configuration's streams)."""
+    """Device fill from the restated reference RNG (the configuration's own
+    streams: every rank generates the same global tensor)."""
     lib = m3.load()
     err = m3.M3Error()
     fn = lib.m3_cuda_fill_normal_device if kind == "normal" else lib.m3_cuda_fill_uniform_device
-    sequence = shardsmod().shard_sequence(sequence, RANK)
     m3.check(fn(seed, sequence, a, b, ctypes.c_void_p(tensor.data_ptr()), tensor.numel(),
                 ctypes.c_void_p(stream), ctypes.byref(err)), err)
 
@@ -400,7 +490,8 @@ def measured_peaks():
 
 def ncu_traffic(config_name: str):
     """Per-launch DRAM bytes of the dominant kernel from a committed ncu
-    summary (profiles/ncu_traffic.json), or None."""
+    summary (profiles/ncu_traffic.json): cold-cache figures of one captured
+    launch, scaled to a full launch where the capture ran a scaled case."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if not os.path.exists(path):
         return None
@@ -464,57 +555,79 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ------------------------------------------------------- reference arm
+# ----------------------------------------------------- reference timing
 
-def reference_seconds_per_run(m3, oracle, config, scale, threads):
-    """Run the reference CPU provider on `threads` independent row shards in
-    parallel threads (ctypes releases the GIL); returns seconds per run of
-    the scaled workload."""
-    lib = m3.bind(oracle.reference(), cuda=False)
+def reference_sessions(m3, lib, rng, config, scale, threads):
+    """`threads` reference CPU-only sessions, each over its own 1/threads
+    slice of the scaled workload along the configuration's shard axis (the
+    data of every slice is the configuration's seeded stream)."""
     sessions = []
     per = scale / threads
-    for t in range(threads):
+    for _ in range(threads):
         g = m3.Graph(lib=lib)
-        handles, outputs = config.build(m3, g, per)
+        handles, _ = config.build(m3, g, rng, per)
         s = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
-        data = config.inputs_host(m3, oracle, per)
+        data = config.inputs_host(rng, per)
         for name, vid in handles.items():
             s.write(vid, data[name])
         sessions.append(s)
+    return sessions
 
-    def run(s, repeat):
-        for _ in range(repeat):
+
+def time_reference(sessions, runs):
+    """Seconds for every session to make `runs` runs, one thread per session
+    (ctypes releases the GIL during each run)."""
+    def work(s):
+        for _ in range(runs):
             s.run()
 
-    run(sessions[0], 1)  # warm
+    workers = [threading.Thread(target=work, args=(s,)) for s in sessions]
     start = time.perf_counter()
-    workers = [threading.Thread(target=run, args=(s, config.runs_per_step)) for s in sessions]
     for w in workers:
         w.start()
     for w in workers:
         w.join()
-    return (time.perf_counter() - start)
+    return time.perf_counter() - start
+
+
+def reference_scale(m3, lib, rng, config, threads, seconds):
+    """Sample scale whose one step takes about `seconds` on `threads`
+    threads (from a 1/64 probe on one thread)."""
+    probe = 1.0 / 64
+    sessions = reference_sessions(m3, lib, rng, config, probe, 1)
+    time_reference(sessions, 1)
+    t = time_reference(sessions, config.runs_per_step)
+    for s in sessions:
+        s.close()
+    scale = probe * seconds * threads / max(t, 1e-6)
+    return float(min(1.0, max(probe, scale)))
 
 
 def cpu_baseline(m3, oracle, config, budget_seconds):
     """Single-core reference CPU provider on a bounded sample (rank 0, N=1)."""
     if not oracle.reference_available():
         return None
-    probe = 1.0 / 64
-    t = reference_seconds_per_run(m3, oracle, config, probe, 1)
-    scale = min(1.0, max(probe, probe * budget_seconds / max(t, 1e-6) / 3))
-    times = [reference_seconds_per_run(m3, oracle, config, scale, 1) for _ in range(3)]
+    lib = m3.bind(oracle.reference(), cuda=False)
+    rng = ReferenceRng(lib, oracle)
+    scale = reference_scale(m3, lib, rng, config, 1, budget_seconds / 3)
+    sessions = reference_sessions(m3, lib, rng, config, scale, 1)
+    time_reference(sessions, 1)
+    times = [time_reference(sessions, config.runs_per_step) for _ in range(3)]
+    for s in sessions:
+        s.close()
     sec = statistics.median(times)
-    value = config.algorithmic_bytes(scale) / sec / 1e9
-    return {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
-            "sample": f"{config.name} at {scale:.4g} of full size (median of 3 runs, "
-                      f"{sec:.2f} s each), reference CPU-only m3_session_run, 1 thread",
+    return {"value": config.algorithmic_bytes(scale) / sec / 1e9, "unit": "GB/s",
+            "cores": 1, "kind": "reference",
+            "sample": f"{config.name} at {scale:.4g} of full size along its "
+                      f"{config.shard_axis_name} axis (median of 3 steps, {sec:.2f} s each), "
+                      "reference CPU-only m3_session_run, 1 thread",
             "elems_per_s": config.elements(scale) / sec}
 
 
-def run_reference_arm(args, config):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+def run_reference_arm(args, headline):
+    """The reference's CPU provider, all host threads, bounded samples of
+    every configuration: one JSON line (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return 0
     m3 = m3mod()
     oracle = oraclemod()
@@ -522,186 +635,56 @@ def run_reference_arm(args, config):
         print(json.dumps({"impl": "reference",
                           "unavailable": "reference CPU library oracle/_ref/libm3ref.so not built"}))
         return 0
+    lib = m3.bind(oracle.reference(), cuda=False)
+    rng = ReferenceRng(lib, oracle)
     threads = max(1, os.cpu_count() or 1)
-    # size each step to a few seconds of CPU time
-    probe = 1.0 / 64
-    t = reference_seconds_per_run(m3, oracle, config, probe, 1)
-    scale = min(1.0, max(probe, probe * 3.0 * threads / max(t, 1e-6)))
-    scale = max(scale, threads * probe / 8)
-    for _ in range(args.warmup):
-        reference_seconds_per_run(m3, oracle, config, scale, threads)
-    times = [reference_seconds_per_run(m3, oracle, config, scale, threads)
-             for _ in range(args.steps)]
-    sec = statistics.mean(times)
-    value = config.algorithmic_bytes(scale) / sec / 1e9
-    sample = (f"{config.name} at {scale:.4g} of full size per step, split into {threads} row "
-              f"shards run by {threads} threads, each its own reference CPU-only session")
-    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+    world = args.gpus
+
+    def measure(config, seconds):
+        scale = reference_scale(m3, lib, rng, config, threads, seconds)
+        sessions = reference_sessions(m3, lib, rng, config, scale, threads)
+        for _ in range(args.warmup):
+            time_reference(sessions, config.runs_per_step)
+        times = [time_reference(sessions, config.runs_per_step) for _ in range(args.steps)]
+        for s in sessions:
+            s.close()
+        sec = statistics.mean(times)
+        value = config.algorithmic_bytes(scale) / sec / 1e9
+        sample = (f"{config.name} at {scale:.4g} of full size along its {config.shard_axis_name} "
+                  f"axis per step, split into {threads} slices run by {threads} threads, each its "
+                  "own reference CPU-only session (libm3ref.so; inputs from the reference RNG)")
+        return value, sec, scale, sample
+
+    value, sec, scale, sample = measure(headline, args.ref_seconds)
+    per_config = {}
+    if not args.no_per_config:
+        for name, config in CONFIGS.items():
+            if name == headline.name:
+                continue
+            v, s, sc, smp = measure(config, args.ref_seconds / 3)
+            per_config[name] = {"workload": config.workload, "value": v, "unit": "GB/s",
+                                "ms_per_step": s * 1e3, "sample_scale": sc,
+                                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads,
+                                                 "kind": "reference", "sample": smp},
+                                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": config.dtype, "data": "synthetic (seeded PCG32, reference RNG)",
-            "impl": "reference",
-            "config": {"workload": config.workload, "sample_scale": scale},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": headline.dtype, "data": "synthetic (seeded PCG32, reference RNG)",
+            "impl": "reference", "config": config_dict(headline, world),
+            "sample_scale": scale, "threads": threads,
             "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads,
                              "kind": "reference", "sample": sample},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "elems_per_s": config.elements(scale) / sec}
+            "elems_per_s": headline.elements(scale) / sec,
+            "per_config": per_config}
     print(json.dumps(line))
     return 0
 
 
 # ------------------------------------------------------------- CUDA arm
-
-def main():
-    parser = argparse.ArgumentParser()
-    parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
-    parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    parser.add_argument("--cpu-seconds", type=float, default=12.0,
-                        help="CPU work budget of the cpu_baseline sample")
-    parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--no-e2e", action="store_true")
-    parser.add_argument("--scale", type=float, default=1.0,
-                        help="fraction of the configuration's size (profiling only; "
-                             "reported numbers use 1.0)")
-    args = parser.parse_args()
-    config = CONFIGS[args.config]
-    if args.warmup < 3:
-        args.warmup = 3
-    if args.impl == "reference":
-        return run_reference_arm(args, config)
-
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=device)
-    m3 = m3mod()
-    lib = m3.load()
-    stream = torch.cuda.Stream(device)
-    torch.cuda.set_stream(stream)
-
-    g = m3.Graph()
-    handles, outputs = config.build(m3, g, args.scale)
-    session = m3.Session(g, device=local, stream=stream.cuda_stream)
-    report, plan_text = session.plan_report()
-    data = config.inputs_device(m3, torch, device, args.scale)
-    host_in = {}
-    for name, vid in handles.items():
-        t = data[name]
-        session.write_device(vid, t.data_ptr(), t.numel() * t.element_size())
-        if not args.no_e2e:
-            pinned = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-            pinned.copy_(t)
-            host_in[vid] = pinned
-    del data
-    torch.cuda.synchronize(device)
-
-    flush = L2Flush(torch, device)
-    collective = None
-    if config.name == "c5" and world > 1:
-        collective = torch.zeros(1, dtype=torch.int32, device=device)
-
-    def one_step():
-        if config.name == "c4":
-            # the 30 Euler steps with x' carried on the device: one call
-            session.run_steps(config.runs_per_step, *config.carry)
-        else:
-            for _ in range(config.runs_per_step):
-                session.run_async()
-        if collective is not None:
-            session.read_device_async(outputs[0], collective.data_ptr(), 4)
-            shardsmod().global_abs_max_bits(collective)
-
-    for _ in range(args.warmup):
-        one_step()
-    session.synchronize()
-    torch.cuda.synchronize(device)
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    sampler = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    sampler.start()
-    time.sleep(0.3)
-    for k in range(args.steps):
-        flush()
-        starts[k].record(stream)
-        one_step()
-        ends[k].record(stream)
-    session.synchronize()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop()
-    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(per_step)
-    if world > 1:
-        total_ms = shardsmod().max_over_ranks(total_ms, device)
-    ms_per_step = total_ms / args.steps
-    bytes_step = config.algorithmic_bytes(args.scale)
-    value = bytes_step * world / (ms_per_step / 1e3) / 1e9
-
-    # dominant kernel: one launch per run for c1/c2/c4/c5; c3's two launches
-    # are timed separately on their own sub-graphs
-    peak, peak_kind = measured_peaks()
-    kernel_ms = ms_per_step / config.runs_per_step
-    kernel_bytes = bytes_step / config.runs_per_step
-    kernel_name = plan_text
-    if config.name == "c3":
-        kernel_ms, kernel_bytes, kernel_name = time_c3_gsilu(m3, torch, device, stream, flush,
-                                                            args.steps)
-    achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": ncu_traffic(config.name),
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
-                "kernel": kernel_name, "algorithmic_bytes_per_launch": kernel_bytes}
-
-    e2e = None
-    if not args.no_e2e:
-        e2e = measure_e2e(m3, torch, device, stream, config, session, handles, outputs,
-                          flush, args, world, host_in)
-
-    baseline = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        baseline = cpu_baseline(m3, oraclemod(), config, args.cpu_seconds)
-
-    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": config.dtype,
-            "data": "synthetic: seeded PCG32 streams of the reference RNG, generated on device",
-            "config": {"workload": config.workload, "per_gpu": "one full batch per rank",
-                       "l2": "256 MiB buffer written, then another 256 MiB read, between timed steps",
-                       "parallelism": f"dp{world}" + (" + NCCL all-reduce(max) of abs-max"
-                                                       if collective is not None else
-                                                       " (independent batches, no collective)"),
-                       "plan": plan_text},
-            "roofline": roofline, "cpu_baseline": baseline, "e2e": e2e,
-            "clocks": clocks,
-            "gpu_launches": report.launch_count * config.runs_per_step * args.steps,
-            "elems_per_s": config.elements(args.scale) * world / (ms_per_step / 1e3)}
-    if args.scale != 1.0:
-        line["config"]["scale"] = args.scale
-    session.close()
-    if world > 1:
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
-    return 0
-
 
 class L2Flush:
     """Evicts every cached line between timed steps: a 256 MiB buffer (twice
@@ -720,15 +703,151 @@ class L2Flush:
         self.sink.copy_(self.read.max())
 
 
-def time_c3_gsilu(m3, torch, device, stream, flush, steps):
-    """C3's dominant kernel (the gated-SiLU launch), timed alone."""
-    c = CONFIGS["c3"]
+class Env:
+    """This process's place in the job (torchrun variables) and its device."""
+
+    def __init__(self, torch):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.device = torch.device("cuda", self.local)
+        self.shard_id = None
+
+
+def make_session(m3, env, g, stream, config):
+    """A plain session at N=1; at N>1 this rank's shard of the fixed graph
+    (the library partitions it along the configuration's shard axis and
+    all-reduces global reductions over NCCL)."""
+    if env.world == 1:
+        return m3.Session(g, device=env.local, stream=stream.cuda_stream)
+    return m3.Session(g, device=env.local, stream=stream.cuda_stream,
+                      shard=m3.ShardOptions(env.rank, env.world, config.shard_axis, env.shard_id))
+
+
+def write_inputs(session, env, handles, data):
+    """Each input's device data into the session: the whole tensor at N=1,
+    this rank's slab of the global tensor (a strided device copy) at N>1."""
+    for name, vid in handles.items():
+        t = data[name]
+        nbytes = t.numel() * t.element_size()
+        if env.world == 1:
+            session.write_device(vid, t.data_ptr(), nbytes)
+        else:
+            session.shard_write(vid, t.data_ptr(), nbytes, device=True)
+
+
+def measure_cuda(m3, torch, dist, env, config, args, stream, flush, with_baseline):
+    """One configuration at its full size on this rank: device-timed steps,
+    the roofline of its dominant kernel, end to end through the C API and
+    (rank 0, N=1) the single-core reference CPU baseline."""
+    rng = ProductRng(m3)
     g = m3.Graph()
-    gate = g.value(m3.INPUT, m3.F16, (c.rows, c.ffn))
-    up = g.value(m3.INPUT, m3.F16, (c.rows, c.ffn))
+    handles, outputs = config.build(m3, g, rng, args.scale)
+    session = make_session(m3, env, g, stream, config)
+    report, plan_text = session.plan_report()
+    data = config.inputs_device(m3, torch, env.device, args.scale)
+    torch.cuda.synchronize(env.device)
+    write_inputs(session, env, handles, data)
+    host_in = {}
+    if not args.no_e2e:
+        # pinned host copies of this rank's inputs for the end-to-end leg
+        for name, vid in handles.items():
+            t = data[name]
+            if env.world > 1:
+                slab = session.shard_slab(vid)
+                if slab.split:
+                    t = t.narrow(slab.axis, slab.begin, slab.extent)
+            pinned = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            pinned.copy_(t)
+            host_in[vid] = pinned
+    del data
+    session.synchronize()
+    torch.cuda.empty_cache()
+
+    def one_step():
+        if config.name == "c4":
+            session.run_steps(config.runs_per_step, *config.carry)
+        else:
+            for _ in range(config.runs_per_step):
+                session.run_async()
+
+    for _ in range(args.warmup):
+        one_step()
+    session.synchronize()
+    torch.cuda.synchronize(env.device)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(env.local)
+    if env.world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(env.device)
+    sampler.start()
+    time.sleep(0.3)
+    for k in range(args.steps):
+        flush()
+        starts[k].record(stream)
+        one_step()
+        ends[k].record(stream)
+    session.synchronize()
+    torch.cuda.synchronize(env.device)
+    if env.world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(per_step)
+    if env.world > 1:
+        total_ms = shardsmod().max_over_ranks(total_ms, env.device)
+    ms_per_step = total_ms / args.steps
+    bytes_step = config.algorithmic_bytes(args.scale)
+    value = bytes_step / (ms_per_step / 1e3) / 1e9
+
+    # the dominant kernel: one launch per run for c1/c2/c4/c5 (C5 at N>1 adds
+    # the all-reduce's launches); c3's gated-SiLU launch timed on its own graph
+    peak, peak_kind = measured_peaks()
+    kernel_ms = ms_per_step / config.runs_per_step
+    kernel_bytes = bytes_step / config.runs_per_step / env.world
+    kernel_name = plan_text
+    if config.name == "c3":
+        kernel_ms, kernel_bytes, kernel_name = time_c3_gsilu(m3, torch, env, stream, flush,
+                                                            args.steps, args.scale)
+    achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": ncu_traffic(config.name) if args.scale == 1.0 and env.world == 1 else None,
+                "peak_source": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                                else "fallback 6650 GB/s"),
+                "kernel": kernel_name, "algorithmic_bytes_per_launch": kernel_bytes,
+                "launch_ms": kernel_ms}
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(m3, torch, dist, env, stream, config, session, host_in, outputs,
+                          flush, args)
+    del host_in
+    baseline = None
+    if with_baseline:
+        baseline = cpu_baseline(m3, oraclemod(), config, args.cpu_seconds)
+    session.close()
+    torch.cuda.empty_cache()
+    return {"workload": config.workload, "value": value, "unit": "GB/s",
+            "ms_per_step": ms_per_step, "dtype": config.dtype, "plan": plan_text,
+            "roofline": roofline, "cpu_baseline": baseline, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": report.launch_count * config.runs_per_step * args.steps,
+            "elems_per_s": config.elements(args.scale) / (ms_per_step / 1e3)}
+
+
+def time_c3_gsilu(m3, torch, env, stream, flush, steps, scale):
+    """C3's dominant kernel (the gated-SiLU launch, this rank's rows), timed
+    alone."""
+    c = CONFIGS["c3"]
+    rows = _rows(c.rows, scale) // env.world
+    g = m3.Graph()
+    gate = g.value(m3.INPUT, m3.F16, (rows, c.ffn))
+    up = g.value(m3.INPUT, m3.F16, (rows, c.ffn))
     y = g.inferred("GATED_SILU", [gate, up], m3.OUTPUT, m3.F16)
     g.node("GATED_SILU", [gate, up], [y])
-    s = m3.Session(g, device=device.index, stream=stream.cuda_stream)
+    s = m3.Session(g, device=env.local, stream=stream.cuda_stream)
     _, text = s.plan_report()
     for _ in range(3):
         s.run_async()
@@ -743,26 +862,23 @@ def time_c3_gsilu(m3, torch, device, stream, flush, steps):
         b.record(stream)
         times.append((a, b))
     s.synchronize()
-    torch.cuda.synchronize(device)
+    torch.cuda.synchronize(env.device)
     ms = statistics.mean(a.elapsed_time(b) for a, b in times)
     s.close()
-    return ms, c.rows * c.ffn * 2 * 3, text
+    return ms, rows * c.ffn * 2 * 3, text
 
 
-def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, flush, args,
-                world, host_in):
-    """The same metric through the public C API with pinned host buffers,
-    every step's host-to-device input copies and device-to-host output
-    copies inside the timed region: single-run configurations submit each
-    step with m3_cuda_session_submit_host_async (steps pipelined, timed from
-    the first submission to the synchronise after the last); C4 writes,
-    runs its 30 carried steps and reads back per step."""
-    import torch.distributed as dist
+def measure_e2e(m3, torch, dist, env, stream, config, session, host_in, outputs, flush, args):
+    """The same metric through the public C API with pinned host buffers of
+    this rank's data, every step's host-to-device input copies and
+    device-to-host output copies inside the timed region: single-run
+    configurations submit each step with m3_cuda_session_submit_host_async
+    (steps pipelined, timed from the first submission to the synchronise
+    after the last); C4 writes, runs its 30 carried steps and reads back per
+    step."""
     host_out = {}
     for vid in outputs:
-        dtype, shape, _ = session.values[vid]
-        nbytes = int(np.prod(shape)) * m3.ITEMSIZE[dtype]
-        host_out[vid] = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        host_out[vid] = torch.empty(session.value_bytes(vid), dtype=torch.uint8, pin_memory=True)
     err = m3.M3Error()
     lib = m3.load()
 
@@ -772,14 +888,9 @@ def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, fl
     def one():
         for vid, buf in host_in.items():
             call(lib.m3_session_write_input, vid, ctypes.c_void_p(buf.data_ptr()), buf.nbytes)
-        if config.name == "c4":
-            # x' carried on the device between the 30 runs
-            x_in, x_out = config.carry
-            call(lib.m3_cuda_session_run_steps_async, config.runs_per_step, x_in, x_out)
-            call(lib.m3_cuda_session_synchronize)
-        else:
-            for _ in range(config.runs_per_step):
-                call(lib.m3_session_run)
+        x_in, x_out = config.carry
+        call(lib.m3_cuda_session_run_steps_async, config.runs_per_step, x_in, x_out)
+        call(lib.m3_cuda_session_synchronize)
         for vid, buf in host_out.items():
             call(lib.m3_session_read_output, vid, ctypes.c_void_p(buf.data_ptr()), buf.nbytes)
 
@@ -788,20 +899,18 @@ def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, fl
     outs = {vid: buf.data_ptr() for vid, buf in host_out.items()}
 
     def submit():
-        # one step = upload, run, download through the session's host
-        # submission entry point; consecutive steps overlap their copies
         session.submit_host(ins, outs)
 
     for _ in range(2):
         submit() if pipelined else one()
     session.synchronize()
-    torch.cuda.synchronize(device)
-    if world > 1:
+    torch.cuda.synchronize(env.device)
+    if env.world > 1:
         dist.barrier()
     if pipelined:
-        count = max(4, args.steps)
+        count = max(4, min(args.steps, 8) if config.name == "c5" else args.steps)
         flush()
-        torch.cuda.synchronize(device)
+        torch.cuda.synchronize(env.device)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -809,31 +918,103 @@ def measure_e2e(m3, torch, device, stream, config, session, handles, outputs, fl
             submit()
         session.synchronize()
         b.record(stream)
-        torch.cuda.synchronize(device)
+        torch.cuda.synchronize(env.device)
         ms = a.elapsed_time(b) / count
     else:
         times = []
         for _ in range(max(3, args.steps // 2)):
             flush()
-            torch.cuda.synchronize(device)
+            torch.cuda.synchronize(env.device)
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
             one()
             b.record(stream)
-            torch.cuda.synchronize(device)
+            torch.cuda.synchronize(env.device)
             times.append(a.elapsed_time(b))
         ms = statistics.mean(times)
-    if world > 1:
-        ms = shardsmod().max_over_ranks(ms, device)
+    if env.world > 1:
+        ms = shardsmod().max_over_ranks(ms, env.device)
     h2d = sum(b.nbytes for b in host_in.values())
     d2h = sum(b.nbytes for b in host_out.values())
     mode = ("m3_cuda_session_submit_host_async per step, steps pipelined (one step's upload "
             "overlaps the previous step's download)" if pipelined else
             "m3_session_write_input, m3_cuda_session_run_steps_async + synchronize, "
             "m3_session_read_output per step")
-    return {"value": config.algorithmic_bytes(args.scale) * world / (ms / 1e3) / 1e9, "unit": "GB/s",
-            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "mode": mode}
+    del host_out
+    return {"value": config.algorithmic_bytes(args.scale) / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "per_rank": env.world > 1, "mode": mode}
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--config", default="c5", choices=sorted(CONFIGS),
+                        help="headline configuration (the others go to per_config)")
+    parser.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    parser.add_argument("--cpu-seconds", type=float, default=9.0,
+                        help="CPU work budget of each cpu_baseline sample")
+    parser.add_argument("--ref-seconds", type=float, default=1.0,
+                        help="reference arm: seconds per step of the headline sample")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-per-config", action="store_true")
+    parser.add_argument("--scale", type=float, default=1.0,
+                        help="fraction of each configuration along its shard axis "
+                             "(profiling only; reported numbers use 1.0)")
+    args = parser.parse_args()
+    headline = CONFIGS[args.config]
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args, headline)
+
+    import torch
+    import torch.distributed as dist
+
+    env = Env(torch)
+    if env.world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=env.device)
+    m3 = m3mod()
+    m3.load()
+    if env.world > 1:
+        env.shard_id = shardsmod().shared_shard_id(m3, env.device)
+    stream = torch.cuda.Stream(env.device)
+    torch.cuda.set_stream(stream)
+    flush = L2Flush(torch, env.device)
+    baseline_here = env.rank == 0 and env.world == 1 and not args.no_cpu_baseline
+
+    result = measure_cuda(m3, torch, dist, env, headline, args, stream, flush, baseline_here)
+    per_config = {}
+    if not args.no_per_config:
+        for name, config in CONFIGS.items():
+            if name != headline.name:
+                per_config[name] = measure_cuda(m3, torch, dist, env, config, args, stream, flush,
+                                                baseline_here)
+    launches = result["gpu_launches"] + sum(r["gpu_launches"] for r in per_config.values())
+    config = config_dict(headline, env.world)
+    if args.scale != 1.0:
+        config["scale"] = args.scale
+    line = {"metric": METRIC, "value": result["value"], "unit": "GB/s", "n_gpus": env.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": result["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": headline.dtype,
+            "data": "synthetic: seeded PCG32 streams of the reference RNG, generated on device",
+            "config": config, "plan": result["plan"],
+            "roofline": result["roofline"], "cpu_baseline": result["cpu_baseline"],
+            "e2e": result["e2e"], "clocks": result["clocks"],
+            "gpu_launches": launches, "gpu_launches_headline": result["gpu_launches"],
+            "elems_per_s": result["elems_per_s"], "per_config": per_config}
+    if env.world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if env.rank == 0:
+        print(json.dumps(line))
+    return 0
 
 
 if __name__ == "__main__":

@@ -438,6 +438,16 @@ typedef struct {
 #define M3_OP_ABS_MAX ((m3_op_kind)64)
 #define M3_OP_CLAMP_UNIT ((m3_op_kind)65)
 
+/* M3_OP_ROW_SUM (extension, unary like the two above): the sum of each row
+ * over the last axis, output F32 with the input's shape and the last axis 1
+ * (input F32, F16 or BF16).  The additions run left to right in F32, each
+ * rounded on its own: the order of the reference's softmax sum
+ * (src/m3_op_execute_basic.c:150-158), so results are bit-exact against a
+ * sequential F32 loop.  No data check: a NaN or infinity propagates as IEEE
+ * addition makes it.  A SOFTMAX, TOP_K or ROW_SUM of the same input in one
+ * graph shares one row pass. */
+#define M3_OP_ROW_SUM ((m3_op_kind)66)
+
 #define M3_CUDA_DEVICE_CURRENT (-1)
 
 typedef struct {
@@ -583,6 +593,112 @@ m3_status m3_cuda_graph_plan(const m3_graph *graph,
                              m3_session_plan_info *info,
                              m3_cuda_plan_report *report, char *text,
                              size_t text_capacity, m3_error *error);
+
+/* ------------------------------------------------------------------------
+ * Sharding: one fixed graph split across the GPUs of a box
+ * ------------------------------------------------------------------------
+ * One process per GPU.  Every rank creates a shard session from the same
+ * GLOBAL graph (global shapes and constants); the library cuts each value
+ * along one split axis and keeps only this rank's slab in its own device
+ * arena.  The split axis is counted in the shape of the graph's first input
+ * of largest rank; other values are right-aligned against that shape.  A
+ * value whose extent on that axis equals the global extent is split (slabs
+ * are contiguous ranges, balanced, in whole blocks of 4 elements when the
+ * extent allows); a value of extent 1 there, or without that axis, is
+ * replicated (broadcast constants such as a snake alpha [1,C,1] split along
+ * time, a norm scale, scalars).  Row operators (SOFTMAX, TOP_K, ROW_SUM,
+ * RMS_NORM, LAYER_NORM, CATEGORICAL) need the split axis to differ from
+ * their input's last axis.  M3_OP_ABS_MAX is a global reduction: every rank
+ * reduces its slab, then one NCCL all-reduce (MAX over the unsigned bit
+ * patterns, exact and order-free) on the session's stream gives every rank
+ * the global result; its output may not feed another node.  When the graph
+ * has a data check (NaN, F32-to-I32 range, categorical checks) the first
+ * failing command is agreed on by the same all-reduce, so a failure on any
+ * rank fails the run on every rank and leaves every rank's outputs as the
+ * reference leaves them.  Element-wise and row operators exchange nothing.
+ *
+ * m3_session_write_input / read_output on a shard session move this rank's
+ * slab (the local shape); m3_cuda_shard_write_input / read_output move it
+ * out of / into a buffer laid out as the whole global tensor. */
+#define M3_CUDA_SHARD_AXIS_AUTO (-1)
+
+/* The identity of one communicator (NCCL's unique id). */
+typedef struct {
+    unsigned char bytes[128];
+} m3_cuda_shard_id;
+
+typedef struct {
+    int rank;                    /* this process's shard, 0 <= rank < count */
+    int count;                   /* number of shards (GPUs) */
+    int axis;                    /* split axis, or M3_CUDA_SHARD_AXIS_AUTO:
+                                    the outermost axis that every value
+                                    allows and whose extent is at least
+                                    `count` */
+    const m3_cuda_shard_id *id;  /* communicator shared by all ranks; NULL:
+                                    no collective (count 1, or a caller that
+                                    combines global reductions itself) */
+    double timeout_seconds;      /* bound on communicator set-up and each
+                                    collective enqueue (default 120) */
+} m3_cuda_shard_options;
+
+void m3_cuda_shard_options_init(m3_cuda_shard_options *options);
+
+/* A new communicator id (rank 0 calls this and hands the bytes to the other
+ * ranks by its own means: MPI, a store, torch.distributed).  Loads NCCL
+ * (libnccl.so.2) on first use; M3_STATUS_UNSUPPORTED when it is absent. */
+m3_status m3_cuda_shard_id_create(m3_cuda_shard_id *id, m3_error *error);
+
+/* Where one value's slab lies in the global tensor. */
+typedef struct {
+    bool split;                  /* false: replicated on every rank */
+    uint8_t axis;                /* the value's own split axis (if split) */
+    uint64_t begin;              /* this rank's first index on that axis */
+    uint64_t extent;             /* this rank's extent on that axis */
+    m3_tensor_metadata global;   /* the value in the global graph */
+    m3_tensor_metadata local;    /* this rank's part */
+} m3_cuda_shard_slab;
+
+/* Host-only partition of `graph` for `shard` (no GPU, no communicator):
+ * the slab of `value` and, through `axis_out`, the split axis chosen. */
+m3_status m3_cuda_shard_plan(const m3_graph *graph,
+                             const m3_cuda_shard_options *shard,
+                             m3_graph_value_id value, m3_cuda_shard_slab *slab,
+                             int *axis_out, m3_error *error);
+
+/* This rank's session of the global graph: the local graph is planned,
+ * fused and allocated as any session on `cuda->device`; with shard->id set
+ * and count > 1 the ranks then join one communicator (every rank must call
+ * this; the call returns once all have joined, or fails after the
+ * timeout). */
+m3_status m3_cuda_shard_session_create(m3_session **session,
+                                       const m3_graph *graph,
+                                       const m3_session_options *options,
+                                       const m3_cuda_session_options *cuda,
+                                       const m3_cuda_shard_options *shard,
+                                       m3_error *error);
+
+m3_status m3_cuda_shard_get_slab(const m3_session *session,
+                                 m3_graph_value_id value,
+                                 m3_cuda_shard_slab *slab, m3_error *error);
+
+/* This rank's slab of an INPUT out of `global_data`, a buffer laid out as
+ * the whole global tensor (global_byte_count bytes, host memory, or device
+ * memory of any device when `device_memory`): one strided copy on the
+ * session's stream, complete when the call returns.  A replicated input
+ * takes the whole buffer. */
+m3_status m3_cuda_shard_write_input(m3_session *session,
+                                    m3_graph_value_id value,
+                                    const void *global_data,
+                                    size_t global_byte_count,
+                                    bool device_memory, m3_error *error);
+
+/* This rank's slab of an OUTPUT into its place in `global_data` (the rest of
+ * the buffer is not touched); a replicated output is written whole. */
+m3_status m3_cuda_shard_read_output(const m3_session *session,
+                                    m3_graph_value_id value,
+                                    void *global_data,
+                                    size_t global_byte_count,
+                                    bool device_memory, m3_error *error);
 
 /* ------------------------------------------------------------------------
  * Backend plug-in (reference src/m3_backend_internal.h:9-17)

@@ -888,7 +888,7 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
             __threadfence();
             const uint32_t result = atomicExch(&p.reduce->max_bits, 0u);
             atomicExch(&p.reduce->done_ctas, 0u);
-            if (!failed_before(p.status, p.absmax_command + 1u)) {
+            if (p.absmax_publish_always || !failed_before(p.status, p.absmax_command + 1u)) {
                 *static_cast<uint32_t *>(p.absmax_out) = result;
             }
         }

@@ -3,8 +3,10 @@
  * Same contracts as the reference: descriptors are copied, constants are
  * copied at m3_graph_set_constant, topology is only checked at session
  * creation (reference src/m3_graph.c:27-341, src/m3_graph_infer.c:41-296).
- * Shape inference covers every m3.h operator so graphs build identically;
- * unsupported operators are rejected later, at placement. */
+ * Shape inference covers the operators this provider executes (and the
+ * extensions); the reference's other kinds (contractions, attention, RoPE,
+ * embedding, convolutions, resize) are M3_STATUS_UNSUPPORTED here, as they
+ * would be at placement. */
 
 #include "m3c_internal.h"
 
@@ -205,24 +207,6 @@ m3_status m3_graph_add_node(m3_graph *graph,
 
 /* ------------------------------------------------------ shape inference */
 
-static bool add_u64(uint64_t a, uint64_t b, uint64_t *sum)
-{
-    if (a > UINT64_MAX - b) {
-        return false;
-    }
-    *sum = a + b;
-    return true;
-}
-
-static bool mul_u64(uint64_t a, uint64_t b, uint64_t *product)
-{
-    if (a != 0U && b > UINT64_MAX / a) {
-        return false;
-    }
-    *product = a * b;
-    return true;
-}
-
 static m3_status inferred_input(const m3_graph *graph, m3_graph_value_id id,
                                 const m3_tensor_metadata **metadata,
                                 m3_error *error)
@@ -267,65 +251,6 @@ static m3_status infer_broadcast(const m3_tensor_metadata *a,
 }
 
 /* Output length of the 1-D convolutions (src/m3_graph_infer.c:65-131). */
-static m3_status infer_convolution(const m3_graph_node_desc *node,
-                                   const m3_tensor_metadata *input,
-                                   const m3_tensor_metadata *weight,
-                                   m3_graph_value_desc *out, m3_error *error)
-{
-    const uint64_t groups = node->parameters.convolution.groups;
-    const uint64_t stride = node->parameters.convolution.stride;
-    const uint64_t dilation = node->parameters.convolution.dilation;
-    uint64_t span;
-    uint64_t reach;
-    uint64_t padded;
-    uint64_t channels;
-
-    if (input->rank != 3U || weight->rank != 3U || groups == 0U ||
-        stride == 0U || dilation == 0U || input->shape[2] == 0U ||
-        weight->shape[2] == 0U) {
-        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                             "cannot infer invalid convolution dimensions");
-    }
-    out->rank = 3U;
-    out->shape[0] = input->shape[0];
-    if (node->kind == M3_OP_CONV1D) {
-        channels = weight->shape[0];
-        if (!mul_u64(weight->shape[2] - 1U, dilation, &span) ||
-            !add_u64(span, 1U, &reach) ||
-            !add_u64(input->shape[2], node->parameters.convolution.pad_left,
-                     &padded) ||
-            !add_u64(padded, node->parameters.convolution.pad_right,
-                     &padded) ||
-            reach > padded) {
-            return m3c_error_set(error, M3_STATUS_OVERFLOW,
-                                 "Conv1d inferred length is invalid");
-        }
-        out->shape[2] = (padded - reach) / stride + 1U;
-    } else {
-        uint64_t padding;
-
-        if (!mul_u64(weight->shape[1], groups, &channels) ||
-            !mul_u64(input->shape[2] - 1U, stride, &reach) ||
-            !mul_u64(weight->shape[2] - 1U, dilation, &span) ||
-            !add_u64(reach, span, &reach) ||
-            !add_u64(reach, node->parameters.convolution.output_padding,
-                     &reach) ||
-            !add_u64(reach, 1U, &reach) ||
-            !add_u64(node->parameters.convolution.pad_left,
-                     node->parameters.convolution.pad_right, &padding) ||
-            reach <= padding) {
-            return m3c_error_set(error, M3_STATUS_OVERFLOW,
-                                 "ConvTranspose1d inferred length is invalid");
-        }
-        out->shape[2] = reach - padding;
-    }
-    out->shape[1] = channels;
-    return M3_STATUS_OK;
-}
-
-/* Per-operator output shape and forced dtypes (src/m3_graph_infer.c:133-272);
- * the extension operators infer [1] F32 (abs-max) and the input shape
- * (clamp). */
 static m3_status infer_shape(const m3_graph *graph,
                              const m3_graph_node_desc *node,
                              size_t output_index, m3_graph_value_desc *out,
@@ -347,8 +272,6 @@ static m3_status infer_shape(const m3_graph *graph,
     case M3_OP_CAST:
     case M3_OP_RMS_NORM:
     case M3_OP_LAYER_NORM:
-    case M3_OP_ROPE:
-    case M3_OP_ATTENTION:
     case M3_OP_SOFTMAX:
     case M3_OP_SNAKE1D:
     case M3_OP_TANH:
@@ -367,50 +290,21 @@ static m3_status infer_shape(const m3_graph *graph,
         out->shape[0] = 1U;
         out->dtype = M3_DTYPE_F32;
         return M3_STATUS_OK;
+    case (int)M3_OP_ROW_SUM:
+        if (first->rank == 0U) {
+            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                                 "cannot infer row-sum shape");
+        }
+        copy_shape(out, first);
+        out->shape[first->rank - 1U] = 1U;
+        out->dtype = M3_DTYPE_F32;
+        return M3_STATUS_OK;
     case M3_OP_ADD:
     case M3_OP_MUL:
         status = inferred_input(graph, node->inputs[1], &second, error);
         return status != M3_STATUS_OK
                    ? status
                    : infer_broadcast(first, second, out, error);
-    case M3_OP_EMBEDDING:
-        status = inferred_input(graph, node->inputs[1], &second, error);
-        if (status != M3_STATUS_OK) {
-            return status;
-        }
-        if (first->rank >= M3_TENSOR_MAX_RANK || second->rank != 2U) {
-            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                                 "cannot infer embedding shape");
-        }
-        copy_shape(out, first);
-        out->rank = (uint8_t)(first->rank + 1U);
-        out->shape[first->rank] = second->shape[1];
-        return M3_STATUS_OK;
-    case M3_OP_MATMUL:
-        status = inferred_input(graph, node->inputs[1], &second, error);
-        if (status != M3_STATUS_OK) {
-            return status;
-        }
-        if (first->rank != 2U || second->rank != 2U) {
-            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                                 "cannot infer matmul shape");
-        }
-        out->rank = 2U;
-        out->shape[0] = first->shape[0];
-        out->shape[1] = second->shape[1];
-        return M3_STATUS_OK;
-    case M3_OP_LINEAR:
-        status = inferred_input(graph, node->inputs[1], &second, error);
-        if (status != M3_STATUS_OK) {
-            return status;
-        }
-        if (first->rank == 0U || second->rank != 2U) {
-            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                                 "cannot infer linear shape");
-        }
-        copy_shape(out, first);
-        out->shape[first->rank - 1U] = second->shape[0];
-        return M3_STATUS_OK;
     case M3_OP_TOP_K:
         if (first->rank == 0U || output_index > 1U) {
             return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
@@ -428,22 +322,6 @@ static m3_status infer_shape(const m3_graph *graph,
         copy_shape(out, first);
         out->rank = (uint8_t)(first->rank - 1U);
         out->dtype = M3_DTYPE_I32;
-        return M3_STATUS_OK;
-    case M3_OP_CONV1D:
-    case M3_OP_CONV_TRANSPOSE1D:
-        status = inferred_input(graph, node->inputs[1], &second, error);
-        return status != M3_STATUS_OK
-                   ? status
-                   : infer_convolution(node, first, second, out, error);
-    case M3_OP_NEAREST_RESIZE1D:
-        if (first->rank != 3U || node->parameters.resize.output_length == 0U) {
-            return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
-                                 "cannot infer nearest resize shape");
-        }
-        out->rank = 3U;
-        out->shape[0] = first->shape[0];
-        out->shape[1] = first->shape[1];
-        out->shape[2] = node->parameters.resize.output_length;
         return M3_STATUS_OK;
     default:
         return m3c_error_set(error, M3_STATUS_UNSUPPORTED,

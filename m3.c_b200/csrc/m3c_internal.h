@@ -195,6 +195,50 @@ int m3c_launch_rng_normal(uint64_t seed, uint64_t sequence, float mean,
                           void *stream);
 const char *m3c_cuda_error_string(int code);
 
+/* ------------------------------------------------------------ sharding */
+
+/* One rank's share of a sharded session (m3c_shard.c). */
+typedef struct {
+    int rank;
+    int count;
+    int axis;                      /* split axis in the primary value's shape */
+    size_t value_count;
+    m3_cuda_shard_slab *slabs;     /* per value */
+    void *comm;                    /* NCCL communicator, or NULL */
+    double timeout_seconds;
+    int reduction_count;           /* ABS_MAX outputs, all-reduced per run */
+    uint32_t reductions[M3C_SHARD_MAX_REDUCTIONS];
+    uint32_t reduction_commands[M3C_SHARD_MAX_REDUCTIONS];
+    bool checks;                   /* the graph has a data-checked command */
+    uint32_t *staging;             /* device words: reductions, then status */
+} m3c_shard;
+
+/* The collective step after each run is needed (a communicator and
+ * something to agree on). */
+bool m3c_shard_collective(const m3c_shard *shard);
+void m3c_shard_free(m3c_shard *shard);
+
+/* NCCL (m3c_nccl.c), loaded at run time. */
+m3_status m3c_comm_create(const m3_cuda_shard_id *id, int rank, int count,
+                          double limit_seconds, void **comm, m3_error *error);
+void m3c_comm_destroy(void *comm);
+m3_status m3c_comm_max_u32(void *comm, uint32_t *words, size_t count,
+                           void *stream, double limit_seconds,
+                           m3_error *error);
+
+/* Session internals the sharding layer needs (m3c_session.c). */
+void m3c_session_attach_shard(m3_session *session, m3c_shard *shard);
+const m3c_shard *m3c_session_shard(const m3_session *session);
+const m3_tensor_metadata *m3c_session_metadata(const m3_session *session,
+                                               m3_graph_value_id value);
+m3_graph_value_role m3c_session_role(const m3_session *session,
+                                     m3_graph_value_id value);
+size_t m3c_session_value_count(const m3_session *session);
+
+/* Pack / unpack around the per-run all-reduce (m3c_util.cu). */
+int m3c_launch_shard_pack(const m3c_shard_words *words, void *stream);
+int m3c_launch_shard_unpack(const m3c_shard_words *words, void *stream);
+
 /* -------------------------------------------------------------- rng */
 
 typedef struct {

@@ -137,6 +137,12 @@ typedef struct {
     void *absmax_out;               /* one F32 element */
     uint32_t absmax_command;
     uint32_t skip_before;           /* skip when a command < this failed */
+    int32_t absmax_publish_always;  /* shard of a sharded session: publish the
+                                       slab's maximum even when it is a NaN
+                                       pattern (the all-reduce after the run
+                                       turns it into the failure of every
+                                       rank) */
+    int32_t reserved;
     m3c_operand operands[M3C_EW_MAX_OPERANDS];
     m3c_ew_op ops[M3C_EW_MAX_OPS];
     m3c_ew_out outputs[M3C_EW_MAX_OUTPUTS];
@@ -201,6 +207,20 @@ typedef struct {
 } m3c_categorical_params;
 
 int m3c_launch_categorical(const m3c_categorical_params *params, void *stream);
+
+/* The words a sharded session's ranks agree on after each run: the bit
+ * patterns of its global reductions (ABS_MAX outputs) and the complement of
+ * the first failing command, all combined by one MAX all-reduce. */
+#define M3C_SHARD_MAX_REDUCTIONS 8
+
+typedef struct {
+    uint32_t *values[M3C_SHARD_MAX_REDUCTIONS];   /* F32 reduction outputs */
+    uint32_t commands[M3C_SHARD_MAX_REDUCTIONS];
+    int32_t count;
+    int32_t reserved;
+    m3c_status *status;
+    uint32_t *staging;                            /* count + 1 words */
+} m3c_shard_words;
 
 /* The kernel and grid m3c_launch_ew would use, chosen once (sessions keep it
  * per launch so repeated runs skip the program search), and the launch with

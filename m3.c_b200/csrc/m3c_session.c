@@ -102,6 +102,8 @@ struct m3_session {
     size_t graph_next;
     /* host submissions: copy streams, double-buffered staging, events */
     host_pipe pipe;
+    /* this rank's share of a sharded session (NULL: not sharded) */
+    m3c_shard *shard;
 };
 
 static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, UINT32_MAX};
@@ -213,6 +215,15 @@ void m3_session_free(m3_session *session)
         drop_graph(&session->graphs[g]);
     }
     drop_pipe(&session->pipe);
+    if (session->shard != NULL) {
+        /* the stream is idle: no collective of this communicator is pending */
+        m3c_comm_destroy(session->shard->comm);
+        session->shard->comm = NULL;
+        (void)cudaFree(session->shard->staging);
+        session->shard->staging = NULL;
+        m3c_shard_free(session->shard);
+        session->shard = NULL;
+    }
     if (session->arena != NULL) {
         (void)cudaFree(session->arena);
     }
@@ -540,6 +551,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         if (l->has_absmax) {
             p.reduce = &s->reduce[index];
             p.absmax_out = ref_pointer(s, l->absmax_out);
+            p.absmax_publish_always = m3c_shard_collective(s->shard) ? 1 : 0;
         }
         return m3c_launch_ew_chosen(&s->ew_choices[index], &p, s->stream);
     }
@@ -752,6 +764,45 @@ static cudaGraphExec_t capture_runs(m3_session *s, size_t runs, size_t a,
     return exec;
 }
 
+/* The ranks of a sharded session agree after each run: the global
+ * reductions' bit patterns and the first failing command, packed into one
+ * staging area, all-reduced (MAX) on the session's stream, unpacked. */
+static m3_status shard_collect(m3_session *s, m3_error *error)
+{
+    m3c_shard *sh = s->shard;
+    m3c_shard_words w;
+    int code;
+    int i;
+    m3_status status;
+
+    memset(&w, 0, sizeof(w));
+    w.count = sh->reduction_count;
+    for (i = 0; i < sh->reduction_count; ++i) {
+        w.values[i] = (uint32_t *)value_pointer(s, sh->reductions[i], false);
+        w.commands[i] = sh->reduction_commands[i];
+    }
+    w.status = s->status_device;
+    w.staging = sh->staging;
+    code = m3c_launch_shard_pack(&w, s->stream);
+    if (code != 0) {
+        return m3c_error_set(error, M3_STATUS_INTERNAL, "shard pack failed: %s",
+                             m3c_cuda_error_string(code));
+    }
+    status = m3c_comm_max_u32(sh->comm, sh->staging,
+                              (size_t)sh->reduction_count + 1U, s->stream,
+                              sh->timeout_seconds, error);
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    code = m3c_launch_shard_unpack(&w, s->stream);
+    if (code != 0) {
+        return m3c_error_set(error, M3_STATUS_INTERNAL,
+                             "shard unpack failed: %s",
+                             m3c_cuda_error_string(code));
+    }
+    return M3_STATUS_OK;
+}
+
 /* Enqueue `runs` runs, exchanging slots a and b between consecutive runs
  * (SIZE_MAX: no exchange).  With cuda_graphs the whole sequence is one graph
  * launch, captured on first use for each starting buffer assignment and kept
@@ -784,7 +835,7 @@ static m3_status enqueue_runs(m3_session *s, size_t runs, size_t a, size_t b,
     if (status != M3_STATUS_OK) {
         return status;
     }
-    if (s->cuda.cuda_graphs) {
+    if (s->cuda.cuda_graphs && !m3c_shard_collective(s->shard)) {
         enum cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
 
         if (cudaStreamIsCapturing(s->stream, &capturing) == cudaSuccess &&
@@ -823,6 +874,9 @@ static m3_status enqueue_runs(m3_session *s, size_t runs, size_t a, size_t b,
         }
         /* assume success; a failure found at synchronise is replayed */
         status = account_run(s, error);
+        if (status == M3_STATUS_OK && m3c_shard_collective(s->shard)) {
+            status = shard_collect(s, error);
+        }
         if (status == M3_STATUS_OK && r + 1U < runs && a != SIZE_MAX) {
             status = account_swap(s, a, b, error);
         }
@@ -1536,4 +1590,33 @@ m3_status m3_cuda_graph_plan(const m3_graph *graph,
     m3c_plan_free(&plan);
     m3_error_reset(error);
     return M3_STATUS_OK;
+}
+
+/* ------------------------------------------------- sharding internals */
+
+void m3c_session_attach_shard(m3_session *session, m3c_shard *shard)
+{
+    session->shard = shard;
+}
+
+const m3c_shard *m3c_session_shard(const m3_session *session)
+{
+    return session->shard;
+}
+
+const m3_tensor_metadata *m3c_session_metadata(const m3_session *session,
+                                               m3_graph_value_id value)
+{
+    return &session->metadata[value];
+}
+
+m3_graph_value_role m3c_session_role(const m3_session *session,
+                                     m3_graph_value_id value)
+{
+    return session->descriptions[value].role;
+}
+
+size_t m3c_session_value_count(const m3_session *session)
+{
+    return session->plan.value_count;
 }

@@ -431,6 +431,51 @@ extern "C" int m3c_launch_scan(const void *data, int32_t dtype, uint64_t count, 
     return static_cast<int>(cudaGetLastError());
 }
 
+namespace m3c {
+namespace {
+
+// staging = [reduction bits..., ~first failing command]: a MAX over ranks of
+// each word is the largest bit pattern (|x| of non-NaN F32 values orders like
+// the value; a NaN pattern beats every number) and the smallest failing
+// command.
+__global__ void shard_pack_kernel(m3c_shard_words w)
+{
+    const int i = static_cast<int>(threadIdx.x);
+    if (i < w.count) {
+        w.staging[i] = *reinterpret_cast<volatile uint32_t *>(w.values[i]);
+    } else if (i == w.count) {
+        w.staging[i] = ~*reinterpret_cast<volatile uint32_t *>(&w.status->fail_command);
+    }
+}
+
+__global__ void shard_unpack_kernel(m3c_shard_words w)
+{
+    const int i = static_cast<int>(threadIdx.x);
+    if (i < w.count) {
+        const uint32_t bits = w.staging[i];
+        *w.values[i] = bits;
+        if (bits > 0x7f800000u) record_failure(w.status, w.commands[i]);  // a NaN on some rank
+    } else if (i == w.count) {
+        const uint32_t first = ~w.staging[i];
+        if (first != 0xffffffffu) record_failure(w.status, first);
+    }
+}
+
+}  // namespace
+}  // namespace m3c
+
+extern "C" int m3c_launch_shard_pack(const m3c_shard_words *words, void *stream)
+{
+    m3c::shard_pack_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*words);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int m3c_launch_shard_unpack(const m3c_shard_words *words, void *stream)
+{
+    m3c::shard_unpack_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*words);
+    return static_cast<int>(cudaGetLastError());
+}
+
 extern "C" const char *m3c_cuda_error_string(int code)
 {
     return cudaGetErrorString(static_cast<cudaError_t>(code));

@@ -31,7 +31,7 @@ OPS = dict(COPY=0, CAST=1, ADD=2, MUL=3, EMBEDDING=4, MATMUL=5, LINEAR=6,
            RMS_NORM=7, LAYER_NORM=8, ROPE=9, ATTENTION=10, GATED_SILU=11,
            SOFTMAX=12, TOP_K=13, CATEGORICAL=14, CONV1D=15,
            CONV_TRANSPOSE1D=16, NEAREST_RESIZE1D=17, SNAKE1D=18, TANH=19,
-           ABS_MAX=64, CLAMP_UNIT=65)
+           ABS_MAX=64, CLAMP_UNIT=65, ROW_SUM=66)
 # include/m3.h:80-91
 PROVIDER_NEURAL_ENGINE, PROVIDER_METAL, PROVIDER_CPU, PROVIDER_CUDA = 0, 1, 2, 3
 INPUT, CONSTANT, TEMPORARY, OUTPUT = 0, 1, 2, 3
@@ -107,6 +107,33 @@ class CudaSessionOptions(ctypes.Structure):
                 ("fuse", ctypes.c_bool), ("cuda_graphs", ctypes.c_bool)]
 
 
+class ShardOptions(ctypes.Structure):
+    """m3_cuda_shard_options: this rank's place in a graph split across
+    `count` GPUs along `axis` (AXIS_AUTO: the library's choice); `id` is the
+    communicator id (ShardId or None: no collective)."""
+
+    AXIS_AUTO = -1
+
+    def __init__(self, rank: int = 0, count: int = 1, axis: int = -1, id=None,
+                 timeout_seconds: float = 120.0):
+        super().__init__()
+        self.rank = rank
+        self.count = count
+        self.axis = axis
+        self._id = id
+        self.id = ctypes.pointer(id) if id is not None else None
+        self.timeout_seconds = timeout_seconds
+
+
+class ShardId(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 128)]
+
+
+ShardOptions._fields_ = [("rank", ctypes.c_int), ("count", ctypes.c_int),
+                         ("axis", ctypes.c_int), ("id", ctypes.POINTER(ShardId)),
+                         ("timeout_seconds", ctypes.c_double)]
+
+
 class PlanReport(ctypes.Structure):
     _fields_ = [("launch_count", ctypes.c_size_t),
                 ("fused_node_count", ctypes.c_size_t),
@@ -120,6 +147,14 @@ class TensorMetadata(ctypes.Structure):
                 ("shape", ctypes.c_uint64 * MAX_RANK),
                 ("element_count", ctypes.c_size_t),
                 ("byte_count", ctypes.c_size_t)]
+
+
+class ShardSlab(ctypes.Structure):
+    """m3_cuda_shard_slab: where one value's slab lies in the global tensor."""
+
+    _fields_ = [("split", ctypes.c_bool), ("axis", ctypes.c_uint8),
+                ("begin", ctypes.c_uint64), ("extent", ctypes.c_uint64),
+                ("global_", TensorMetadata), ("local", TensorMetadata)]
 
 
 class TensorView(ctypes.Structure):
@@ -337,6 +372,25 @@ _CUDA_SIGNATURES = {
     "m3_cuda_exp_self_test": (ctypes.c_int, [
         ctypes.c_int, ctypes.POINTER(ctypes.c_uint32),
         ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_options_init": (None, [ctypes.POINTER(ShardOptions)]),
+    "m3_cuda_shard_id_create": (ctypes.c_int, [ctypes.POINTER(ShardId),
+                                               ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_plan": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.POINTER(ShardOptions), ctypes.c_uint32,
+        ctypes.POINTER(ShardSlab), ctypes.POINTER(ctypes.c_int), ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_session_create": (ctypes.c_int, [
+        ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
+        ctypes.POINTER(SessionOptions), ctypes.POINTER(CudaSessionOptions),
+        ctypes.POINTER(ShardOptions), ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_get_slab": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ShardSlab),
+        ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_write_input": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_bool, ctypes.POINTER(M3Error)]),
+    "m3_cuda_shard_read_output": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_bool, ctypes.POINTER(M3Error)]),
     "m3_cuda_abs_max_static": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
         ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_uint64),
@@ -457,6 +511,8 @@ class Graph:
             return first[:-1] + (k,)
         if kind == OPS["ABS_MAX"]:
             return (1,)
+        if kind == OPS["ROW_SUM"]:
+            return first[:-1] + (1,)
         if kind == OPS["CATEGORICAL"]:
             return first[:-1]
         return first
@@ -472,7 +528,7 @@ class Graph:
             ctypes.byref(out), ctypes.byref(err)), err)
         code = desc.kind
         if code in (OPS["SNAKE1D"], OPS["TANH"], OPS["CLAMP_UNIT"],
-                    OPS["ABS_MAX"]):
+                    OPS["ABS_MAX"], OPS["ROW_SUM"]):
             dtype = F32
         elif code == OPS["COPY"]:
             dtype = self.values[inputs[0]][0]
@@ -492,13 +548,33 @@ class Session:
     def __init__(self, graph: Graph, allow_metal: bool = True,
                  allow_cpu: bool = True, allow_neural_engine: bool = True,
                  device: int = -1, stream: int | None = None,
-                 fuse: bool = True, cuda: bool = True, cuda_graphs: bool = True):
+                 fuse: bool = True, cuda: bool = True, cuda_graphs: bool = True,
+                 shard: ShardOptions | None = None):
         self.lib = graph.lib
         self.values = list(graph.values)
         self.handle = ctypes.c_void_p()
         self.cuda = cuda
+        self.shard = shard
         options = SessionOptions(allow_neural_engine, allow_metal, allow_cpu)
         err = M3Error()
+        if shard is not None:
+            extra = CudaSessionOptions()
+            self.lib.m3_cuda_session_options_init(ctypes.byref(extra))
+            extra.device = device
+            extra.stream = stream
+            extra.fuse = fuse
+            extra.cuda_graphs = cuda_graphs
+            status = self.lib.m3_cuda_shard_session_create(
+                ctypes.byref(self.handle), graph.handle, ctypes.byref(options),
+                ctypes.byref(extra), ctypes.byref(shard), ctypes.byref(err))
+            check(status, err)
+            # reads and writes move this rank's slab: local shapes
+            for vid in range(len(self.values)):
+                slab = self.shard_slab(vid)
+                dtype, _, role = self.values[vid]
+                local = tuple(slab.local.shape[a] for a in range(slab.local.rank))
+                self.values[vid] = (dtype, local, role)
+            return
         if cuda:
             extra = CudaSessionOptions()
             self.lib.m3_cuda_session_options_init(ctypes.byref(extra))
@@ -636,6 +712,35 @@ class Session:
         check(self.lib.m3_cuda_session_read_output_device_async(
             self.handle, vid, ctypes.c_void_p(pointer), nbytes, ctypes.byref(err)), err)
 
+    def value_bytes(self, vid: int) -> int:
+        """Bytes of a value on this session (a shard's local slab)."""
+        dtype, shape, _ = self.values[vid]
+        return int(np.prod(shape, dtype=np.int64)) * ITEMSIZE[dtype]
+
+    def shard_slab(self, vid: int) -> ShardSlab:
+        slab = ShardSlab()
+        err = M3Error()
+        check(self.lib.m3_cuda_shard_get_slab(self.handle, vid, ctypes.byref(slab),
+                                              ctypes.byref(err)), err)
+        return slab
+
+    def shard_write(self, vid: int, pointer: int, global_bytes: int,
+                    device: bool = False) -> None:
+        """This rank's slab of an input out of a buffer laid out as the
+        global tensor (host or device memory)."""
+        err = M3Error()
+        check(self.lib.m3_cuda_shard_write_input(
+            self.handle, vid, ctypes.c_void_p(pointer), global_bytes, device,
+            ctypes.byref(err)), err)
+
+    def shard_read(self, vid: int, pointer: int, global_bytes: int,
+                   device: bool = False) -> None:
+        """This rank's slab of an output into its place in a global buffer."""
+        err = M3Error()
+        check(self.lib.m3_cuda_shard_read_output(
+            self.handle, vid, ctypes.c_void_p(pointer), global_bytes, device,
+            ctypes.byref(err)), err)
+
     def swap(self, input_vid: int, output_vid: int) -> None:
         err = M3Error()
         check(self.lib.m3_cuda_session_swap_values(
@@ -682,6 +787,26 @@ def fill_normal(seed: int, sequence: int, mean: float, deviation: float,
         seed, sequence, mean, deviation, out.ctypes.data_as(ctypes.c_void_p),
         count, ctypes.byref(err)), err)
     return out
+
+
+def shard_id() -> ShardId:
+    """m3_cuda_shard_id_create: a new communicator id (rank 0)."""
+    out = ShardId()
+    err = M3Error()
+    check(load().m3_cuda_shard_id_create(ctypes.byref(out), ctypes.byref(err)), err)
+    return out
+
+
+def shard_plan(graph: Graph, rank: int, count: int, axis: int, vid: int):
+    """m3_cuda_shard_plan (host only): (slab, chosen axis) of one value."""
+    options = ShardOptions(rank, count, axis, None)
+    slab = ShardSlab()
+    chosen = ctypes.c_int(-1)
+    err = M3Error()
+    check(graph.lib.m3_cuda_shard_plan(graph.handle, ctypes.byref(options), vid,
+                                       ctypes.byref(slab), ctypes.byref(chosen),
+                                       ctypes.byref(err)), err)
+    return slab, chosen.value
 
 
 ABS_MAX_STATIC_MAX_TENSORS = 64

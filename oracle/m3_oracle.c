@@ -667,6 +667,60 @@ int m3o_clamp_unit(const m3o_view *input, m3o_view *output)
     return M3O_OK;
 }
 
+/* Row sum, an extension operator: the sum of each row over the last axis,
+ * accumulated in F32 from the first column to the last, the order (and the
+ * per-addition rounding) of the reference's softmax sum
+ * (src/m3_op_execute_basic.c:150-158).  Output: F32, the input's shape with
+ * the last axis 1.  A NaN or infinity propagates as IEEE addition makes it;
+ * there is no data check.  An empty row sums to +0. */
+int m3o_row_sum(const m3o_view *input, m3o_view *output)
+{
+    uint64_t count = element_count(input);
+    uint64_t width = input->rank == 0 ? 1U : input->shape[input->rank - 1];
+    uint64_t rows = width == 0U ? element_count(output) : count / width;
+    uint64_t row;
+
+    if (output->dtype != M3O_F32 || input->dtype == M3O_I32) {
+        return M3O_INVALID_ARGUMENT;
+    }
+    for (row = 0U; row < rows; ++row) {
+        float sum = 0.0F;
+        uint64_t column;
+
+        for (column = 0U; column < width; ++column) {
+            sum += load_float(input, flat_offset(input, row * width + column));
+        }
+        store_float(output, flat_offset(output, row), sum);
+    }
+    return M3O_OK;
+}
+
+/* ------------------------------------------------------------------ RNG */
+
+/* The reference's PCG32 stream (src/m3_rng.c:9-39): seeding, then `count`
+ * successive 32-bit words.  Benchmark inputs are functions of these words
+ * (uniforms: src/m3_rng.c:53-66). */
+void m3o_pcg32_fill(uint64_t seed, uint64_t sequence, uint32_t *words,
+                    size_t count)
+{
+    const uint64_t multiplier = UINT64_C(6364136223846793005);
+    uint64_t increment = (sequence << 1U) | UINT64_C(1);
+    uint64_t state = 0U;
+    size_t index;
+
+    state = state * multiplier + increment;
+    state += seed;
+    state = state * multiplier + increment;
+    for (index = 0U; index < count; ++index) {
+        uint64_t old = state;
+        uint32_t shifted = (uint32_t)(((old >> 18U) ^ old) >> 27U);
+        uint32_t rotation = (uint32_t)(old >> 59U);
+
+        state = old * multiplier + increment;
+        words[index] = (shifted >> rotation) | (shifted << ((0U - rotation) & 31U));
+    }
+}
+
 /* ---------------------------------------------------------- flow time grid */
 
 /* src/m3_flow_common.c:159-172 */

@@ -66,6 +66,11 @@ int m3o_layer_norm(const m3o_view *input, const m3o_view *scale,
 /* Extension operators of the CUDA provider (no reference operator exists). */
 int m3o_abs_max(const m3o_view *input, m3o_view *output);
 int m3o_clamp_unit(const m3o_view *input, m3o_view *output);
+int m3o_row_sum(const m3o_view *input, m3o_view *output);
+
+/* The reference RNG's 32-bit word stream (src/m3_rng.c:9-39). */
+void m3o_pcg32_fill(uint64_t seed, uint64_t sequence, uint32_t *words,
+                    size_t count);
 
 /* Flow-matching time grid (reference src/m3_flow_common.c:159-190). */
 float m3o_flow_timestep(uint32_t step, uint32_t step_count);

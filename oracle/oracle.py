@@ -83,6 +83,7 @@ def restatement() -> ctypes.CDLL:
             "m3o_rms_norm": [vp, vp, vp, ctypes.c_float],
             "m3o_layer_norm": [vp, vp, vp, vp, ctypes.c_float],
             "m3o_abs_max": [vp, vp], "m3o_clamp_unit": [vp, vp],
+            "m3o_row_sum": [vp, vp],
         }.items():
             getattr(lib, name).argtypes = args
             getattr(lib, name).restype = ctypes.c_int
@@ -98,6 +99,9 @@ def restatement() -> ctypes.CDLL:
         lib.m3o_flow_timestep_delta.restype = ctypes.c_float
         lib.m3o_flow_timestep.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
         lib.m3o_flow_timestep.restype = ctypes.c_float
+        lib.m3o_pcg32_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64,
+                                       ctypes.c_void_p, ctypes.c_size_t]
+        lib.m3o_pcg32_fill.restype = None
         _restatement = lib
     return _restatement
 
@@ -150,6 +154,24 @@ def widen(bits: np.ndarray, dtype: int) -> np.ndarray:
                    ctypes.byref(view(out)))
     assert status == 0
     return out
+
+
+def pcg32_words(seed: int, sequence: int, count: int) -> np.ndarray:
+    """`count` words of the reference's PCG32 stream (src/m3_rng.c:9-39)."""
+    out = np.empty(count, dtype=np.uint32)
+    restatement().m3o_pcg32_fill(seed, sequence, out.ctypes.data, count)
+    return out
+
+
+def uniform(seed: int, sequence: int, low: float, high: float,
+            count: int) -> np.ndarray:
+    """Uniforms on [low, high) from the reference stream: 24 bits scaled by
+    2^-24 (src/m3_rng.c:53-66), then low + (high - low) * u in F32 (the
+    benchmark's scaling, one rounding per statement)."""
+    u = (pcg32_words(seed, sequence, count) >> np.uint32(8)).astype(np.float32)
+    u *= np.float32(2.0 ** -24)
+    span = np.float32(high) - np.float32(low)
+    return (np.float32(low) + span * u).astype(np.float32)
 
 
 def run(name: str, *arrays_and_dtypes, **scalars) -> int:

@@ -8,8 +8,9 @@ not depend on size and by comparisons on sampled rows/positions:
   against the oracle within 1e-6 relative; every row sums to 1;
 * C3: the residual sum bit-exact everywhere; sampled rows of RMSNorm
   (bit-exact) and gated SiLU (1 ulp) against the reference CPU provider;
-* C5: sampled positions against the oracle's snake and clamp (0x1p-19),
-  the abs-max against the maximum of the clamped output;
+* C5: the abs-max bit-exact against the oracle's abs-max of the oracle's
+  snake over the WHOLE input (row slices on all host threads); sampled
+  positions against the oracle's snake and clamp (0x1p-19);
 * one element-wise launch over more than 2^32 elements (64-bit indexing).
 """
 
@@ -40,16 +41,20 @@ def _bits(a):
     return np.ascontiguousarray(a).view(np.uint32 if a.dtype.itemsize == 4 else np.uint16)
 
 
+def _rng(m3):
+    return _bench().ProductRng(m3)
+
+
 def _session(m3, name):
     cfg = _bench().CONFIGS[name]
     g = m3.Graph()
-    handles, outputs = cfg.build(m3, g)
+    handles, outputs = cfg.build(m3, g, _rng(m3))
     return cfg, m3.Session(g), handles, outputs
 
 
 def test_c1_full_size_bit_exact(m3, oracle, gpu):
     cfg, s, h, o = _session(m3, "c1")
-    x = cfg.inputs_host(m3, oracle)["x"]
+    x = cfg.inputs_host(_rng(m3))["x"]
     s.write(h["x"], x)
     s.run()
     c = m3.fill_uniform(0, 1, 0.5, 2.0, cfg.width)
@@ -59,7 +64,7 @@ def test_c1_full_size_bit_exact(m3, oracle, gpu):
 
 def test_c2_full_size(m3, oracle, gpu):
     cfg, s, h, o = _session(m3, "c2")
-    x = cfg.inputs_host(m3, oracle)["x"]
+    x = cfg.inputs_host(_rng(m3))["x"]
     s.write(h["x"], x)
     s.run()
     probs, values, indices = (s.read(v) for v in o)
@@ -78,7 +83,7 @@ def test_c2_full_size(m3, oracle, gpu):
 
 def test_c3_full_size(m3, ref, oracle, gpu):
     cfg, s, h, o = _session(m3, "c3")
-    data = cfg.inputs_host(m3, oracle)
+    data = cfg.inputs_host(_rng(m3))
     for name, vid in h.items():
         s.write(vid, data[name])
     s.run()
@@ -91,7 +96,7 @@ def test_c3_full_size(m3, ref, oracle, gpu):
     g = m3.Graph(lib=ref)
     sub = type(cfg)()
     sub.rows = len(rows)
-    handles, outputs = sub.build(m3, g)
+    handles, outputs = sub.build(m3, g, _rng(m3))
     rs = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
     for name, vid in handles.items():
         rs.write(vid, np.ascontiguousarray(data[name][rows]))
@@ -105,7 +110,7 @@ def test_c3_full_size(m3, ref, oracle, gpu):
 
 def test_c4_full_size_thirty_steps_bit_exact(m3, oracle, gpu):
     cfg, s, h, o = _session(m3, "c4")
-    data = cfg.inputs_host(m3, oracle)
+    data = cfg.inputs_host(_rng(m3))
     for name, vid in h.items():
         s.write(vid, data[name])
     s.run_steps(30, *cfg.carry)
@@ -129,7 +134,7 @@ def test_c5_full_size(m3, oracle, gpu):
     cfg = bench.CONFIGS["c5"]
     device = torch.device("cuda", 0)
     g = m3.Graph()
-    handles, outputs = cfg.build(m3, g)
+    handles, outputs = cfg.build(m3, g, _rng(m3))
     s = m3.Session(g, device=0, stream=torch.cuda.current_stream(device).cuda_stream)
     x = cfg.inputs_device(m3, torch, device)["x"]
     torch.cuda.synchronize(device)  # the session's stream does not wait on torch's
@@ -161,6 +166,39 @@ def test_c5_full_size(m3, oracle, gpu):
     assert bool(np.all((diff <= 2.0 ** -19) | (diff <= 2.0 ** -19 * np.abs(want))))
     assert np.abs(z).max() <= m * (1 + 2.0 ** -19)
     s.close()
+    # the abs-max bits against the oracle over the whole signal: snake of
+    # each (batch, channel) row, then its abs-max, rows spread over threads
+    host = x.cpu().numpy().reshape(-1, cfg.length)
+    del x, y, flat
+    torch.cuda.empty_cache()
+    assert _oracle_abs_max_bits(oracle, host, alpha, cfg.channels) == \
+        np.float32(m).view(np.uint32)
+
+
+def _oracle_abs_max_bits(oracle, rows, alpha, channels):
+    """max over rows of the oracle's abs-max of snake1d(row, alpha[channel])
+    as F32 bits, rows processed by all host threads (ctypes releases the
+    GIL)."""
+    import threading
+
+    threads = max(1, os.cpu_count() or 1)
+    best = [0] * threads
+
+    def work(t):
+        z = np.empty((1, 1, rows.shape[1]), np.float32)
+        out = np.zeros(1, np.float32)
+        for r in range(t, rows.shape[0], threads):
+            a = np.array([[[alpha[r % channels]]]], np.float32)
+            assert oracle.run("snake1d", rows[r].reshape(1, 1, -1), a, z) == 0
+            assert oracle.run("abs_max", z, out) == 0
+            best[t] = max(best[t], int(out.view(np.uint32)[0]))
+
+    workers = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    for w in workers:
+        w.start()
+    for w in workers:
+        w.join()
+    return np.uint32(max(best))
 
 
 def test_element_wise_beyond_two_to_the_32_elements(m3, gpu):
