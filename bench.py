@@ -76,6 +76,9 @@ def shardsmod():
 METRIC = ("achieved HBM GB/s (fraction of B200 peak) per op; "
           "elems/s at 1/2/4/8 GPUs vs CPU")
 L2_NOTE = "256 MiB buffer written, then another 256 MiB read, between timed steps"
+REFERENCE_C5_NOTE = ("; SNAKE1D by the reference's CPU provider, then the abs-max and the "
+                     "waveform clamp loop (no reference operators) by the oracle's C "
+                     "restatements on the host")
 
 F32, F16, BF16 = 0, 1, 2
 
@@ -390,6 +393,29 @@ class C5(Config):
         shape = self.shape(scale)
         return {"x": rng.normal(4, 0, 0.0, 0.5, int(np.prod(shape))).reshape(shape)}
 
+    def reference_build(self, m3, g, rng, scale=1.0):
+        """The reference has SNAKE1D but no abs-max or clamp operator (its
+        waveform assembly clamps in a host loop, src/m3_waveform.c:360-380):
+        its graph stops at z, and the CPU leg finishes each run with the
+        oracle's restatements of the abs-max and of that clamp loop."""
+        alpha = rng.uniform(4, 1, 0.2, 2.0, self.channels).reshape(1, self.channels, 1)
+        x = g.value(m3.INPUT, m3.F32, self.shape(scale))
+        va = g.constant(m3.F32, alpha)
+        z = g.inferred("SNAKE1D", [x, va], m3.OUTPUT, m3.F32)
+        g.node("SNAKE1D", [x, va], [z])
+        return {"x": x}, [z]
+
+    def reference_finish(self, oracle):
+        """Host work after each reference run: abs-max and clamp of z."""
+        def finish(session, outputs, buffers):
+            z = session.read(outputs[0], out=buffers.setdefault(
+                "z", np.empty(session.values[outputs[0]][1], np.float32)))
+            y = buffers.setdefault("y", np.empty_like(z))
+            m = buffers.setdefault("m", np.zeros(1, np.float32))
+            assert oracle.run("abs_max", z, m) == 0
+            assert oracle.run("clamp_unit", z, y) == 0
+        return finish
+
     def inputs_device(self, m3, torch, device, scale=1.0):
         shape = self.shape(scale)
         x = torch.empty(int(np.prod(shape)), dtype=torch.float32, device=device)
@@ -413,7 +439,8 @@ def config_dict(cfg, world: int) -> dict:
             "shards": world, "shard_axis": cfg.shard_axis_name,
             "split": "one fixed tensor split across the ranks (strong scaling)",
             "l2": L2_NOTE,
-            "parallelism": (f"{world}-way {cfg.shard_axis_name} shards" +
+            "parallelism": ("one GPU" if world == 1 else
+                            f"{world}-way {cfg.shard_axis_name} shards" +
                             (", NCCL all-reduce(max) of the abs-max" if cfg.name == "c5" else
                              ", no data-path collective"))}
 
@@ -557,21 +584,38 @@ class ClockSampler:
 
 # ----------------------------------------------------- reference timing
 
+class ReferenceRunner:
+    """One reference CPU-only session over a slice of a configuration, and
+    the host work the reference does after each run (C5's abs-max/clamp)."""
+
+    def __init__(self, m3, lib, rng, config, scale, oracle):
+        g = m3.Graph(lib=lib)
+        build = getattr(config, "reference_build", config.build)
+        handles, self.outputs = build(m3, g, rng, scale)
+        self.session = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
+        data = config.inputs_host(rng, scale)
+        for name, vid in handles.items():
+            self.session.write(vid, data[name])
+        finish = getattr(config, "reference_finish", None)
+        self.finish = finish(oracle) if finish is not None else None
+        self.buffers = {}
+
+    def run(self):
+        self.session.run()
+        if self.finish is not None:
+            self.finish(self.session, self.outputs, self.buffers)
+
+    def close(self):
+        self.session.close()
+
+
 def reference_sessions(m3, lib, rng, config, scale, threads):
     """`threads` reference CPU-only sessions, each over its own 1/threads
     slice of the scaled workload along the configuration's shard axis (the
     data of every slice is the configuration's seeded stream)."""
-    sessions = []
-    per = scale / threads
-    for _ in range(threads):
-        g = m3.Graph(lib=lib)
-        handles, _ = config.build(m3, g, rng, per)
-        s = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
-        data = config.inputs_host(rng, per)
-        for name, vid in handles.items():
-            s.write(vid, data[name])
-        sessions.append(s)
-    return sessions
+    oracle = oraclemod()
+    return [ReferenceRunner(m3, lib, rng, config, scale / threads, oracle)
+            for _ in range(threads)]
 
 
 def time_reference(sessions, runs):
@@ -620,7 +664,8 @@ def cpu_baseline(m3, oracle, config, budget_seconds):
             "cores": 1, "kind": "reference",
             "sample": f"{config.name} at {scale:.4g} of full size along its "
                       f"{config.shard_axis_name} axis (median of 3 steps, {sec:.2f} s each), "
-                      "reference CPU-only m3_session_run, 1 thread",
+                      "reference CPU-only m3_session_run, 1 thread" +
+                      (REFERENCE_C5_NOTE if config.name == "c5" else ""),
             "elems_per_s": config.elements(scale) / sec}
 
 
@@ -652,7 +697,8 @@ def run_reference_arm(args, headline):
         value = config.algorithmic_bytes(scale) / sec / 1e9
         sample = (f"{config.name} at {scale:.4g} of full size along its {config.shard_axis_name} "
                   f"axis per step, split into {threads} slices run by {threads} threads, each its "
-                  "own reference CPU-only session (libm3ref.so; inputs from the reference RNG)")
+                  "own reference CPU-only session (libm3ref.so; inputs from the reference RNG)" +
+                  (REFERENCE_C5_NOTE if config.name == "c5" else ""))
         return value, sec, scale, sample
 
     value, sec, scale, sample = measure(headline, args.ref_seconds)

@@ -520,6 +520,35 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         }
         return m3c_launch_softmax(&p, b->stream);
     }
+    case (int)M3_OP_ROW_SUM: {
+        const m3_tensor_view *in = c->descriptor.copy.input;
+        m3c_softmax_params p;
+        const void *data;
+
+        code = dense_input(b, in, index, &data, temporary);
+        if (code != 0) {
+            return code;
+        }
+        memset(&p, 0, sizeof(p));
+        p.input = data;
+        p.in_dtype = (int32_t)in->metadata.dtype;
+        p.width = in->metadata.shape[in->metadata.rank - 1U];
+        p.rows = p.width ? in->metadata.element_count / p.width : 0U;
+        p.status = b->status;
+        p.softmax_command = UINT32_MAX;
+        p.topk_command = UINT32_MAX;
+        p.skip_before = index;
+        p.row_sums = (float *)(view_base(b, c->descriptor.copy.output) +
+                               c->descriptor.copy.output->byte_offset);
+        p.rowsum_command = index;
+        if (p.width == 0U) {
+            /* empty rows sum to +0 */
+            return (int)cudaMemsetAsync(p.row_sums, 0,
+                                        c->descriptor.copy.output->metadata.byte_count,
+                                        b->stream);
+        }
+        return m3c_launch_softmax(&p, b->stream);
+    }
     case M3_OP_CATEGORICAL: {
         const m3_tensor_view *probabilities = c->descriptor.categorical.probabilities;
         const m3_tensor_view *uniforms = c->descriptor.categorical.uniforms;

@@ -81,7 +81,7 @@ const char *m3c_kind_name(m3_op_kind kind);
 
 typedef enum {
     M3C_LAUNCH_EW = 0,
-    M3C_LAUNCH_SOFTMAX,     /* softmax and/or top-k over the same rows */
+    M3C_LAUNCH_SOFTMAX,     /* softmax, top-k and/or row sums of the same rows */
     M3C_LAUNCH_NORM,        /* RMSNorm / LayerNorm, optional residual add */
     M3C_LAUNCH_CATEGORICAL  /* categorical sampling: row_in probabilities,
                                row_in_b uniforms, row_out indices */
@@ -125,6 +125,7 @@ typedef struct {
     m3c_ref row_out;               /* softmax probs / norm output */
     m3c_ref row_out2;              /* top-k values */
     m3c_ref row_out3;              /* top-k indices */
+    m3c_ref row_out4;              /* row sums */
     m3c_ref norm_scale;
     m3c_ref norm_bias;
     bool layer_norm;
@@ -132,6 +133,7 @@ typedef struct {
     uint64_t k;
     uint32_t command_a;            /* softmax command */
     uint32_t command_b;            /* top-k command */
+    uint32_t command_c;            /* row-sum command */
     char text[96];
 } m3c_launch;
 

@@ -166,6 +166,10 @@ typedef struct {
     uint64_t k;
     uint32_t topk_command;
     uint32_t skip_before;       /* skip when a command < this failed */
+    /* row sums (NULL: none): F32 [rows], left to right in F32 */
+    float *row_sums;
+    uint32_t rowsum_command;
+    uint32_t reserved;
 } m3c_softmax_params;
 
 typedef struct {
@@ -207,6 +211,10 @@ typedef struct {
 } m3c_categorical_params;
 
 int m3c_launch_categorical(const m3c_categorical_params *params, void *stream);
+
+/* The warp-specialised SOFTMAX/TOP_K(k <= 1)/ROW_SUM pipeline for F32 rows of
+ * 512 or 1024 elements (m3c_ring.cu); -1 when it does not apply. */
+int m3c_launch_softmax_ring(const m3c_softmax_params *params, void *stream);
 
 /* The words a sharded session's ranks agree on after each run: the bit
  * patterns of its global reductions (ABS_MAX outputs) and the complement of

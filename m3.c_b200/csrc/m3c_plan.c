@@ -9,8 +9,8 @@
  * Fusion.  Consecutive element-wise nodes over one iteration shape become one
  * launch; their intermediates stay in registers when nothing outside the
  * group reads them.  A residual ADD feeding RMSNorm/LayerNorm becomes the
- * norm kernel's prologue; SOFTMAX and TOP_K of one input share one row
- * kernel.
+ * norm kernel's prologue; SOFTMAX, TOP_K and ROW_SUM of one input share one
+ * row kernel.
  *
  * Atomic commit.  Operators with all-or-nothing data checks (SOFTMAX and
  * TOP_K reject NaN, CAST to I32 rejects out-of-range values, ABS_MAX rejects
@@ -52,6 +52,7 @@ static m3_status regular_schema(m3_op_kind kind, schema_t *schema,
     case M3_OP_TANH:
     case (int)M3_OP_ABS_MAX:
     case (int)M3_OP_CLAMP_UNIT:
+    case (int)M3_OP_ROW_SUM:
         schema->inputs = 1U;
         return M3_STATUS_OK;
     case M3_OP_ADD:
@@ -1062,12 +1063,29 @@ static m3_status flush_ew(planner *p, node_list *list, m3_error *error)
     return status;
 }
 
-/* Row launch for SOFTMAX and/or TOP_K reading one input. */
+static bool row_pass_kind(m3_op_kind kind)
+{
+    return kind == M3_OP_SOFTMAX || kind == M3_OP_TOP_K ||
+           kind == M3_OP_ROW_SUM;
+}
+
+static int row_pass_bit(m3_op_kind kind)
+{
+    return kind == M3_OP_SOFTMAX ? 0 : kind == M3_OP_TOP_K ? 1 : 2;
+}
+
+/* Row launch for SOFTMAX, TOP_K and/or ROW_SUM reading one input (one row
+ * pass).  With a data-checked sibling every output is shadowed under its own
+ * command, so a NaN failure commits exactly the outputs of the commands
+ * before the failing one. */
 static m3_status plan_softmax(planner *p, size_t n, size_t count,
                               m3_error *error)
 {
     m3c_launch launch;
     size_t i;
+    bool checked = false;
+    char parts[3][12] = {"", "", ""};
+    int named = 0;
     m3_status status = M3_STATUS_OK;
 
     memset(&launch, 0, sizeof(launch));
@@ -1078,12 +1096,17 @@ static m3_status plan_softmax(planner *p, size_t n, size_t count,
     launch.row_out.value = NO_VALUE;
     launch.row_out2.value = NO_VALUE;
     launch.row_out3.value = NO_VALUE;
+    launch.row_out4.value = NO_VALUE;
     launch.row_in_b.value = NO_VALUE;
     launch.row_sum_out.value = NO_VALUE;
     launch.norm_scale.value = NO_VALUE;
     launch.norm_bias.value = NO_VALUE;
     launch.command_a = UINT32_MAX;
     launch.command_b = UINT32_MAX;
+    launch.command_c = UINT32_MAX;
+    for (i = 0U; i < count; ++i) {
+        checked = checked || p->graph->nodes[n + i].kind != M3_OP_ROW_SUM;
+    }
     for (i = 0U; i < count && status == M3_STATUS_OK; ++i) {
         const m3_graph_node_desc *node = &p->graph->nodes[n + i];
 
@@ -1091,6 +1114,12 @@ static m3_status plan_softmax(planner *p, size_t n, size_t count,
             launch.command_a = (uint32_t)(n + i);
             status = write_ref(p, node->outputs[0], true, (uint32_t)(n + i),
                                &launch.row_out, error);
+            (void)snprintf(parts[named++], sizeof(parts[0]), "SOFTMAX");
+        } else if (node->kind == M3_OP_ROW_SUM) {
+            launch.command_c = (uint32_t)(n + i);
+            status = write_ref(p, node->outputs[0], checked, (uint32_t)(n + i),
+                               &launch.row_out4, error);
+            (void)snprintf(parts[named++], sizeof(parts[0]), "ROW_SUM");
         } else {
             launch.command_b = (uint32_t)(n + i);
             launch.k = node->parameters.top_k.k;
@@ -1100,12 +1129,11 @@ static m3_status plan_softmax(planner *p, size_t n, size_t count,
                 status = write_ref(p, node->outputs[1], true,
                                    (uint32_t)(n + i), &launch.row_out3, error);
             }
+            (void)snprintf(parts[named++], sizeof(parts[0]), "TOP_K");
         }
     }
-    (void)snprintf(launch.text, sizeof(launch.text), "row[%s%s%s]",
-                   launch.command_a != UINT32_MAX ? "SOFTMAX" : "",
-                   count == 2U ? "+" : "",
-                   launch.command_b != UINT32_MAX ? "TOP_K" : "");
+    (void)snprintf(launch.text, sizeof(launch.text), "row[%s%s%s%s%s]", parts[0],
+                   named > 1 ? "+" : "", parts[1], named > 2 ? "+" : "", parts[2]);
     if (status == M3_STATUS_OK) {
         status = push_launch(p, &launch, error);
         if (count > 1U) {
@@ -1310,17 +1338,22 @@ static m3_status fuse(planner *p, bool fuse_enabled, m3_error *error)
             ++n;
             continue;
         }
-        if (node->kind == M3_OP_SOFTMAX || node->kind == M3_OP_TOP_K) {
+        if (row_pass_kind(node->kind)) {
+            /* siblings: consecutive SOFTMAX / TOP_K / ROW_SUM nodes of
+             * distinct kinds reading the same input share one row pass */
             size_t count = 1U;
+            unsigned seen = 1U << row_pass_bit(node->kind);
 
-            if (fuse_enabled && n + 1U < graph->node_count) {
-                const m3_graph_node_desc *next = &graph->nodes[n + 1U];
+            while (fuse_enabled && count < 3U && n + count < graph->node_count) {
+                const m3_graph_node_desc *next = &graph->nodes[n + count];
 
-                if ((next->kind == M3_OP_SOFTMAX || next->kind == M3_OP_TOP_K) &&
-                    next->kind != node->kind &&
-                    next->inputs[0] == node->inputs[0]) {
-                    count = 2U;
+                if (!row_pass_kind(next->kind) ||
+                    (seen & (1U << row_pass_bit(next->kind))) != 0U ||
+                    next->inputs[0] != node->inputs[0]) {
+                    break;
                 }
+                seen |= 1U << row_pass_bit(next->kind);
+                ++count;
             }
             status = plan_softmax(p, n, count, error);
             n += count;
@@ -1410,6 +1443,7 @@ static m3_status mark_needed_slots(const m3_graph *graph, m3c_plan *plan,
         } else if (launch->kind == M3C_LAUNCH_SOFTMAX) {
             mark_ref(plan, launch->row_out2);
             mark_ref(plan, launch->row_out3);
+            mark_ref(plan, launch->row_out4);
         } else {
             mark_ref(plan, launch->row_in_b);
             mark_ref(plan, launch->row_sum_out);

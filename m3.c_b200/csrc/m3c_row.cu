@@ -360,6 +360,15 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
         tile_copy(smem, in, row0, live, nvec, raw_pitch);
         cp_async_wait_all();
         __syncthreads();
+        if (p.row_sums != nullptr) {
+            // ROW_SUM: the left-to-right F32 sums of the raw rows, one row
+            // per lane of warp 0, before the exponentials overwrite them
+            if (threadIdx.x < static_cast<unsigned>(live)) {
+                p.row_sums[row0 + threadIdx.x] =
+                    ordered_raw<EB, 0>(smem + threadIdx.x * raw_pitch, nvec, IN, 0.0f);
+            }
+            __syncthreads();
+        }
 
         // maximum, its first index and NaN, for the warp's share of its row
         const bool active = r < live;
@@ -400,7 +409,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 6)
         }
         // a row of -inf only: the first index (NaN rows fail the command)
         if (best_i == 0xffffffffu) best_i = 0u;
-        if (active && nan && sub == 0 && lane == 0) {
+        if (active && nan && sub == 0 && lane == 0 && first_command != 0xffffffffu) {
             record_failure(p.status, first_command);
         }
         if (active && p.top_values != nullptr && sub == 0) {
@@ -582,7 +591,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 3)
         warp_best(best, best_i);
         nan = __any_sync(0xffffffffu, nan);
         if (best_i == 0xffffffffu) best_i = 0u;  // a row of -inf only
-        if (nan && lane == 0) record_failure(p.status, first_command);
+        if (nan && lane == 0 && first_command != 0xffffffffu) record_failure(p.status, first_command);
         const uint64_t row = tile * TILE_WARPS + r;
         if (p.top_values != nullptr && lane == 0) {
             p.top_values[row] = best;
@@ -898,6 +907,18 @@ __device__ void softmax_row(const m3c_softmax_params &p, uint64_t row, float *sm
             best_i = static_cast<uint32_t>(j);
         }
     });
+    if (p.row_sums != nullptr) {
+        // ROW_SUM: the left-to-right F32 sum of the row, on one lane
+        __syncwarp();
+        if (lane == 0) {
+            float s = 0.0f;
+            for (uint64_t j = 0; j < width; ++j) {
+                s = __fadd_rn(s, smem_row ? smem_row[j] : load_elem(in_row, p.in_dtype, j));
+            }
+            p.row_sums[row] = s;
+        }
+        __syncwarp();
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float other = __shfl_xor_sync(0xffffffffu, maximum, off);
@@ -906,7 +927,7 @@ __device__ void softmax_row(const m3c_softmax_params &p, uint64_t row, float *sm
     }
     if (__any_sync(0xffffffffu, nan) && lane == 0) {
         const uint32_t first = p.softmax_command < p.topk_command ? p.softmax_command : p.topk_command;
-        record_failure(p.status, first);
+        if (first != 0xffffffffu) record_failure(p.status, first);
     }
     __syncwarp();
     if (p.top_values != nullptr) {
@@ -1171,7 +1192,7 @@ template <int IN, int OUT>
 int softmax_tile(const m3c_softmax_params &p, const Tile &g, size_t smem, void *stream)
 {
     // widths with a compiled geometry: 8-row tiles in two stages
-    if (IN == M3C_F32 && g.rows == TILE_WARPS && g.group == 1 && p.k <= 1 &&
+    if (IN == M3C_F32 && g.rows == TILE_WARPS && g.group == 1 && p.k <= 1 && p.row_sums == nullptr &&
         (g.width == 1024 || g.width == 512)) {
         const size_t stages = 2u * static_cast<size_t>(TILE_WARPS) * static_cast<size_t>(g.raw_pitch);
         if (g.width == 1024) {
@@ -1251,6 +1272,10 @@ void row_shape(uint64_t width, int *rows_per_cta, size_t *smem_bytes, bool *fits
 
 extern "C" int m3c_launch_softmax(const m3c_softmax_params *params, void *stream)
 {
+    if (params->rows > 0) {
+        const int ring = m3c_launch_softmax_ring(params, stream);
+        if (ring != -1) return ring;
+    }
     const int eb = m3c::bytes_of(params->in_dtype);
     const m3c::Tile g = m3c::tile_geometry(params->width, eb, true, false, false);
     if (g.rows > 0 && params->rows > 0 && m3c::aligned16(params->input) &&

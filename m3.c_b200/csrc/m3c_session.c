@@ -596,6 +596,20 @@ static int launch_one(m3_session *s, size_t index, bool first)
             p.top_indices = (int32_t *)ref_pointer(s, l->row_out3);
             p.k = l->k;
         }
+        p.rowsum_command = l->command_c;
+        if (l->row_out4.value != UINT32_MAX) {
+            p.row_sums = (float *)ref_pointer(s, l->row_out4);
+            if (p.width == 0U) {
+                /* rows of no element sum to +0 */
+                cudaError_t code = cudaMemsetAsync(
+                    p.row_sums, 0, s->metadata[l->row_out4.value].byte_count,
+                    s->stream);
+
+                if (code != cudaSuccess) {
+                    return (int)code;
+                }
+            }
+        }
         return m3c_launch_softmax(&p, s->stream);
     }
     {

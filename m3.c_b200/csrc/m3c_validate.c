@@ -521,6 +521,36 @@ static m3_status validate_abs_max(const m3c_vcommand *c, m3_error *error)
     return check_alias(&c->out[0], &c->in[0], false, "abs-max", error);
 }
 
+/* Extension: row sums of a float tensor into F32 [..., 1]. */
+static m3_status validate_row_sum(const m3c_vcommand *c, m3_error *error)
+{
+    const m3_tensor_metadata *in;
+    const m3_tensor_metadata *out;
+    bool shape_ok;
+    uint8_t axis;
+    m3_status status = check_view(&c->in[0], false, "row-sum input", error);
+
+    if (status == M3_STATUS_OK) {
+        status = check_view(&c->out[0], true, "row-sum output", error);
+    }
+    if (status != M3_STATUS_OK) {
+        return status;
+    }
+    in = c->in[0].metadata;
+    out = c->out[0].metadata;
+    shape_ok = in->rank != 0U && out->rank == in->rank &&
+               out->shape[in->rank - 1U] == 1U;
+    for (axis = 0U; shape_ok && axis + 1U < in->rank; ++axis) {
+        shape_ok = out->shape[axis] == in->shape[axis];
+    }
+    if (!m3c_dtype_float(in->dtype) || out->dtype != M3_DTYPE_F32 || !shape_ok) {
+        return m3c_error_set(
+            error, M3_STATUS_INVALID_ARGUMENT,
+            "row-sum requires a float input and F32 output [..., 1]");
+    }
+    return check_alias(&c->out[0], &c->in[0], false, "row-sum", error);
+}
+
 /* Extension: bit-preserving clamp of F32 to [-1, 1]. */
 static m3_status validate_clamp(const m3c_vcommand *c, m3_error *error)
 {
@@ -555,6 +585,7 @@ bool m3c_kind_supported(m3_op_kind kind)
     case M3_OP_TANH:
     case (int)M3_OP_ABS_MAX:
     case (int)M3_OP_CLAMP_UNIT:
+    case (int)M3_OP_ROW_SUM:
         return true;
     default:
         return false;
@@ -578,6 +609,7 @@ const char *m3c_kind_name(m3_op_kind kind)
     case M3_OP_TANH: return "TANH";
     case (int)M3_OP_ABS_MAX: return "ABS_MAX";
     case (int)M3_OP_CLAMP_UNIT: return "CLAMP_UNIT";
+    case (int)M3_OP_ROW_SUM: return "ROW_SUM";
     default: return "UNSUPPORTED";
     }
 }
@@ -626,6 +658,9 @@ m3_status m3c_validate(const m3c_vcommand *command, m3_error *error)
         break;
     case (int)M3_OP_CLAMP_UNIT:
         status = validate_clamp(command, error);
+        break;
+    case (int)M3_OP_ROW_SUM:
+        status = validate_row_sum(command, error);
         break;
     default:
         status = m3c_error_set(error, M3_STATUS_UNSUPPORTED,

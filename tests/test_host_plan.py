@@ -300,3 +300,66 @@ def test_categorical_plans_as_checked_row_launch(m3):
     with pytest.raises(m3.M3Failure) as failure:
         m3.graph_plan(bad)
     assert failure.value.message == "categorical dtype or shape is invalid"
+
+
+def test_row_sum_plans_and_fuses_as_a_row_pass_sibling(m3):
+    """ROW_SUM (extension) alone is a row launch; beside SOFTMAX and TOP_K of
+    the same input the three share one row pass, and in that launch every
+    output is committed per command (shadow buffers); shape and dtype rules."""
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F16, (6, 40))
+    r = g.inferred("ROW_SUM", [x], m3.OUTPUT, m3.F32)
+    g.node("ROW_SUM", [x], [r])
+    assert g.values[r][:2] == (m3.F32, (6, 1))
+    info, report, text = m3.graph_plan(g)
+    assert text == "row[ROW_SUM]" and report.launch_count == 1 and report.shadow_bytes == 0
+    g = m3.Graph()
+    x = g.value(m3.INPUT, m3.F32, (6, 40))
+    p = g.inferred("SOFTMAX", [x], m3.OUTPUT, m3.F32)
+    g.node("SOFTMAX", [x], [p])
+    tv = g.inferred("TOP_K", [x], m3.OUTPUT, m3.F32, 0, k=1)
+    ti = g.inferred("TOP_K", [x], m3.OUTPUT, m3.I32, 1, k=1)
+    g.node("TOP_K", [x], [tv, ti], k=1)
+    r = g.inferred("ROW_SUM", [x], m3.OUTPUT, m3.F32)
+    g.node("ROW_SUM", [x], [r])
+    info, report, text = m3.graph_plan(g)
+    assert text == "row[SOFTMAX+TOP_K+ROW_SUM]"
+    assert report.launch_count == 1 and report.fused_node_count == 3
+    assert m3.graph_plan(g, fuse=False)[1].launch_count == 3
+    for shape, dtype in (((6, 2), m3.F32), ((6, 1), m3.F16), ((1, 6), m3.F32)):
+        bad = m3.Graph()
+        x = bad.value(m3.INPUT, m3.F32, (6, 40))
+        o = bad.value(m3.OUTPUT, dtype, shape)
+        bad.node("ROW_SUM", [x], [o])
+        with pytest.raises(m3.M3Failure) as failure:
+            m3.graph_plan(bad)
+        assert "row-sum" in failure.value.message
+
+
+def test_out_of_scope_inference_is_unsupported(m3):
+    """Shape inference covers the provider's operators; the reference's
+    other kinds are rejected at once."""
+    g = m3.Graph()
+    a = g.value(m3.INPUT, m3.F32, (2, 3))
+    b = g.value(m3.INPUT, m3.F32, (3, 4))
+    with pytest.raises(m3.M3Failure) as failure:
+        g.inferred("MATMUL", [a, b], m3.OUTPUT, m3.F32)
+    assert failure.value.status == m3.UNSUPPORTED
+
+
+def test_reference_rng_words_restated(oracle, ref):
+    """The oracle's PCG32 word stream, which the benchmark's reference arm
+    scales into uniforms, is the reference's m3_rng_u32 stream."""
+    ref.m3_rng_seed.argtypes = [ctypes.c_void_p, ctypes.c_uint64,
+                                ctypes.c_uint64, ctypes.c_void_p]
+    ref.m3_rng_u32.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    state = ctypes.create_string_buffer(64)
+    for seed, sequence in ((1, 1), (4, 1), (99, 5)):
+        ref.m3_rng_seed(state, seed, sequence, None)
+        word = ctypes.c_uint32()
+        theirs = []
+        for _ in range(513):
+            ref.m3_rng_u32(state, ctypes.byref(word), None)
+            theirs.append(word.value)
+        assert np.array_equal(oracle.pcg32_words(seed, sequence, 513),
+                              np.array(theirs, np.uint32))

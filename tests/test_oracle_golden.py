@@ -226,6 +226,30 @@ def test_abs_max_extension(oracle):
     assert out[0] == 7
 
 
+def test_row_sum_extension(oracle):
+    """Row sums accumulate left to right in F32: a row whose tree sum
+    differs from its sequential sum shows the order."""
+    x = np.array([[1.0, 2.0 ** -24, 2.0 ** -24, 2.0 ** -24, 2.0 ** -24]], np.float32)
+    out = np.zeros((1, 1), np.float32)
+    assert oracle.run("row_sum", x, out) == 0
+    assert out[0, 0] == np.float32(1.0)          # each 2^-24 rounds away
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((7, 33)).astype(np.float32)
+    want = np.zeros(7, np.float32)
+    for j in range(33):
+        want = (want + x[:, j]).astype(np.float32)
+    out = np.zeros((7, 1), np.float32)
+    assert oracle.run("row_sum", x, out) == 0
+    assert np.array_equal(out[:, 0].view(np.uint32), want.view(np.uint32))
+    h = oracle.to_f16(x)
+    assert oracle.run("row_sum", (h, oracle.F16), out) == 0
+    widened = oracle.widen(h, oracle.F16)
+    want = np.zeros(7, np.float32)
+    for j in range(33):
+        want = (want + widened[:, j]).astype(np.float32)
+    assert np.array_equal(out[:, 0].view(np.uint32), want.view(np.uint32))
+
+
 # ----------------------------------- 2. against the compiled reference
 
 
