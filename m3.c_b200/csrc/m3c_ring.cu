@@ -11,30 +11,36 @@
 // with independent work.  So the CTA is split by role, and the chain gets a
 // scheduler of its own:
 //
-//   warp 0 (sub-partition 0)  the chain warp: lane r runs the ordered sum of
-//                             row r of a group, straight out of shared memory
-//                             (rows are padded by 16 bytes, so the 8 lanes of
-//                             each quarter-warp phase read 8 distinct bank
-//                             groups);
+//   warp 0 (sub-partition 0)  the chain warp.  Its lanes are staggered: the
+//                             CTA's local row i is summed by lane i % 32 over
+//                             chunks i .. i+31 of 32 elements each, so at
+//                             every chunk boundary exactly one lane finishes a
+//                             row (publishes its sum) and starts the next.
+//                             Rows enter and leave the chain one at a time;
+//                             the 16-byte row padding keeps the 8 lanes of
+//                             each quarter-warp load phase on distinct bank
+//                             groups;
 //   warp 4 (sub-partition 0)  the producer: one thread issues a 1-D TMA bulk
 //                             copy (cp.async.bulk, global -> shared, mbarrier
 //                             completion, no tensor map, no multicast) per
-//                             row into a free slot of the ring;
+//                             row as soon as the row's slot is free;
 //   warps 8, 12               idle (they leave sub-partition 0 to the chain);
-//   the 12 warps of sub-partitions 1-3, the row warps: per row, max / first
-//                             argmax / NaN in one pass, the top-1 outputs, the
-//                             exponentials written in place; after the chain,
-//                             the probabilities e / sum with Markstein's
+//   the 12 warps of sub-partitions 1-3, the row warps: row warp w owns rows
+//                             i = w (mod 12); for each it computes max /
+//                             first argmax / NaN in one pass, writes the
+//                             top-1 outputs and the exponentials in place, and
+//                             36 rows later (once the chain is done with that
+//                             row) the probabilities e / sum with Markstein's
 //                             quotient, streamed to HBM.
 //
-// The ring holds two groups of G rows (G = 28 for 4 KiB rows: 56 slots, the
-// whole 227 KiB of shared memory); while the chain warp sums group g, the
-// row warps compute the exponentials of group g+1 and write out group g-1,
-// and the producer refills group g-1's slots with group g+1's successor.
-// Every wait is an mbarrier phase (bounded: a wait that runs past its
-// deadline records an internal failure in the status word and the thread
-// leaves its loop); the dependency graph of the phases has no cycle, so the
-// bound is never reached by a correct run.
+// Row i lives in ring slot i % SLOTS (55 slots of 4 KiB + 16, nearly all of
+// the 227 KiB of shared memory).  Four mbarriers per slot carry the row
+// through its life: full (TMA landed), expd (exponentials ready), summed
+// (the chain is done), empty (written out; the producer may reuse the slot).
+// Every wait is bounded: a wait past its deadline records an internal
+// failure in the status word and the thread leaves its loop.  Each row
+// depends only on rows with smaller indices, so the waits form no cycle and
+// the bound is never reached by a correct run.
 
 #include <cuda_runtime.h>
 
@@ -57,14 +63,16 @@ template <int WIDTH>
 struct RingGeometry {
     static constexpr int BYTES = WIDTH * 4;
     static constexpr int PITCH = BYTES + 16;
-    static constexpr int VPL = WIDTH / 128;          // 16-byte vectors per lane
-    static constexpr int G = WIDTH == 1024 ? 28 : 32;  // rows per group
-    static constexpr int SLOTS = 2 * G;
-    // per slot: full, empty barriers; max, sum, reciprocal, flags
-    static constexpr int SLOT_STATE = 8 + 8 + 4 + 4 + 4 + 4;
-    static constexpr int GROUP_STATE = 2 * (8 + 8);      // exp_done, summed
+    static constexpr int VPL = WIDTH / 128;            // 16-byte vectors per lane
+    static constexpr int CHUNKS = 32;                  // chain chunks per row (one per lane)
+    static constexpr int VPC = WIDTH / 128;            // 16-byte vectors per chunk
+    static constexpr int SLOTS = WIDTH == 1024 ? 55 : 96;
+    static constexpr int LAG = 36;                     // exp(i) ... out(i - LAG)
+    // per slot: full, expd, summed, empty barriers; sum, reciprocal; flags,
+    // issued
     static constexpr int ROWS_BYTES = SLOTS * PITCH;
-    static constexpr int SMEM = ROWS_BYTES + SLOTS * SLOT_STATE + GROUP_STATE + SLOTS;
+    static constexpr int SMEM = ROWS_BYTES + SLOTS * (4 * 8 + 4 + 4 + 1 + 1);
+    static_assert(LAG % 12 == 0 && LAG >= 32, "a row warp's out lag: its own rows, after the chain");
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p)
@@ -156,21 +164,22 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     softmax_ring_kernel(const __grid_constant__ m3c_softmax_params p)
 {
     using Geo = RingGeometry<WIDTH>;
-    constexpr int G = Geo::G;
     constexpr int SLOTS = Geo::SLOTS;
     constexpr int PITCH = Geo::PITCH;
     constexpr int VPL = Geo::VPL;
+    constexpr int CHUNKS = Geo::CHUNKS;
+    constexpr int VPC = Geo::VPC;
+    constexpr int LAG = Geo::LAG;
     extern __shared__ __align__(16) unsigned char smem[];
     unsigned char *rows_area = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Geo::ROWS_BYTES);
-    uint64_t *empty = full + SLOTS;
-    uint64_t *exp_done = empty + SLOTS;            // [2]
-    uint64_t *summed = exp_done + 2;               // [2]
-    float *slot_max = reinterpret_cast<float *>(summed + 2);
-    float *slot_sum = slot_max + SLOTS;
+    uint64_t *expd = full + SLOTS;
+    uint64_t *summed = expd + SLOTS;
+    uint64_t *empty = summed + SLOTS;
+    float *slot_sum = reinterpret_cast<float *>(empty + SLOTS);
     float *slot_rcp = slot_sum + SLOTS;
-    int *slot_flags = reinterpret_cast<int *>(slot_rcp + SLOTS);
-    unsigned char *slot_issued = reinterpret_cast<unsigned char *>(slot_flags + SLOTS);
+    unsigned char *slot_flags = reinterpret_cast<unsigned char *>(slot_rcp + SLOTS);
+    unsigned char *slot_issued = slot_flags + SLOTS;
     __shared__ int skip;
 
     const int warp = static_cast<int>(threadIdx.x) / 32;
@@ -184,8 +193,6 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     const uint64_t row_begin = p.rows * blockIdx.x / gridDim.x;
     const uint64_t row_end = p.rows * (blockIdx.x + 1) / gridDim.x;
     const int local_rows = static_cast<int>(row_end - row_begin);
-    const int groups = (local_rows + G - 1) / G;
-    auto group_rows = [&](int g) { return local_rows - g * G < G ? local_rows - g * G : G; };
 
     if (threadIdx.x == 0) {
         skip = failed_before(p.status, p.skip_before) ? 1 : 0;
@@ -194,12 +201,10 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         }
         for (int s = 0; s < SLOTS; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&expd[s], 32);
+            mbar_init(&summed[s], 1);
             mbar_init(&empty[s], 32);
             slot_issued[s] = 0;
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&exp_done[b], 32 * G);
-            mbar_init(&summed[b], 32);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -212,21 +217,18 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     if (warp == PRODUCER_WARP) {
         if (lane != 0) return;
         bool ok = true;
-        for (int g = 0; g < groups && ok; ++g) {
-            const int live = group_rows(g);
-            for (int r = 0; r < live; ++r) {
-                const int s = (g & 1) * G + r;
-                if (g >= 2 && !mbar_wait(&empty[s], ((g >> 1) + 1) & 1)) {
-                    timed_out(p.status, first_command);
-                    ok = false;
-                    break;
-                }
-                mbar_expect_tx(&full[s], Geo::BYTES);
-                bulk_load(rows_area + s * PITCH, in + (row_begin + g * G + r) * (WIDTH / 4), Geo::BYTES,
-                          &full[s]);
-                // bit 0: a copy was issued; bit 1: the parity of its phase
-                slot_issued[s] = static_cast<unsigned char>(1u | (((g >> 1) & 1) << 1));
+        for (int i = 0; i < local_rows; ++i) {
+            const int s = i % SLOTS;
+            const int use = i / SLOTS;
+            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                timed_out(p.status, first_command);
+                ok = false;
+                break;
             }
+            mbar_expect_tx(&full[s], Geo::BYTES);
+            bulk_load(rows_area + s * PITCH, in + (row_begin + i) * (WIDTH / 4), Geo::BYTES, &full[s]);
+            // bit 0: a copy was issued; bit 1: the parity of its phase
+            slot_issued[s] = static_cast<unsigned char>(1u | ((use & 1) << 1));
         }
         if (!ok) {
             // let every copy this thread issued land before the CTA ends
@@ -238,48 +240,52 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     }
 
     if (warp == CHAIN_WARP) {
-        for (int g = 0; g < groups; ++g) {
-            const int b = g & 1;
-            if (!mbar_wait(&exp_done[b], (g >> 1) & 1)) {
-                timed_out(p.status, first_command);
-                return;
-            }
-            const int live = group_rows(g);
-            const int s = b * G + lane;
-            if (lane < live) {
-                const bool need = p.probs != nullptr ? (slot_flags[s] & FLAG_SPECIAL) == 0
-                                                     : p.row_sums != nullptr;
-                if (need) {
-                    // the reference's left-to-right F32 sum (of e, or of x
-                    // for ROW_SUM without SOFTMAX), two vectors ahead
-                    const float4 *v4 = reinterpret_cast<const float4 *>(rows_area + s * PITCH);
-                    float sum = 0.0f;
-                    float4 a = v4[0];
-                    float4 c = v4[1];
-#pragma unroll 4
-                    for (int v = 0; v < WIDTH / 4; v += 2) {
-                        const float4 a_next = v + 2 < WIDTH / 4 ? v4[v + 2] : a;
-                        const float4 c_next = v + 3 < WIDTH / 4 ? v4[v + 3] : c;
-                        sum = __fadd_rn(sum, a.x);
-                        sum = __fadd_rn(sum, a.y);
-                        sum = __fadd_rn(sum, a.z);
-                        sum = __fadd_rn(sum, a.w);
-                        sum = __fadd_rn(sum, c.x);
-                        sum = __fadd_rn(sum, c.y);
-                        sum = __fadd_rn(sum, c.z);
-                        sum = __fadd_rn(sum, c.w);
-                        a = a_next;
-                        c = c_next;
-                    }
+        // lane l sums rows l, l + 32, ...; row i over chunks i .. i + 31, a
+        // 32nd of the row each
+        const bool summing = p.probs != nullptr || p.row_sums != nullptr;
+        float sum = 0.0f;
+        int cur = -1;        // the row this lane sums, -1: none
+        int slot = 0;
+        bool failed = false;
+        for (int k = 0; k < local_rows + CHUNKS && !failed; ++k) {
+            if (lane == (k % 32)) {
+                if (cur >= 0) {
+                    // the row is complete: publish its sum
                     if (p.probs != nullptr) {
-                        slot_sum[s] = sum;
-                        slot_rcp[s] = __frcp_rn(sum);
-                    } else {
-                        p.row_sums[row_begin + g * G + lane] = sum;
+                        slot_sum[slot] = sum;
+                        slot_rcp[slot] = __frcp_rn(sum);
+                    } else if (p.row_sums != nullptr) {
+                        p.row_sums[row_begin + cur] = sum;
+                    }
+                    mbar_arrive(&summed[slot]);
+                }
+                cur = k < local_rows ? k : -1;
+                sum = 0.0f;
+                if (cur >= 0) {
+                    slot = cur % SLOTS;
+                    if (!mbar_wait(&expd[slot], (cur / SLOTS) & 1)) {
+                        timed_out(p.status, first_command);
+                        failed = true;
                     }
                 }
             }
-            mbar_arrive(&summed[b]);
+            failed = __any_sync(0xffffffffu, failed);
+            if (cur >= 0 && summing) {
+                // the reference's left-to-right F32 sum, 32 elements of the
+                // row (of e, or of x for ROW_SUM without SOFTMAX)
+                const float4 *v4 =
+                    reinterpret_cast<const float4 *>(rows_area + slot * PITCH) + (k - cur) * VPC;
+                float4 a[VPC];
+#pragma unroll
+                for (int j = 0; j < VPC; ++j) a[j] = v4[j];
+#pragma unroll
+                for (int j = 0; j < VPC; ++j) {
+                    sum = __fadd_rn(sum, a[j].x);
+                    sum = __fadd_rn(sum, a[j].y);
+                    sum = __fadd_rn(sum, a[j].z);
+                    sum = __fadd_rn(sum, a[j].w);
+                }
+            }
         }
         return;
     }
@@ -291,150 +297,145 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     const int rw = warp - 1 - warp / 4;
     const uint64_t out_pitch = static_cast<uint64_t>(WIDTH) * (OUT == M3C_F32 ? 4u : 2u);
 
-    auto exp_phase = [&](int g) -> bool {
-        const int live = group_rows(g);
-        for (int r = rw; r < G; r += ROW_WARPS) {
-            const int s = (g & 1) * G + r;
-            if (r < live) {
-                if (!mbar_wait(&full[s], (g >> 1) & 1)) {
-                    timed_out(p.status, first_command);
-                    return false;
-                }
-                float4 *row4 = reinterpret_cast<float4 *>(rows_area + s * PITCH);
-                float4 q[VPL];
-#pragma unroll
-                for (int k = 0; k < VPL; ++k) q[k] = row4[lane + 32 * k];
-                float m = -pos_inf;
-#pragma unroll
-                for (int k = 0; k < VPL; ++k) {
-                    m = max_nan(m, max_nan(max_nan(q[k].x, q[k].y), max_nan(q[k].z, q[k].w)));
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
-                const bool nan = m != m;
-                const uint64_t row = row_begin + static_cast<uint64_t>(g) * G + r;
-                if (nan && lane == 0 && check_command != 0xffffffffu) {
-                    record_failure(p.status, check_command);
-                }
-                if (p.top_values != nullptr) {
-                    // first index holding a value equal to the maximum (+0 ==
-                    // -0, src/m3_op_execute_sampling.c:7-12), and its value
-                    uint32_t best = 0xffffffffu;
-#pragma unroll
-                    for (int k = VPL - 1; k >= 0; --k) {
-                        const uint32_t base = static_cast<uint32_t>(lane + 32 * k) * 4u;
-                        best = q[k].w == m ? base + 3u : best;
-                        best = q[k].z == m ? base + 2u : best;
-                        best = q[k].y == m ? base + 1u : best;
-                        best = q[k].x == m ? base : best;
-                    }
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, off));
-                    if (best == 0xffffffffu) best = 0u;  // NaN row (the command fails)
-                    if (lane == 0) {
-                        p.top_values[row] = reinterpret_cast<const float *>(row4)[best];
-                        p.top_indices[row] = static_cast<int32_t>(best);
-                    }
-                }
-                if (p.probs != nullptr) {
-                    int flags = 0;
-                    if (m == pos_inf || m == -pos_inf) {
-                        // src/m3_op_execute_basic.c:165-170
-                        uint32_t infinities = 0u;
-#pragma unroll
-                        for (int k = 0; k < VPL; ++k) {
-                            infinities += (q[k].x == pos_inf) + (q[k].y == pos_inf) + (q[k].z == pos_inf) +
-                                          (q[k].w == pos_inf);
-                        }
-#pragma unroll
-                        for (int off = 16; off > 0; off >>= 1) {
-                            infinities += __shfl_xor_sync(0xffffffffu, infinities, off);
-                        }
-                        const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
-                        const bool plus = m == pos_inf;
-                        __syncwarp();
-#pragma unroll
-                        for (int k = 0; k < VPL; ++k) {
-                            row4[lane + 32 * k] = make_float4(
-                                plus && q[k].x == pos_inf ? share : 0.0f, plus && q[k].y == pos_inf ? share : 0.0f,
-                                plus && q[k].z == pos_inf ? share : 0.0f, plus && q[k].w == pos_inf ? share : 0.0f);
-                        }
-                        flags = FLAG_SPECIAL;
-                    } else {
-                        bool tiny = false;
-                        __syncwarp();   // the top-1 value was read from the row
-#pragma unroll
-                        for (int k = 0; k < VPL; ++k) {
-                            const float4 e = make_float4(expf(__fsub_rn(q[k].x, m)), expf(__fsub_rn(q[k].y, m)),
-                                                         expf(__fsub_rn(q[k].z, m)), expf(__fsub_rn(q[k].w, m)));
-                            tiny |= fminf(fminf(e.x, e.y), fminf(e.z, e.w)) < 0x1p-100f;
-                            row4[lane + 32 * k] = e;
-                        }
-                        flags = __any_sync(0xffffffffu, tiny) ? FLAG_TINY : 0;
-                    }
-                    if (lane == 0) slot_flags[s] = flags;
-                }
-            }
-            mbar_arrive(&exp_done[g & 1]);
-        }
-        return true;
-    };
-
-    auto out_phase = [&](int g) -> bool {
-        if (!mbar_wait(&summed[g & 1], (g >> 1) & 1)) {
+    // max / first argmax / NaN, top-1, exponentials in place
+    auto exp_row = [&](int i) -> bool {
+        const int s = i % SLOTS;
+        if (!mbar_wait(&full[s], (i / SLOTS) & 1)) {
             timed_out(p.status, first_command);
             return false;
         }
-        const int live = group_rows(g);
-        for (int r = rw; r < G; r += ROW_WARPS) {
-            const int s = (g & 1) * G + r;
-            if (r < live && p.probs != nullptr) {
-                const float4 *e4 = reinterpret_cast<const float4 *>(rows_area + s * PITCH);
-                const int flags = slot_flags[s];
-                const float sum = slot_sum[s];
-                const float y = slot_rcp[s];
-                unsigned char *orow = static_cast<unsigned char *>(p.probs) +
-                                      (row_begin + static_cast<uint64_t>(g) * G + r) * out_pitch;
+        float4 *row4 = reinterpret_cast<float4 *>(rows_area + s * PITCH);
+        float4 q[VPL];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) q[k] = row4[lane + 32 * k];
+        float m = -pos_inf;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            m = max_nan(m, max_nan(max_nan(q[k].x, q[k].y), max_nan(q[k].z, q[k].w)));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const bool nan = m != m;
+        const uint64_t row = row_begin + static_cast<uint64_t>(i);
+        if (nan && lane == 0 && check_command != 0xffffffffu) {
+            record_failure(p.status, check_command);
+        }
+        if (p.top_values != nullptr) {
+            // first index holding a value equal to the maximum (+0 == -0,
+            // src/m3_op_execute_sampling.c:7-12), and its value
+            uint32_t best = 0xffffffffu;
+#pragma unroll
+            for (int k = VPL - 1; k >= 0; --k) {
+                const uint32_t base = static_cast<uint32_t>(lane + 32 * k) * 4u;
+                best = q[k].w == m ? base + 3u : best;
+                best = q[k].z == m ? base + 2u : best;
+                best = q[k].y == m ? base + 1u : best;
+                best = q[k].x == m ? base : best;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, off));
+            if (best == 0xffffffffu) best = 0u;  // NaN row (the command fails)
+            if (lane == 0) {
+                p.top_values[row] = reinterpret_cast<const float *>(row4)[best];
+                p.top_indices[row] = static_cast<int32_t>(best);
+            }
+        }
+        if (p.probs != nullptr) {
+            int flags = 0;
+            if (m == pos_inf || m == -pos_inf) {
+                // src/m3_op_execute_basic.c:165-170
+                uint32_t infinities = 0u;
 #pragma unroll
                 for (int k = 0; k < VPL; ++k) {
-                    const int v = lane + 32 * k;
-                    const float4 e = e4[v];
-                    float pr[4] = {e.x, e.y, e.z, e.w};
-                    if ((flags & FLAG_SPECIAL) == 0) {
-                        if ((flags & FLAG_TINY) == 0) {
-                            // e in [2^-100, 1] and sum >= 1: Markstein's
-                            // quotient is the IEEE one
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) pr[t] = div_markstein(pr[t], sum, y);
-                        } else {
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                pr[t] = pr[t] >= 0x1p-100f ? div_markstein(pr[t], sum, y) : ring_ieee_div(pr[t], sum);
-                            }
-                        }
-                    }
-                    if (OUT == M3C_F32) {
-                        __stcs(reinterpret_cast<float4 *>(orow) + v, make_float4(pr[0], pr[1], pr[2], pr[3]));
-                    } else {
-                        uint32_t h[2];
-                        narrow_pairs<2>(OUT, pr, h);
-                        __stcs(reinterpret_cast<uint2 *>(orow) + v, make_uint2(h[0], h[1]));
-                    }
+                    infinities += (q[k].x == pos_inf) + (q[k].y == pos_inf) + (q[k].z == pos_inf) +
+                                  (q[k].w == pos_inf);
                 }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    infinities += __shfl_xor_sync(0xffffffffu, infinities, off);
+                }
+                const float share = __fdiv_rn(1.0f, __uint2float_rn(infinities));
+                const bool plus = m == pos_inf;
+                __syncwarp();
+#pragma unroll
+                for (int k = 0; k < VPL; ++k) {
+                    row4[lane + 32 * k] =
+                        make_float4(plus && q[k].x == pos_inf ? share : 0.0f, plus && q[k].y == pos_inf ? share : 0.0f,
+                                    plus && q[k].z == pos_inf ? share : 0.0f, plus && q[k].w == pos_inf ? share : 0.0f);
+                }
+                flags = FLAG_SPECIAL;
+            } else {
+                bool tiny = false;
+                __syncwarp();   // the top-1 value was read from the row
+#pragma unroll
+                for (int k = 0; k < VPL; ++k) {
+                    const float4 e = make_float4(expf(__fsub_rn(q[k].x, m)), expf(__fsub_rn(q[k].y, m)),
+                                                 expf(__fsub_rn(q[k].z, m)), expf(__fsub_rn(q[k].w, m)));
+                    tiny |= fminf(fminf(e.x, e.y), fminf(e.z, e.w)) < 0x1p-100f;
+                    row4[lane + 32 * k] = e;
+                }
+                flags = __any_sync(0xffffffffu, tiny) ? FLAG_TINY : 0;
             }
-            // the slot's reads (and the exponentials' generic-proxy writes)
-            // are ordered before the next bulk copy into it
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&empty[s]);
+            if (lane == 0) slot_flags[s] = static_cast<unsigned char>(flags);
         }
+        mbar_arrive(&expd[s]);
         return true;
     };
 
-    for (int g = 0; g < groups; ++g) {
-        if (!exp_phase(g)) return;
-        if (g > 0 && !out_phase(g - 1)) return;
+    // probabilities e / sum once the chain is done with the row; frees the slot
+    auto out_row = [&](int j) -> bool {
+        const int s = j % SLOTS;
+        if (!mbar_wait(&summed[s], (j / SLOTS) & 1)) {
+            timed_out(p.status, first_command);
+            return false;
+        }
+        if (p.probs != nullptr) {
+            const float4 *e4 = reinterpret_cast<const float4 *>(rows_area + s * PITCH);
+            const int flags = slot_flags[s];
+            const float sum = slot_sum[s];
+            const float y = slot_rcp[s];
+            unsigned char *orow = static_cast<unsigned char *>(p.probs) +
+                                  (row_begin + static_cast<uint64_t>(j)) * out_pitch;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int v = lane + 32 * k;
+                const float4 e = e4[v];
+                float pr[4] = {e.x, e.y, e.z, e.w};
+                if ((flags & FLAG_SPECIAL) == 0) {
+                    if ((flags & FLAG_TINY) == 0) {
+                        // e in [2^-100, 1] and sum >= 1: Markstein's quotient
+                        // is the IEEE one
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) pr[t] = div_markstein(pr[t], sum, y);
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            pr[t] = pr[t] >= 0x1p-100f ? div_markstein(pr[t], sum, y) : ring_ieee_div(pr[t], sum);
+                        }
+                    }
+                }
+                if (OUT == M3C_F32) {
+                    __stcs(reinterpret_cast<float4 *>(orow) + v, make_float4(pr[0], pr[1], pr[2], pr[3]));
+                } else {
+                    uint32_t h[2];
+                    narrow_pairs<2>(OUT, pr, h);
+                    __stcs(reinterpret_cast<uint2 *>(orow) + v, make_uint2(h[0], h[1]));
+                }
+            }
+        }
+        // the slot's reads (and the exponentials' generic-proxy writes) are
+        // ordered before the next bulk copy into it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&empty[s]);
+        return true;
+    };
+
+    for (int i = rw;; i += ROW_WARPS) {
+        const int j = i - LAG;
+        if (j >= local_rows) break;
+        if (i < local_rows && !exp_row(i)) return;
+        if (j >= 0 && !out_row(j)) return;
     }
-    (void)out_phase(groups - 1);
 }
 
 template <int OUT, int WIDTH>
@@ -451,8 +452,8 @@ int launch_ring(const m3c_softmax_params &p, void *stream)
     }
     cudaError_t code = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
     if (code != cudaSuccess) return static_cast<int>(code);
-    // one CTA per SM; fewer when a CTA would get less than one group
-    uint64_t grid = (p.rows + Geo::G - 1) / Geo::G;
+    // one CTA per SM; fewer when a CTA would get less than a chain's rows
+    uint64_t grid = (p.rows + 31) / 32;
     if (grid > static_cast<uint64_t>(sm_count)) grid = static_cast<uint64_t>(sm_count);
     if (grid == 0) grid = 1;
     kernel<<<static_cast<unsigned>(grid), RING_THREADS, Geo::SMEM, static_cast<cudaStream_t>(stream)>>>(p);

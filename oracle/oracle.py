@@ -60,10 +60,12 @@ _reference = None
 
 
 def build() -> None:
-    """Compile the checkers (the reference library only where its sources
-    exist)."""
+    """Compile the checkers: the restatement always, the reference library
+    when M3_REFERENCE names the reference tree (a library built earlier is
+    kept and used otherwise)."""
     targets = ["oracle"]
-    if os.path.isdir(os.environ.get("M3_REFERENCE", "/root/reference")):
+    reference = os.environ.get("M3_REFERENCE", "")
+    if reference and os.path.isdir(reference):
         targets.append("ref")
     subprocess.run(["make", "-C", HERE, *targets], check=True,
                    stdout=subprocess.DEVNULL)
