@@ -758,17 +758,18 @@ class Env:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(self.local)
         self.device = torch.device("cuda", self.local)
-        self.shard_id = None
 
 
 def make_session(m3, env, g, stream, config):
     """A plain session at N=1; at N>1 this rank's shard of the fixed graph
     (the library partitions it along the configuration's shard axis and
-    all-reduces global reductions over NCCL)."""
+    all-reduces global reductions and data-check verdicts over NCCL, on a
+    communicator of its own: a fresh id per session)."""
     if env.world == 1:
         return m3.Session(g, device=env.local, stream=stream.cuda_stream)
+    ident = shardsmod().shared_shard_id(m3, env.device)
     return m3.Session(g, device=env.local, stream=stream.cuda_stream,
-                      shard=m3.ShardOptions(env.rank, env.world, config.shard_axis, env.shard_id))
+                      shard=m3.ShardOptions(env.rank, env.world, config.shard_axis, ident))
 
 
 def write_inputs(session, env, handles, data):
@@ -1027,8 +1028,6 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=env.device)
     m3 = m3mod()
     m3.load()
-    if env.world > 1:
-        env.shard_id = shardsmod().shared_shard_id(m3, env.device)
     stream = torch.cuda.Stream(env.device)
     torch.cuda.set_stream(stream)
     flush = L2Flush(torch, env.device)

@@ -634,9 +634,12 @@ typedef struct {
                                     the outermost axis that every value
                                     allows and whose extent is at least
                                     `count` */
-    const m3_cuda_shard_id *id;  /* communicator shared by all ranks; NULL:
-                                    no collective (count 1, or a caller that
-                                    combines global reductions itself) */
+    const m3_cuda_shard_id *id;  /* communicator shared by all ranks, used
+                                    when the graph has a global reduction or
+                                    a data check (one id per communicator:
+                                    each such session needs a fresh id);
+                                    NULL: no collective (count 1, or a caller
+                                    that combines global reductions itself) */
     double timeout_seconds;      /* bound on communicator set-up and each
                                     collective enqueue (default 120) */
 } m3_cuda_shard_options;

@@ -6,7 +6,8 @@
  * one stream, one launch per command (no liveness information reaches a
  * backend, so nothing is fused here).  Views may be strided: element-wise
  * operands are addressed through their strides directly; row operators gather
- * a non-contiguous input into a temporary first.  Data-checked operators
+ * a non-contiguous input into the backend's reusable gather buffer first.
+ * Data-checked operators
  * (SOFTMAX/TOP_K NaN, float-to-I32 CAST range) run a scan kernel before the
  * computing kernel; the computing kernel skips its writes when the scan (or
  * any earlier command) failed, so a failing list leaves the failing command's
@@ -28,6 +29,11 @@ typedef struct {
     m3c_status *status;
     m3c_status *status_host;
     m3c_reduce_scratch *reduce;
+    /* dense copies of strided row-operator inputs: one buffer, grown on
+     * demand and reused (commands run in stream order, so each command's
+     * copy is consumed before the next command overwrites it) */
+    void *gather;
+    size_t gather_bytes;
 } cuda_backend;
 
 static const m3c_status clean = {UINT32_MAX, 0U, 0U, UINT32_MAX};
@@ -115,6 +121,7 @@ void m3_cuda_backend_destroy_context(void *context)
     }
     (void)cudaFree(b->status);
     (void)cudaFree(b->reduce);
+    (void)cudaFree(b->gather);
     (void)cudaFreeHost(b->status_host);
     (void)cudaGetLastError();
     free(b);
@@ -355,15 +362,14 @@ static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
     return m3c_launch_ew(&p, b->stream);
 }
 
-/* Row operators need a dense row-major input: gather strided views into a
- * temporary device buffer. */
+/* Row operators need a dense row-major input: gather strided views into the
+ * backend's gather buffer. */
 static int dense_input(cuda_backend *b, const m3_tensor_view *view,
                        uint32_t command,
                        const void **data, void **temporary)
 {
     m3_tensor_view dense;
     size_t stride = m3c_dtype_size(view->metadata.dtype);
-    cudaError_t code;
     int axis;
     int result;
 
@@ -372,10 +378,24 @@ static int dense_input(cuda_backend *b, const m3_tensor_view *view,
         *data = view_base(b, view) + view->byte_offset;
         return 0;
     }
-    code = cudaMallocAsync(temporary, view->metadata.byte_count, b->stream);
-    if (code != cudaSuccess) {
-        return (int)code;
+    if (view->metadata.byte_count > b->gather_bytes) {
+        /* grow: earlier commands of this list may still read the old
+         * buffer, so wait for them before releasing it */
+        cudaError_t code = cudaStreamSynchronize(b->stream);
+
+        if (code == cudaSuccess) {
+            (void)cudaFree(b->gather);
+            b->gather = NULL;
+            b->gather_bytes = 0U;
+            code = cudaMalloc(&b->gather, view->metadata.byte_count);
+        }
+        if (code != cudaSuccess) {
+            b->gather = NULL;
+            return (int)code;
+        }
+        b->gather_bytes = view->metadata.byte_count;
     }
+    *temporary = b->gather;
     dense = *view;
     dense.byte_offset = 0U;
     for (axis = (int)dense.metadata.rank - 1; axis >= 0; --axis) {
@@ -690,11 +710,6 @@ m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
                 result < 0 ? "unsupported view layout"
                            : m3c_cuda_error_string(result));
             break;
-        }
-    }
-    for (i = 0U; i < command_count; ++i) {
-        if (temporaries[i] != NULL) {
-            (void)cudaFreeAsync(temporaries[i], b->stream);
         }
     }
     free(temporaries);

@@ -338,7 +338,10 @@ __device__ __forceinline__ float sin_squared(float t)
 
 // a / b within about one ulp for normal a / b and b: the hardware reciprocal
 // approximation refined by one step of the Markstein correction.  Like
-// exp_moderate, only for results rounded to F16 or BF16 afterwards.
+// exp_moderate, only for results rounded to F16 or BF16 afterwards.  (The
+// unrefined product a * rcp(b), a couple of ulps, was measured: through the
+// gated SiLU's two 16-bit roundings it let a 16-bit result reach 2 ulps from
+// the reference's on the C3 benchmark data.)
 __device__ __forceinline__ float div_approx(float a, float b)
 {
     float y;
@@ -355,10 +358,13 @@ __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const m3c_fastdiv &d)
     return static_cast<uint32_t>(t >> d.shift);
 }
 
-// Status of a session's run: has a command before `bound` failed?
+// Status of a session's run: has a command before `bound` failed, or was
+// the run halted (M3C_RUN_HALTED in runs_started: an earlier run of the
+// same batch failed, so this run must not execute at all)?
 __device__ __forceinline__ bool failed_before(const m3c_status *status, uint32_t bound)
 {
-    return *reinterpret_cast<const volatile uint32_t *>(&status->fail_command) < bound;
+    return *reinterpret_cast<const volatile uint32_t *>(&status->fail_command) < bound ||
+           (*reinterpret_cast<const volatile uint32_t *>(&status->runs_started) & M3C_RUN_HALTED) != 0u;
 }
 
 // Has any command of the run failed?

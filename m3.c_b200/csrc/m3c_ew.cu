@@ -754,6 +754,19 @@ struct Gsilu16 {
         }
     }
 
+    // packed 16-bit product, rounded once
+    __device__ __forceinline__ static uint32_t mul2(uint32_t a, uint32_t b)
+    {
+        if constexpr (DT == M3C_F16) {
+            const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+            return *reinterpret_cast<const uint32_t *>(&r);
+        } else {
+            const __nv_bfloat162 r =
+                __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&a), *reinterpret_cast<const __nv_bfloat162 *>(&b));
+            return *reinterpret_cast<const uint32_t *>(&r);
+        }
+    }
+
     __device__ __forceinline__ static uint32_t narrow2(float lo, float hi)
     {
         if constexpr (DT == M3C_F16) {
@@ -783,14 +796,14 @@ struct Gsilu16 {
         const float largest = fmaxf(fmaxf(fabsf(g[0]), fabsf(g[1])), fmaxf(fabsf(g[2]), fabsf(g[3])));
         if (special == 0u && largest <= 80.0f) {
             // src/m3_op_execute_basic.c:113-117: the activation is stored in
-            // the gate's dtype before the product
+            // the gate's dtype before the product.  The product of two 16-bit
+            // values is exact in F32, so the reference's F32 product rounded
+            // to 16 bits is one packed 16-bit multiply (RN of the exact
+            // product; no NaN or infinity reaches this path)
             float s[VEC];
 #pragma unroll
             for (int j = 0; j < VEC; ++j) s[j] = div_approx(g[j], __fadd_rn(1.0f, exp_moderate(-g[j])));
-            widen2(narrow2(s[0], s[1]), s[0], s[1]);
-            widen2(narrow2(s[2], s[3]), s[2], s[3]);
-            return make_uint2(narrow2(__fmul_rn(s[0], u[0]), __fmul_rn(s[1], u[1])),
-                              narrow2(__fmul_rn(s[2], u[2]), __fmul_rn(s[3], u[3])));
+            return make_uint2(mul2(narrow2(s[0], s[1]), uw.x), mul2(narrow2(s[2], s[3]), uw.y));
         }
         RegisterFile rf;
         rf.w[0][0] = gw.x & 0xffffu;

@@ -237,6 +237,9 @@ m3_graph_value_role m3c_session_role(const m3_session *session,
                                      m3_graph_value_id value);
 size_t m3c_session_value_count(const m3_session *session);
 
+/* Halts the runs after a failed one in a batch (m3c_util.cu). */
+int m3c_launch_run_gate(m3c_status *status, void *stream);
+
 /* Pack / unpack around the per-run all-reduce (m3c_util.cu). */
 int m3c_launch_shard_pack(const m3c_shard_words *words, void *stream);
 int m3c_launch_shard_unpack(const m3c_shard_words *words, void *stream);

@@ -110,10 +110,14 @@ typedef struct {
  * skips its work when a command before its `skip_before` bound has failed
  * (an earlier command of the run), but not for failures of its own
  * commands, so unchecked commands of a fused launch always complete. */
+/* runs_started's top bit: a run of the batch failed and the run gate that
+ * precedes the next run halted everything after it (every launch skips). */
+#define M3C_RUN_HALTED 0x80000000u
+
 typedef struct {
     uint32_t fail_command;  /* UINT32_MAX when clean */
     uint32_t fail_code;
-    uint32_t runs_started;
+    uint32_t runs_started;  /* runs started clean; M3C_RUN_HALTED bit */
     uint32_t detail;        /* categorical: smallest row * 4 + reason that
                                failed (UINT32_MAX when clean) */
 } m3c_status;

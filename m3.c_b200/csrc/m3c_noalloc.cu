@@ -174,8 +174,14 @@ extern "C" m3_status m3_cuda_abs_max_static(int device, void *stream, m3_dtype d
     m3c_status *status = reinterpret_cast<m3c_status *>(words);
     m3c_reduce_scratch *reduce = reinterpret_cast<m3c_reduce_scratch *>(words + kStatusWords * kSlots);
 
-    // status words to "no failure" (all ones), reduction slots to zero
+    // status words to "no failure" (all ones) with no run counted yet (the
+    // run counter word zero: its top bit would halt the kernel), reduction
+    // slots to zero
     code = cudaMemsetAsync(status, 0xff, tensor_count * sizeof(m3c_status), s);
+    if (code == cudaSuccess) {
+        code = cudaMemset2DAsync(&status[0].runs_started, sizeof(m3c_status), 0, sizeof(uint32_t),
+                                 tensor_count, s);
+    }
     if (code == cudaSuccess) {
         code = cudaMemsetAsync(reduce, 0, tensor_count * sizeof(m3c_reduce_scratch), s);
     }

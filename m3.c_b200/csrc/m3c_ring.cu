@@ -11,34 +11,42 @@
 // with independent work.  So the CTA is split by role, and the chain gets a
 // scheduler of its own:
 //
-//   warp 0 (sub-partition 0)  the chain warp.  Its lanes are staggered: the
-//                             CTA's local row i is summed by lane i % 32 over
-//                             chunks i .. i+31 of 32 elements each, so at
-//                             every chunk boundary exactly one lane finishes a
-//                             row (publishes its sum) and starts the next.
-//                             Rows enter and leave the chain one at a time;
-//                             the 16-byte row padding keeps the 8 lanes of
-//                             each quarter-warp load phase on distinct bank
-//                             groups;
-//   warp 4 (sub-partition 0)  the producer: one thread issues a 1-D TMA bulk
+//   warp 0 (sub-partition 0)  the chain warp.  Its first 24 lanes sum 24
+//                             rows at a time, in four groups of 6 lanes that
+//                             start their rows a quarter of a row apart: the
+//                             CTA's local row i is summed by lane i % 24, and
+//                             at the start of every quarter one group
+//                             publishes the sums of the rows it finished and
+//                             takes up the next 6.  A lane's loads run 8
+//                             vectors ahead of its additions; the 16-byte row
+//                             padding puts the lanes of a load phase on
+//                             distinct bank groups.  A row holds its slot
+//                             from its copy until its probabilities are
+//                             written, so the rows in the chain and the
+//                             copies in flight share the ring: 24 rows (of
+//                             16, 20, 24, 28 and 32 measured) balance the
+//                             chain's speed against the depth of the copies;
+//   warp 5 (sub-partition 1)  the producer: one thread issues a 1-D TMA bulk
 //                             copy (cp.async.bulk, global -> shared, mbarrier
 //                             completion, no tensor map, no multicast) per
 //                             row as soon as the row's slot is free;
-//   warps 8, 12               idle (they leave sub-partition 0 to the chain);
-//   the 12 warps of sub-partitions 1-3, the row warps: row warp w owns rows
-//                             i = w (mod 12); for each it computes max /
+//   warps 4, 8, 12            idle (they leave sub-partition 0 to the chain);
+//   the other 11 warps of sub-partitions 1-3, the row warps: row warp w owns
+//                             rows i = w (mod 11); for each it computes max /
 //                             first argmax / NaN in one pass, writes the
 //                             top-1 outputs and the exponentials in place, and
-//                             36 rows later (once the chain is done with that
+//                             33 rows later (once the chain is done with that
 //                             row) the probabilities e / sum with Markstein's
 //                             quotient, streamed to HBM.
 //
 // Row i lives in ring slot i % SLOTS (55 slots of 4 KiB + 16, nearly all of
-// the 227 KiB of shared memory).  Four mbarriers per slot carry the row
-// through its life: full (TMA landed), expd (exponentials ready), summed
-// (the chain is done), empty (written out; the producer may reuse the slot).
-// Every wait is bounded: a wait past its deadline records an internal
-// failure in the status word and the thread leaves its loop.  Each row
+// the 227 KiB of shared memory).  Per slot, two mbarriers carry the row
+// between the producer and the row warps -- full (TMA landed), empty
+// (written out; the producer may reuse the slot) -- and two sequence words
+// (the slot's use count, published after a block fence) between the row
+// warps and the chain: expd (exponentials ready), summed (the chain is
+// done).  Every wait is bounded: a wait past its deadline records an
+// internal failure in the status word and the thread leaves its loop.  Each row
 // depends only on rows with smaller indices, so the waits form no cycle and
 // the bound is never reached by a correct run.
 
@@ -54,8 +62,12 @@ namespace {
 
 constexpr int RING_THREADS = 512;
 constexpr int CHAIN_WARP = 0;
-constexpr int PRODUCER_WARP = 4;
-constexpr int ROW_WARPS = 12;           // the warps of sub-partitions 1-3
+constexpr int PRODUCER_WARP = 5;        // sub-partition 1: none shares the chain's
+constexpr int CHAIN_LANES = 24;         // rows the chain warp sums at once
+constexpr int GROUPS = 4;               // chain lane groups, a quarter row apart
+constexpr int PREFETCH = 8;             // 16-byte loads a chain lane runs ahead
+constexpr int ROW_WARPS = 11;           // the other warps of sub-partitions 1-3
+constexpr uint32_t SLEEP_NS = 2000;     // suspend hint of waits off the chain
 constexpr uint64_t WAIT_NS = 2000000000ull;   // 2 s per wait, then give up
 constexpr uint32_t INTERNAL_CODE = 9u;  // M3_STATUS_INTERNAL
 
@@ -64,15 +76,16 @@ struct RingGeometry {
     static constexpr int BYTES = WIDTH * 4;
     static constexpr int PITCH = BYTES + 16;
     static constexpr int VPL = WIDTH / 128;            // 16-byte vectors per lane
-    static constexpr int CHUNKS = 32;                  // chain chunks per row (one per lane)
-    static constexpr int VPC = WIDTH / 128;            // 16-byte vectors per chunk
+    // a chain lane's row in GROUPS periods of PV 16-byte vectors each
+    static constexpr int PV = WIDTH / 4 / GROUPS;
+    static_assert(PV % PREFETCH == 0, "whole prefetch windows per period");
     static constexpr int SLOTS = WIDTH == 1024 ? 55 : 96;
-    static constexpr int LAG = 36;                     // exp(i) ... out(i - LAG)
-    // per slot: full, expd, summed, empty barriers; sum, reciprocal; flags,
-    // issued
+    static constexpr int LAG = 33;                     // exp(i) ... out(i - LAG)
+    // per slot: full, empty barriers; the published sum; the exponentials'
+    // sequence word; flags, issued
     static constexpr int ROWS_BYTES = SLOTS * PITCH;
-    static constexpr int SMEM = ROWS_BYTES + SLOTS * (4 * 8 + 4 + 4 + 1 + 1);
-    static_assert(LAG % 12 == 0 && LAG >= 32, "a row warp's out lag: its own rows, after the chain");
+    static constexpr int SMEM = ROWS_BYTES + SLOTS * (2 * 8 + 8 + 4 + 1 + 1);
+    static_assert(LAG % 11 == 0 && LAG > CHAIN_LANES, "a row warp's out lag: its own rows, after the chain");
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p)
@@ -107,19 +120,76 @@ __device__ __forceinline__ uint64_t now_ns()
     return t;
 }
 
-// Wait for the phase of `parity` to complete; false after WAIT_NS.
+// Wait for the phase of `parity` to complete; false after WAIT_NS.  SLEEPY
+// waits ask the hardware to suspend the warp until the phase completes (a
+// suspend-time hint), so a waiting warp takes no issue slots from its
+// sub-partition; the chain warp's own waits poll.
+template <bool SLEEPY>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
 {
     const uint32_t addr = smem_addr(bar);
     uint64_t deadline = 0;
     for (uint32_t spin = 0;; ++spin) {
         uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
+        if (SLEEPY) {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done)
+                : "r"(addr), "r"(parity), "r"(SLEEP_NS)
+                : "memory");
+        } else {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done)
+                : "r"(addr), "r"(parity)
+                : "memory");
+        }
         if (done) return true;
+        if ((spin & 255u) == 0u) {
+            const uint64_t t = now_ns();
+            if (deadline == 0) {
+                deadline = t + WAIT_NS;
+            } else if (t > deadline) {
+                return false;
+            }
+        }
+    }
+}
+
+// Poll a shared-memory word with acquire loads until it equals `want`
+// (false after WAIT_NS): what its writer stored before its release fence is
+// then visible.
+__device__ __forceinline__ bool poll_acquire(volatile int *word, int want)
+{
+    const uint32_t addr = smem_addr(const_cast<int *>(word));
+    uint64_t deadline = 0;
+    for (uint32_t spin = 0;; ++spin) {
+        int seen;
+        asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(seen) : "r"(addr) : "memory");
+        if (seen == want) return true;
+        if ((spin & 255u) == 0u) {
+            const uint64_t t = now_ns();
+            if (deadline == 0) {
+                deadline = t + WAIT_NS;
+            } else if (t > deadline) {
+                return false;
+            }
+        }
+    }
+}
+
+// Poll a published (use, value) word until its use is `want`.
+__device__ __forceinline__ bool poll_sum(volatile unsigned long long *word, unsigned want,
+                                         unsigned long long *value)
+{
+    uint64_t deadline = 0;
+    for (uint32_t spin = 0;; ++spin) {
+        const unsigned long long seen = *word;
+        if (static_cast<unsigned>(seen) == want) {
+            *value = seen;
+            return true;
+        }
+        __nanosleep(32);
         if ((spin & 255u) == 0u) {
             const uint64_t t = now_ns();
             if (deadline == 0) {
@@ -167,18 +237,20 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     constexpr int SLOTS = Geo::SLOTS;
     constexpr int PITCH = Geo::PITCH;
     constexpr int VPL = Geo::VPL;
-    constexpr int CHUNKS = Geo::CHUNKS;
-    constexpr int VPC = Geo::VPC;
+    constexpr int PV = Geo::PV;
     constexpr int LAG = Geo::LAG;
     extern __shared__ __align__(16) unsigned char smem[];
     unsigned char *rows_area = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Geo::ROWS_BYTES);
-    uint64_t *expd = full + SLOTS;
-    uint64_t *summed = expd + SLOTS;
-    uint64_t *empty = summed + SLOTS;
-    float *slot_sum = reinterpret_cast<float *>(empty + SLOTS);
-    float *slot_rcp = slot_sum + SLOTS;
-    unsigned char *slot_flags = reinterpret_cast<unsigned char *>(slot_rcp + SLOTS);
+    uint64_t *empty = full + SLOTS;
+    // the uses of a slot whose exponentials / sum are ready (plain words:
+    // the chain warp polls and publishes one row every 32 steps, too often
+    // for mbarrier round trips)
+    // (use, sum bits): one 64-bit store publishes a row's sum with its use
+    // count, so the reader needs no fence for the sum itself
+    volatile unsigned long long *summed = reinterpret_cast<volatile unsigned long long *>(empty + SLOTS);
+    volatile int *expd_seq = reinterpret_cast<volatile int *>(summed + SLOTS);
+    unsigned char *slot_flags = reinterpret_cast<unsigned char *>(const_cast<int *>(expd_seq + SLOTS));
     unsigned char *slot_issued = slot_flags + SLOTS;
     __shared__ int skip;
 
@@ -201,9 +273,9 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         }
         for (int s = 0; s < SLOTS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&expd[s], 32);
-            mbar_init(&summed[s], 1);
             mbar_init(&empty[s], 32);
+            expd_seq[s] = 0;
+            summed[s] = 0ull;
             slot_issued[s] = 0;
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -220,7 +292,7 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         for (int i = 0; i < local_rows; ++i) {
             const int s = i % SLOTS;
             const int use = i / SLOTS;
-            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+            if (use > 0 && !mbar_wait<false>(&empty[s], (use - 1) & 1)) {
                 timed_out(p.status, first_command);
                 ok = false;
                 break;
@@ -233,74 +305,86 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         if (!ok) {
             // let every copy this thread issued land before the CTA ends
             for (int s = 0; s < SLOTS; ++s) {
-                if (slot_issued[s] & 1u) (void)mbar_wait(&full[s], (slot_issued[s] >> 1) & 1u);
+                if (slot_issued[s] & 1u) (void)mbar_wait<false>(&full[s], (slot_issued[s] >> 1) & 1u);
             }
         }
         return;
     }
 
     if (warp == CHAIN_WARP) {
-        // lane l sums rows l, l + 32, ...; row i over chunks i .. i + 31, a
-        // 32nd of the row each
+        // Lane l < CHAIN_LANES sums rows l, l + CHAIN_LANES, ...  Its group
+        // g = l / (CHAIN_LANES / GROUPS) starts its n-th row in period
+        // n * GROUPS + g and spends GROUPS periods on it, so at the start of
+        // every period one group publishes the rows it finished and takes
+        // up the next ones: rows enter and leave the chain a few at a time.
+        constexpr int PER_GROUP = CHAIN_LANES / GROUPS;
         const bool summing = p.probs != nullptr || p.row_sums != nullptr;
+        const int group = lane < CHAIN_LANES ? lane / PER_GROUP : GROUPS;
         float sum = 0.0f;
         int cur = -1;        // the row this lane sums, -1: none
         int slot = 0;
-        bool failed = false;
-        for (int k = 0; k < local_rows + CHUNKS && !failed; ++k) {
-            if (lane == (k % 32)) {
+        int part = 0;        // the period of the row this lane is in
+        const int per_lane = (local_rows + CHAIN_LANES - 1) / CHAIN_LANES;
+        const int periods = (per_lane + 1) * GROUPS;
+        for (int q = 0; q < periods; ++q) {
+            bool failed = false;
+            if (group < GROUPS && q >= group && (q - group) % GROUPS == 0) {
                 if (cur >= 0) {
-                    // the row is complete: publish its sum
-                    if (p.probs != nullptr) {
-                        slot_sum[slot] = sum;
-                        slot_rcp[slot] = __frcp_rn(sum);
-                    } else if (p.row_sums != nullptr) {
+                    // the row is complete: publish its sum (ROW_SUM alone:
+                    // straight to its output)
+                    if (p.row_sums != nullptr && p.probs == nullptr) {
                         p.row_sums[row_begin + cur] = sum;
                     }
-                    mbar_arrive(&summed[slot]);
+                    summed[slot] = (static_cast<unsigned long long>(__float_as_uint(sum)) << 32) |
+                                   static_cast<unsigned>(cur / SLOTS + 1);
                 }
-                cur = k < local_rows ? k : -1;
+                const int next = (q - group) / GROUPS * CHAIN_LANES + lane;
+                cur = next < local_rows ? next : -1;
                 sum = 0.0f;
+                part = 0;
                 if (cur >= 0) {
                     slot = cur % SLOTS;
-                    if (!mbar_wait(&expd[slot], (cur / SLOTS) & 1)) {
-                        timed_out(p.status, first_command);
-                        failed = true;
-                    }
+                    failed = !poll_acquire(&expd_seq[slot], cur / SLOTS + 1);
                 }
             }
-            failed = __any_sync(0xffffffffu, failed);
+            if (__any_sync(0xffffffffu, failed)) {
+                if (failed) timed_out(p.status, first_command);
+                break;
+            }
             if (cur >= 0 && summing) {
-                // the reference's left-to-right F32 sum, 32 elements of the
-                // row (of e, or of x for ROW_SUM without SOFTMAX)
-                const float4 *v4 =
-                    reinterpret_cast<const float4 *>(rows_area + slot * PITCH) + (k - cur) * VPC;
-                float4 a[VPC];
+                // the reference's left-to-right F32 sum over a quarter of
+                // the row (of e, or of x for ROW_SUM without SOFTMAX); the
+                // loads run PREFETCH vectors ahead of the additions
+                const float4 *v4 = reinterpret_cast<const float4 *>(rows_area + slot * PITCH) + part * PV;
+                float4 a[PREFETCH];
 #pragma unroll
-                for (int j = 0; j < VPC; ++j) a[j] = v4[j];
+                for (int j = 0; j < PREFETCH; ++j) a[j] = v4[j];
 #pragma unroll
-                for (int j = 0; j < VPC; ++j) {
-                    sum = __fadd_rn(sum, a[j].x);
-                    sum = __fadd_rn(sum, a[j].y);
-                    sum = __fadd_rn(sum, a[j].z);
-                    sum = __fadd_rn(sum, a[j].w);
+                for (int j = 0; j < PV; ++j) {
+                    const float4 v = a[j % PREFETCH];
+                    if (j + PREFETCH < PV) a[j % PREFETCH] = v4[j + PREFETCH];
+                    sum = __fadd_rn(sum, v.x);
+                    sum = __fadd_rn(sum, v.y);
+                    sum = __fadd_rn(sum, v.z);
+                    sum = __fadd_rn(sum, v.w);
                 }
+                ++part;
             }
         }
         return;
     }
     if ((warp & 3) == 0) {
-        return;  // warps 8 and 12: sub-partition 0 belongs to the chain
+        return;  // warps 4, 8 and 12: sub-partition 0 belongs to the chain
     }
 
-    // row warps: index 0..11 over sub-partitions 1-3
-    const int rw = warp - 1 - warp / 4;
+    // row warps: index 0..10 over sub-partitions 1-3 (warp 5 is the producer)
+    const int rw = warp - 1 - warp / 4 - (warp > PRODUCER_WARP ? 1 : 0);
     const uint64_t out_pitch = static_cast<uint64_t>(WIDTH) * (OUT == M3C_F32 ? 4u : 2u);
 
     // max / first argmax / NaN, top-1, exponentials in place
     auto exp_row = [&](int i) -> bool {
         const int s = i % SLOTS;
-        if (!mbar_wait(&full[s], (i / SLOTS) & 1)) {
+        if (!mbar_wait<false>(&full[s], (i / SLOTS) & 1)) {
             timed_out(p.status, first_command);
             return false;
         }
@@ -378,22 +462,28 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
             }
             if (lane == 0) slot_flags[s] = static_cast<unsigned char>(flags);
         }
-        mbar_arrive(&expd[s]);
+        __syncwarp();
+        if (lane == 0) {
+            asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(const_cast<int *>(&expd_seq[s]))),
+                         "r"(i / SLOTS + 1)
+                         : "memory");
+        }
         return true;
     };
 
     // probabilities e / sum once the chain is done with the row; frees the slot
     auto out_row = [&](int j) -> bool {
         const int s = j % SLOTS;
-        if (!mbar_wait(&summed[s], (j / SLOTS) & 1)) {
+        unsigned long long published = 0ull;
+        if (!poll_sum(&summed[s], j / SLOTS + 1, &published)) {
             timed_out(p.status, first_command);
             return false;
         }
         if (p.probs != nullptr) {
             const float4 *e4 = reinterpret_cast<const float4 *>(rows_area + s * PITCH);
             const int flags = slot_flags[s];
-            const float sum = slot_sum[s];
-            const float y = slot_rcp[s];
+            const float sum = __uint_as_float(static_cast<uint32_t>(published >> 32));
+            const float y = __frcp_rn(sum);
             unsigned char *orow = static_cast<unsigned char *>(p.probs) +
                                   (row_begin + static_cast<uint64_t>(j)) * out_pitch;
 #pragma unroll
@@ -453,7 +543,7 @@ int launch_ring(const m3c_softmax_params &p, void *stream)
     cudaError_t code = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
     if (code != cudaSuccess) return static_cast<int>(code);
     // one CTA per SM; fewer when a CTA would get less than a chain's rows
-    uint64_t grid = (p.rows + 31) / 32;
+    uint64_t grid = (p.rows + CHAIN_LANES - 1) / CHAIN_LANES;
     if (grid > static_cast<uint64_t>(sm_count)) grid = static_cast<uint64_t>(sm_count);
     if (grid == 0) grid = 1;
     kernel<<<static_cast<unsigned>(grid), RING_THREADS, Geo::SMEM, static_cast<cudaStream_t>(stream)>>>(p);

@@ -35,6 +35,10 @@ typedef struct {
     size_t slot_b;
 } session_event;
 
+/* Launches of one run that may execute at the same time: up to
+ * 1 + M3C_SIDE_STREAMS per wave. */
+#define M3C_SIDE_STREAMS 3
+
 /* A captured sequence of `runs` runs with slots swap_a/swap_b exchanged
  * between consecutive runs (SIZE_MAX: none), valid for the buffer assignment
  * it was captured from (kernel parameters hold buffer addresses). */
@@ -104,6 +108,13 @@ struct m3_session {
     host_pipe pipe;
     /* this rank's share of a sharded session (NULL: not sharded) */
     m3c_shard *shard;
+    /* concurrent launches: wave_join[i] is true when launch i runs beside
+     * the launches before it in its wave (independent slots, no data check
+     * before it in the run); side streams and fork/join events */
+    bool *wave_join;
+    cudaStream_t side[M3C_SIDE_STREAMS];
+    cudaEvent_t fork_event;
+    cudaEvent_t join_event[M3C_SIDE_STREAMS];
 };
 
 static const m3c_status clean_status = {UINT32_MAX, 0U, 0U, UINT32_MAX};
@@ -236,6 +247,19 @@ void m3_session_free(m3_session *session)
     if (session->status_host != NULL) {
         (void)cudaFreeHost(session->status_host);
     }
+    for (int k = 0; k < M3C_SIDE_STREAMS; ++k) {
+        if (session->side[k] != NULL) {
+            (void)cudaStreamSynchronize(session->side[k]);
+            (void)cudaStreamDestroy(session->side[k]);
+        }
+        if (session->join_event[k] != NULL) {
+            (void)cudaEventDestroy(session->join_event[k]);
+        }
+    }
+    if (session->fork_event != NULL) {
+        (void)cudaEventDestroy(session->fork_event);
+    }
+    free(session->wave_join);
     if (session->own_stream && session->stream != NULL) {
         (void)cudaStreamDestroy(session->stream);
     }
@@ -321,6 +345,112 @@ static void build_templates(m3_session *s)
             (void)m3c_ew_choose(&probe, &s->ew_choices[i]);
         }
     }
+}
+
+/* Slots a launch reads or writes (both buffers of a slot count as one). */
+static size_t launch_slots(const m3c_plan *plan, const m3c_launch *l,
+                           size_t *slots, size_t capacity)
+{
+    m3c_ref refs[M3C_EW_MAX_OPERANDS + M3C_EW_MAX_OUTPUTS + 12];
+    size_t n = 0U;
+    size_t count = 0U;
+    size_t i;
+    int k;
+
+    if (l->kind == M3C_LAUNCH_EW) {
+        for (k = 0; k < l->n_operands; ++k) refs[n++] = l->operands[k].ref;
+        for (k = 0; k < l->n_outputs; ++k) refs[n++] = l->outputs[k];
+        if (l->has_absmax) refs[n++] = l->absmax_out;
+    } else {
+        refs[n++] = l->row_in;
+        refs[n++] = l->row_in_b;
+        refs[n++] = l->row_sum_out;
+        refs[n++] = l->row_out;
+        refs[n++] = l->row_out2;
+        refs[n++] = l->row_out3;
+        refs[n++] = l->row_out4;
+        refs[n++] = l->norm_scale;
+        refs[n++] = l->norm_bias;
+    }
+    for (i = 0U; i < n && count < capacity; ++i) {
+        if (refs[i].value != UINT32_MAX) {
+            slots[count++] = plan->value_slot[refs[i].value];
+        }
+    }
+    return count;
+}
+
+/* Waves of launches that may run at the same time: only in a plan without
+ * data checks (no launch can fail, so no later launch must wait for an
+ * earlier one's verdict), a launch joins the wave before it when it shares
+ * no slot with any launch of that wave. */
+static m3_status plan_waves(m3_session *s, m3_error *error)
+{
+    size_t n = s->plan.launch_count;
+    size_t wave_start = 0U;
+    size_t i;
+    size_t widest = 0U;
+    enum { CAP = 32 };
+
+    if (n < 2U || s->plan.flip_count != 0U) {
+        return M3_STATUS_OK;
+    }
+    s->wave_join = calloc(n, sizeof(bool));
+    if (s->wave_join == NULL) {
+        return m3c_error_set(error, M3_STATUS_OUT_OF_MEMORY,
+                             "cannot allocate the launch waves");
+    }
+    for (i = 1U; i < n; ++i) {
+        size_t mine[CAP];
+        size_t mine_count = launch_slots(&s->plan, &s->plan.launches[i], mine, CAP);
+        bool independent = i - wave_start <= M3C_SIDE_STREAMS;
+        size_t j;
+
+        for (j = wave_start; j < i && independent; ++j) {
+            size_t theirs[CAP];
+            size_t theirs_count = launch_slots(&s->plan, &s->plan.launches[j], theirs, CAP);
+            size_t a;
+            size_t b;
+
+            for (a = 0U; a < mine_count && independent; ++a) {
+                for (b = 0U; b < theirs_count; ++b) {
+                    if (mine[a] == theirs[b]) {
+                        independent = false;
+                        break;
+                    }
+                }
+            }
+        }
+        if (independent) {
+            s->wave_join[i] = true;
+            if (i - wave_start > widest) {
+                widest = i - wave_start;
+            }
+        } else {
+            wave_start = i;
+        }
+    }
+    if (widest == 0U) {
+        free(s->wave_join);
+        s->wave_join = NULL;
+        return M3_STATUS_OK;
+    }
+    {
+        cudaError_t code = cudaEventCreateWithFlags(&s->fork_event,
+                                                    cudaEventDisableTiming);
+
+        for (i = 0U; code == cudaSuccess && i < widest; ++i) {
+            code = cudaStreamCreateWithFlags(&s->side[i], cudaStreamNonBlocking);
+            if (code == cudaSuccess) {
+                code = cudaEventCreateWithFlags(&s->join_event[i],
+                                                cudaEventDisableTiming);
+            }
+        }
+        if (code != cudaSuccess) {
+            return cuda_failure(error, code, "cannot create side streams");
+        }
+    }
+    return M3_STATUS_OK;
 }
 
 m3_status m3_cuda_session_create(m3_session **session_output,
@@ -491,6 +621,11 @@ m3_status m3_cuda_session_create(m3_session **session_output,
         return cuda_failure(error, code, "cannot initialise session memory");
     }
     build_templates(s);
+    status = plan_waves(s, error);
+    if (status != M3_STATUS_OK) {
+        m3_session_free(s);
+        return status;
+    }
     memcpy(s->sync_buffer[0], s->buffer[0], count * sizeof(unsigned char *));
     memcpy(s->sync_buffer[1], s->buffer[1], count * sizeof(unsigned char *));
     s->sticky_status = M3_STATUS_OK;
@@ -529,7 +664,7 @@ static m3_status push_event(m3_session *s, event_kind kind, size_t a,
     return M3_STATUS_OK;
 }
 
-static int launch_one(m3_session *s, size_t index, bool first)
+static int launch_one(m3_session *s, size_t index, bool first, cudaStream_t stream)
 {
     const m3c_launch *l = &s->plan.launches[index];
 
@@ -553,7 +688,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
             p.absmax_out = ref_pointer(s, l->absmax_out);
             p.absmax_publish_always = m3c_shard_collective(s->shard) ? 1 : 0;
         }
-        return m3c_launch_ew_chosen(&s->ew_choices[index], &p, s->stream);
+        return m3c_launch_ew_chosen(&s->ew_choices[index], &p, stream);
     }
     if (l->kind == M3C_LAUNCH_CATEGORICAL) {
         const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
@@ -571,7 +706,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         p.command = l->command_a;
         p.skip_before = (uint32_t)l->first_node;
         p.first_of_run = first ? 1 : 0;
-        return m3c_launch_categorical(&p, s->stream);
+        return m3c_launch_categorical(&p, stream);
     }
     if (l->kind == M3C_LAUNCH_SOFTMAX) {
         const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
@@ -603,14 +738,14 @@ static int launch_one(m3_session *s, size_t index, bool first)
                 /* rows of no element sum to +0 */
                 cudaError_t code = cudaMemsetAsync(
                     p.row_sums, 0, s->metadata[l->row_out4.value].byte_count,
-                    s->stream);
+                    stream);
 
                 if (code != cudaSuccess) {
                     return (int)code;
                 }
             }
         }
-        return m3c_launch_softmax(&p, s->stream);
+        return m3c_launch_softmax(&p, stream);
     }
     {
         const m3_tensor_metadata *in = &s->metadata[l->row_in.value];
@@ -636,7 +771,7 @@ static int launch_one(m3_session *s, size_t index, bool first)
         p.epsilon = l->epsilon;
         p.status = s->status_device;
         p.skip_before = (uint32_t)l->first_node;
-        return m3c_launch_norm(&p, s->stream);
+        return m3c_launch_norm(&p, stream);
     }
 }
 
@@ -676,17 +811,56 @@ static m3_status account_swap(m3_session *s, size_t a, size_t b,
     return status;
 }
 
-/* The launches of one run with the buffer assignment as it stands. */
+/* The launches of one run with the buffer assignment as it stands.  A wave
+ * of independent launches forks onto the side streams and joins back (under
+ * stream capture this records parallel branches of the run's graph). */
 static int launch_run(m3_session *s)
 {
-    size_t i;
+    size_t i = 0U;
 
-    for (i = 0U; i < s->plan.launch_count; ++i) {
-        int code = launch_one(s, i, i == 0U);
+    while (i < s->plan.launch_count) {
+        size_t end = i + 1U;
+        size_t k;
+        cudaError_t code;
 
-        if (code != 0) {
-            return code;
+        while (s->wave_join != NULL && end < s->plan.launch_count &&
+               s->wave_join[end]) {
+            ++end;
         }
+        if (end == i + 1U) {
+            int result = launch_one(s, i, i == 0U, s->stream);
+
+            if (result != 0) {
+                return result;
+            }
+            i = end;
+            continue;
+        }
+        code = cudaEventRecord(s->fork_event, s->stream);
+        for (k = i + 1U; code == cudaSuccess && k < end; ++k) {
+            code = cudaStreamWaitEvent(s->side[k - i - 1U], s->fork_event, 0);
+        }
+        if (code != cudaSuccess) {
+            return (int)code;
+        }
+        for (k = i; k < end; ++k) {
+            int result = launch_one(s, k, k == 0U,
+                                    k == i ? s->stream : s->side[k - i - 1U]);
+
+            if (result != 0) {
+                return result;
+            }
+        }
+        for (k = i + 1U; code == cudaSuccess && k < end; ++k) {
+            code = cudaEventRecord(s->join_event[k - i - 1U], s->side[k - i - 1U]);
+            if (code == cudaSuccess) {
+                code = cudaStreamWaitEvent(s->stream, s->join_event[k - i - 1U], 0);
+            }
+        }
+        if (code != cudaSuccess) {
+            return (int)code;
+        }
+        i = end;
     }
     return 0;
 }
@@ -740,7 +914,12 @@ static cudaGraphExec_t capture_runs(m3_session *s, size_t runs, size_t a,
         return NULL;
     }
     for (r = 0U; r < runs && launched == 0; ++r) {
-        launched = launch_run(s);
+        if (r > 0U && s->plan.flip_count != 0U) {
+            launched = m3c_launch_run_gate(s->status_device, s->stream);
+        }
+        if (launched == 0) {
+            launched = launch_run(s);
+        }
         for (i = 0U; i < s->plan.flip_count; ++i) {
             s->current[s->plan.flip_slot[i]] ^= 1U;
         }
@@ -849,6 +1028,16 @@ static m3_status enqueue_runs(m3_session *s, size_t runs, size_t a, size_t b,
     if (status != M3_STATUS_OK) {
         return status;
     }
+    if (s->plan.flip_count != 0U && s->pending_runs != 0U) {
+        /* an earlier run of this batch may have failed: halt this one then */
+        int code = m3c_launch_run_gate(s->status_device, s->stream);
+
+        if (code != 0) {
+            return m3c_error_set(error, M3_STATUS_INTERNAL,
+                                 "kernel launch failed: %s",
+                                 m3c_cuda_error_string(code));
+        }
+    }
     if (s->cuda.cuda_graphs && !m3c_shard_collective(s->shard)) {
         enum cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
 
@@ -878,7 +1067,13 @@ static m3_status enqueue_runs(m3_session *s, size_t runs, size_t a, size_t b,
     }
     for (r = 0U; r < runs; ++r) {
         if (!graphed) {
-            int code = launch_run(s);
+            int code = r > 0U && s->plan.flip_count != 0U
+                           ? m3c_launch_run_gate(s->status_device, s->stream)
+                           : 0;
+
+            if (code == 0) {
+                code = launch_run(s);
+            }
 
             if (code != 0) {
                 return m3c_error_set(error, M3_STATUS_INTERNAL,
@@ -961,7 +1156,8 @@ static m3_status settle(m3_session *s, m3_error *error)
     }
     seen = *s->status_host;
     if (seen.fail_command != UINT32_MAX) {
-        size_t failing_run = seen.runs_started ? seen.runs_started - 1U : 0U;
+        size_t started = seen.runs_started & ~(uint32_t)M3C_RUN_HALTED;
+        size_t failing_run = started ? started - 1U : 0U;
         size_t run = 0U;
         size_t e;
         size_t f;

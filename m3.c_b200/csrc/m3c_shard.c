@@ -445,7 +445,8 @@ m3_status m3_cuda_shard_session_create(m3_session **session,
         m3c_shard_free(sh);
         return status;
     }
-    if (shard->id != NULL && shard->count > 1) {
+    if (shard->id != NULL && shard->count > 1 &&
+        (sh->reduction_count > 0 || sh->checks)) {
         cudaError_t code = cudaSetDevice(m3_cuda_session_device(*session));
 
         if (code == cudaSuccess) {

@@ -464,6 +464,28 @@ __global__ void shard_unpack_kernel(m3c_shard_words w)
 }  // namespace
 }  // namespace m3c
 
+namespace m3c {
+namespace {
+
+// Between two runs of one batch (no synchronise between them): once a run
+// has failed, every later run is halted, as the reference stops at the
+// failing m3_session_run.
+__global__ void run_gate_kernel(m3c_status *status)
+{
+    if (*reinterpret_cast<volatile uint32_t *>(&status->fail_command) != 0xffffffffu) {
+        atomicOr(&status->runs_started, M3C_RUN_HALTED);
+    }
+}
+
+}  // namespace
+}  // namespace m3c
+
+extern "C" int m3c_launch_run_gate(m3c_status *status, void *stream)
+{
+    m3c::run_gate_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(status);
+    return static_cast<int>(cudaGetLastError());
+}
+
 extern "C" int m3c_launch_shard_pack(const m3c_shard_words *words, void *stream)
 {
     m3c::shard_pack_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*words);

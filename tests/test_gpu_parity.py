@@ -412,6 +412,33 @@ def test_abs_max_nan_and_empty(m3, gpu):
     assert s.read(m)[0] == 0.0
 
 
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+@pytest.mark.parametrize("count", [1, 7, 4099, 1 << 20])
+def test_abs_max_16_bit_against_oracle(m3, oracle, gpu, dtype, count):
+    """ABS_MAX of F16/BF16 tensors through a session
+    against the oracle's abs-max over the same bits: signed zeros,
+    subnormals, infinities and the largest finite values included."""
+    dt = getattr(m3, dtype)
+    enc = oracle.to_f16 if dtype == "F16" else oracle.to_bf16
+    x = enc(m3.fill_normal(9, count % 13, 0.0, 2.0, count))
+    specials = np.array([0x8000, 0x0001, 0x8003, 0x7BFF if dtype == "F16" else 0x7F7F],
+                        np.uint16)
+    x[: min(count, len(specials))] = specials[: min(count, len(specials))]
+    if count > 4:
+        x[count // 2] = 0xFC00 if dtype == "F16" else 0xFF80      # -inf
+    g = m3.Graph()
+    v = g.value(m3.INPUT, dt, (count,))
+    m = g.inferred("ABS_MAX", [v], m3.OUTPUT, m3.F32)
+    g.node("ABS_MAX", [v], [m])
+    s = m3.Session(g)
+    s.write(v, x)
+    s.run()
+    want = np.zeros(1, np.float32)
+    assert oracle.run("abs_max", (x, dt), want) == 0
+    assert bits(s.read(m))[0] == bits(want)[0]
+    s.close()
+
+
 def test_async_device_read_follows_pending_runs(m3, gpu):
     """read_device_async copies the output of the runs enqueued before it
     (ABS_MAX writes a shadow buffer that only becomes current when its run
