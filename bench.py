@@ -832,8 +832,14 @@ def measure_cuda(m3, torch, dist, env, config, args, stream, flush, with_baselin
     torch.cuda.synchronize(env.device)
     sampler.start()
     time.sleep(0.3)
+    align = torch.zeros(1, device=env.device) if env.world > 1 else None
     for k in range(args.steps):
         flush()
+        if align is not None:
+            # the flush takes a different time on each GPU: the ranks start
+            # each step together, so a rank's time holds no wait for another
+            # rank's flush inside the run's collective
+            dist.all_reduce(align)
         starts[k].record(stream)
         one_step()
         ends[k].record(stream)

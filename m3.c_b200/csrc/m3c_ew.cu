@@ -35,10 +35,12 @@
 
 #include <cstdint>
 #include <initializer_list>
+#include <type_traits>
 #include <utility>
 
 #include "m3c_device.cuh"
 #include "m3c_kernels.h"
+#include "m3c_bulk.cuh"
 
 namespace m3c {
 namespace {
@@ -862,10 +864,138 @@ struct Gsilu16 {
     }
 };
 
+// The same gated SiLU fed by 1-D TMA, for contiguous 16-byte-aligned
+// operands: one CTA per SM; warp 0's first lane copies tiles of gate and up
+// (TILE elements each, cp.async.bulk with mbarrier completion, no tensor
+// map, no multicast) into a ring of STAGES shared-memory stages; warps 1-15
+// take 16 bytes of both per tile (8 elements each), compute them with
+// Gsilu16's block, and stream the results to HBM.  STAGES tiles (210 KB) are
+// in flight per SM without holding registers, where the register-fed loop
+// keeps about 64 KB in flight at its two CTAs per SM.
+template <int DT, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
+struct Gsilu16Bulk {
+    using Base = Gsilu16<DT, OPSIG, OUTSIG, OPS...>;
+    using Generic = typename Base::Generic;
+    static constexpr bool custom_loop = true;
+    static constexpr bool cta_pipeline = true;  // the CTA's threads wait on one another
+    static constexpr int operands = Base::operands;
+    static constexpr int CONSUMERS = THREADS - 32;
+    static constexpr int TILE = CONSUMERS * 8;       // elements per tile
+    static constexpr int TILE_BYTES = TILE * 2;      // per operand
+    static constexpr int STAGES = 14;
+    static constexpr int SMEM = STAGES * 2 * TILE_BYTES + STAGES * 16;
+
+    __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid, Flags &flags)
+    {
+        Generic::run(p, rf, valid, flags);
+    }
+
+    __device__ static void loop(const m3c_ew_params &p, Flags &flags)
+    {
+        extern __shared__ __align__(16) unsigned char bulk_smem[];
+        uint64_t *full = reinterpret_cast<uint64_t *>(bulk_smem + STAGES * 2 * TILE_BYTES);
+        uint64_t *empty = full + STAGES;
+        const uint16_t *gate = static_cast<const uint16_t *>(p.operands[0].base);
+        const uint16_t *up = static_cast<const uint16_t *>(p.operands[1].base);
+        uint16_t *out = static_cast<uint16_t *>(p.outputs[0].base);
+        const uint32_t command = p.ops[0].command;
+        const uint64_t tiles = p.count / TILE;
+        const uint64_t first = tiles * blockIdx.x / gridDim.x;
+        const int n = static_cast<int>(tiles * (blockIdx.x + 1) / gridDim.x - first);
+        const int warp = static_cast<int>(threadIdx.x) / 32;
+        const int lane = static_cast<int>(threadIdx.x) % 32;
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < STAGES; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], CONSUMERS / 32);
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        if (warp == 0) {
+            if (lane == 0) {
+                int i = 0;
+                for (; i < n; ++i) {
+                    const int s = i % STAGES;
+                    const int use = i / STAGES;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                        bulk_timed_out(p.status, command);
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], 2 * TILE_BYTES);
+                    const uint64_t e = (first + static_cast<uint64_t>(i)) * TILE;
+                    bulk_load(bulk_smem + s * 2 * TILE_BYTES, gate + e, TILE_BYTES, &full[s]);
+                    bulk_load(bulk_smem + s * 2 * TILE_BYTES + TILE_BYTES, up + e, TILE_BYTES, &full[s]);
+                }
+                // every copy issued has landed before the CTA ends
+                for (int r = i - STAGES < 0 ? 0 : i - STAGES; r < i; ++r) {
+                    (void)mbar_wait(&full[r % STAGES], (r / STAGES) & 1);
+                }
+            }
+        } else {
+            // one consumer group takes every tile in order, so a consumer is
+            // never a phase ahead of the producer's copies
+            const int c = static_cast<int>(threadIdx.x) - 32;
+            for (int i = 0; i < n; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+                    bulk_timed_out(p.status, command);
+                    break;
+                }
+                const unsigned char *stage = bulk_smem + s * 2 * TILE_BYTES;
+                const uint4 g = reinterpret_cast<const uint4 *>(stage)[c];
+                const uint4 u = reinterpret_cast<const uint4 *>(stage + TILE_BYTES)[c];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                const uint2 lo = Base::block(p, make_uint2(g.x, g.y), make_uint2(u.x, u.y), flags);
+                const uint2 hi = Base::block(p, make_uint2(g.z, g.w), make_uint2(u.z, u.w), flags);
+                __stcs(reinterpret_cast<uint4 *>(out + (first + static_cast<uint64_t>(i)) * TILE) + c,
+                       make_uint4(lo.x, lo.y, hi.x, hi.y));
+            }
+        }
+        if (blockIdx.x != gridDim.x - 1) return;
+        // the elements after the last whole tile: the last CTA, from HBM
+        const uint2 *g2 = reinterpret_cast<const uint2 *>(gate);
+        const uint2 *u2 = reinterpret_cast<const uint2 *>(up);
+        uint2 *o2 = reinterpret_cast<uint2 *>(out);
+        const uint64_t blocks = p.count / VEC;
+        for (uint64_t b = tiles * (TILE / VEC) + threadIdx.x; b < blocks; b += THREADS) {
+            __stcs(o2 + b, Base::block(p, __ldcs(g2 + b), __ldcs(u2 + b), flags));
+        }
+        const int tail = static_cast<int>(p.count - blocks * VEC);
+        if (tail != 0 && threadIdx.x == 0) {
+            RegisterFile rf;
+            load_operands<false, operands>(p, blocks * VEC, tail, rf);
+            Generic::run(p, rf, tail, flags);
+            store_outputs(p, blocks * VEC, tail, rf);
+        }
+    }
+};
+
+// Programs whose threads wait on one another (a shared-memory pipeline)
+// declare cta_pipeline; their CTA decides once whether to skip.
+template <class Prog, class = void>
+struct UniformSkip {
+    static constexpr bool value = false;
+};
+template <class Prog>
+struct UniformSkip<Prog, std::void_t<decltype(Prog::cta_pipeline)>> {
+    static constexpr bool value = Prog::cta_pipeline;
+};
+
 template <class Prog, bool WIDE>
 __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c_ew_params p)
 {
-    const bool skip = failed_before(p.status, p.skip_before);
+    bool skip;
+    if constexpr (UniformSkip<Prog>::value) {
+        // one reading for the whole CTA: its threads meet at barriers
+        __shared__ int skip_cta;
+        if (threadIdx.x == 0) skip_cta = failed_before(p.status, p.skip_before) ? 1 : 0;
+        __syncthreads();
+        skip = skip_cta != 0;
+    } else {
+        skip = failed_before(p.status, p.skip_before);
+    }
     if (p.first_of_run && !skip && blockIdx.x == 0 && threadIdx.x == 0) {
         atomicAdd(&p.status->runs_started, 1u);
     }
@@ -1030,6 +1160,9 @@ struct Entry {
     uint64_t ops[M3C_EW_MAX_OPS];
     ew_fn kernel;
     int unroll;  // blocks of VEC elements per thread and pass
+    ew_fn bulk;  // the TMA-fed variant (nullptr: none)
+    int bulk_smem;
+    int bulk_tile;  // elements per TMA tile
 };
 
 constexpr int count_of(std::initializer_list<uint64_t> ops)
@@ -1041,12 +1174,13 @@ constexpr int count_of(std::initializer_list<uint64_t> ops)
 // generic kernel's 64-bit addressing.
 #define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS)                                                  \
     {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>, \
-     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll},
+     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll, nullptr, 0, 0},
 
 // the dedicated 16-bit gated SiLU programs, matched like the table's own
 #define M3C_GSILU16_ENTRY(DT, OPSIG, OUTSIG, OPS)                                                  \
     {2, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Gsilu16<DT, OPSIG, OUTSIG, OPS>, false>,    \
-     Gsilu16<DT, OPSIG, OUTSIG, OPS>::unroll},
+     Gsilu16<DT, OPSIG, OUTSIG, OPS>::unroll, ew_kernel<Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>, false>,     \
+     Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::SMEM, Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::TILE},
 
 const Entry PROGRAMS[] = {
     M3C_GSILU16_ENTRY(M3C_F16, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_GSILU_F16)
@@ -1159,12 +1293,40 @@ extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
     if (grid == 0) grid = 1;  // empty tensors still run the reduction epilogue
     choice->kernel = reinterpret_cast<void *>(kernel);
     choice->grid = grid;
+    choice->bulk = nullptr;
+    choice->bulk_grid = 0;
+    choice->bulk_smem = 0;
+    choice->reserved = 0;
+    if (entry != nullptr && entry->bulk != nullptr && params->reduce == nullptr) {
+        // at least one whole tile per CTA, one CTA per SM
+        uint64_t tiles = params->count / static_cast<uint64_t>(entry->bulk_tile);
+        if (tiles > static_cast<uint64_t>(m3c::sm_count())) tiles = static_cast<uint64_t>(m3c::sm_count());
+        if (tiles >= 1u && cudaFuncSetAttribute(entry->bulk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                entry->bulk_smem) == cudaSuccess) {
+            choice->bulk = reinterpret_cast<void *>(entry->bulk);
+            choice->bulk_grid = tiles;
+            choice->bulk_smem = static_cast<uint32_t>(entry->bulk_smem);
+        } else {
+            (void)cudaGetLastError();
+        }
+    }
     return 0;
 }
 
 extern "C" int m3c_launch_ew_chosen(const m3c_ew_choice *choice, const m3c_ew_params *params,
                                     void *stream)
 {
+    if (choice->bulk != nullptr && !params->outputs[0].scalar_only) {
+        const uintptr_t bits = reinterpret_cast<uintptr_t>(params->operands[0].base) |
+                               reinterpret_cast<uintptr_t>(params->operands[1].base) |
+                               reinterpret_cast<uintptr_t>(params->outputs[0].base);
+        if ((bits & 15u) == 0u) {
+            const m3c::ew_fn bulk = reinterpret_cast<m3c::ew_fn>(choice->bulk);
+            bulk<<<static_cast<unsigned>(choice->bulk_grid), m3c::THREADS, choice->bulk_smem,
+                   static_cast<cudaStream_t>(stream)>>>(*params);
+            return static_cast<int>(cudaGetLastError());
+        }
+    }
     const m3c::ew_fn kernel = reinterpret_cast<m3c::ew_fn>(choice->kernel);
     kernel<<<static_cast<unsigned>(choice->grid), m3c::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
         *params);

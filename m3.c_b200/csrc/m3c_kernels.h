@@ -240,6 +240,12 @@ typedef struct {
 typedef struct {
     void *kernel;
     uint64_t grid;
+    /* a TMA-fed variant (NULL: none), taken when the launch's pointers are
+     * 16-byte aligned */
+    void *bulk;
+    uint64_t bulk_grid;
+    uint32_t bulk_smem;
+    uint32_t reserved;
 } m3c_ew_choice;
 int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice);
 int m3c_launch_ew_chosen(const m3c_ew_choice *choice, const m3c_ew_params *params,

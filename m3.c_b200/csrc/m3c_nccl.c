@@ -98,14 +98,19 @@ static m3_status nccl_failure(m3_error *error, ncclResult_t result,
                          nccl.error_string(result));
 }
 
-/* Wait (bounded) until the communicator's pending operation has finished. */
+/* Wait (bounded) until the communicator's pending operation has finished.
+ * An enqueue on a non-blocking communicator usually settles within
+ * microseconds, so the first polls spin; later ones back off to sleeps of up
+ * to 200 us (communicator set-up takes milliseconds). */
 static m3_status settle_comm(ncclComm_t comm, double limit_seconds,
                              const char *what, m3_error *error)
 {
     double deadline = seconds_now() + limit_seconds;
     ncclResult_t state = ncclInProgress;
+    long pause_ns = 1000;
+    unsigned polls;
 
-    for (;;) {
+    for (polls = 0U;; ++polls) {
         ncclResult_t result = nccl.async_error(comm, &state);
 
         if (result != ncclSuccess) {
@@ -119,10 +124,13 @@ static m3_status settle_comm(ncclComm_t comm, double limit_seconds,
                                  "%s: no answer within %.0f s", what,
                                  limit_seconds);
         }
-        {
-            struct timespec pause = {0, 200000};
+        if (polls >= 256U) {
+            struct timespec pause = {0, pause_ns};
 
             (void)nanosleep(&pause, NULL);
+            if (pause_ns < 200000) {
+                pause_ns *= 2;
+            }
         }
     }
     if (state != ncclSuccess) {

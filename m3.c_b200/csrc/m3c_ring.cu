@@ -56,6 +56,7 @@
 
 #include "m3c_device.cuh"
 #include "m3c_kernels.h"
+#include "m3c_bulk.cuh"
 
 namespace m3c {
 namespace {
@@ -67,9 +68,6 @@ constexpr int CHAIN_LANES = 24;         // rows the chain warp sums at once
 constexpr int GROUPS = 4;               // chain lane groups, a quarter row apart
 constexpr int PREFETCH = 8;             // 16-byte loads a chain lane runs ahead
 constexpr int ROW_WARPS = 11;           // the other warps of sub-partitions 1-3
-constexpr uint32_t SLEEP_NS = 2000;     // suspend hint of waits off the chain
-constexpr uint64_t WAIT_NS = 2000000000ull;   // 2 s per wait, then give up
-constexpr uint32_t INTERNAL_CODE = 9u;  // M3_STATUS_INTERNAL
 
 template <int WIDTH>
 struct RingGeometry {
@@ -88,96 +86,6 @@ struct RingGeometry {
     static_assert(LAG % 11 == 0 && LAG > CHAIN_LANES, "a row warp's out lag: its own rows, after the chain");
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
-{
-    asm volatile("{\n\t.reg .b64 state;\n\tmbarrier.arrive.shared::cta.b64 state, [%0];\n\t}" ::"r"(
-                     smem_addr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
-{
-    asm volatile("{\n\t.reg .b64 state;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 state, [%0], %1;\n\t}" ::"r"(
-                     smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ uint64_t now_ns()
-{
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Wait for the phase of `parity` to complete; false after WAIT_NS.  SLEEPY
-// waits ask the hardware to suspend the warp until the phase completes (a
-// suspend-time hint), so a waiting warp takes no issue slots from its
-// sub-partition; the chain warp's own waits poll.
-template <bool SLEEPY>
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
-{
-    const uint32_t addr = smem_addr(bar);
-    uint64_t deadline = 0;
-    for (uint32_t spin = 0;; ++spin) {
-        uint32_t done;
-        if (SLEEPY) {
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(done)
-                : "r"(addr), "r"(parity), "r"(SLEEP_NS)
-                : "memory");
-        } else {
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(done)
-                : "r"(addr), "r"(parity)
-                : "memory");
-        }
-        if (done) return true;
-        if ((spin & 255u) == 0u) {
-            const uint64_t t = now_ns();
-            if (deadline == 0) {
-                deadline = t + WAIT_NS;
-            } else if (t > deadline) {
-                return false;
-            }
-        }
-    }
-}
-
-// Poll a shared-memory word with acquire loads until it equals `want`
-// (false after WAIT_NS): what its writer stored before its release fence is
-// then visible.
-__device__ __forceinline__ bool poll_acquire(volatile int *word, int want)
-{
-    const uint32_t addr = smem_addr(const_cast<int *>(word));
-    uint64_t deadline = 0;
-    for (uint32_t spin = 0;; ++spin) {
-        int seen;
-        asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(seen) : "r"(addr) : "memory");
-        if (seen == want) return true;
-        if ((spin & 255u) == 0u) {
-            const uint64_t t = now_ns();
-            if (deadline == 0) {
-                deadline = t + WAIT_NS;
-            } else if (t > deadline) {
-                return false;
-            }
-        }
-    }
-}
-
 // Poll a published (use, value) word until its use is `want`.
 __device__ __forceinline__ bool poll_sum(volatile unsigned long long *word, unsigned want,
                                          unsigned long long *value)
@@ -193,21 +101,12 @@ __device__ __forceinline__ bool poll_sum(volatile unsigned long long *word, unsi
         if ((spin & 255u) == 0u) {
             const uint64_t t = now_ns();
             if (deadline == 0) {
-                deadline = t + WAIT_NS;
+                deadline = t + BULK_WAIT_NS;
             } else if (t > deadline) {
                 return false;
             }
         }
     }
-}
-
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
-{
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
 }
 
 // NaN-propagating maximum (PTX max.NaN).
@@ -218,11 +117,6 @@ __device__ __forceinline__ float max_nan(float a, float b)
     return r;
 }
 
-__device__ __forceinline__ void timed_out(m3c_status *status, uint32_t command)
-{
-    atomicMin(&status->fail_command, command);
-    atomicExch(&status->fail_code, INTERNAL_CODE);
-}
 
 __device__ __noinline__ float ring_ieee_div(float a, float b) { return __fdiv_rn(a, b); }
 
@@ -292,8 +186,8 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         for (int i = 0; i < local_rows; ++i) {
             const int s = i % SLOTS;
             const int use = i / SLOTS;
-            if (use > 0 && !mbar_wait<false>(&empty[s], (use - 1) & 1)) {
-                timed_out(p.status, first_command);
+            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                bulk_timed_out(p.status, first_command);
                 ok = false;
                 break;
             }
@@ -305,7 +199,7 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         if (!ok) {
             // let every copy this thread issued land before the CTA ends
             for (int s = 0; s < SLOTS; ++s) {
-                if (slot_issued[s] & 1u) (void)mbar_wait<false>(&full[s], (slot_issued[s] >> 1) & 1u);
+                if (slot_issued[s] & 1u) (void)mbar_wait(&full[s], (slot_issued[s] >> 1) & 1u);
             }
         }
         return;
@@ -348,7 +242,7 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
                 }
             }
             if (__any_sync(0xffffffffu, failed)) {
-                if (failed) timed_out(p.status, first_command);
+                if (failed) bulk_timed_out(p.status, first_command);
                 break;
             }
             if (cur >= 0 && summing) {
@@ -384,8 +278,8 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
     // max / first argmax / NaN, top-1, exponentials in place
     auto exp_row = [&](int i) -> bool {
         const int s = i % SLOTS;
-        if (!mbar_wait<false>(&full[s], (i / SLOTS) & 1)) {
-            timed_out(p.status, first_command);
+        if (!mbar_wait(&full[s], (i / SLOTS) & 1)) {
+            bulk_timed_out(p.status, first_command);
             return false;
         }
         float4 *row4 = reinterpret_cast<float4 *>(rows_area + s * PITCH);
@@ -476,7 +370,7 @@ __global__ void __launch_bounds__(RING_THREADS, 1)
         const int s = j % SLOTS;
         unsigned long long published = 0ull;
         if (!poll_sum(&summed[s], j / SLOTS + 1, &published)) {
-            timed_out(p.status, first_command);
+            bulk_timed_out(p.status, first_command);
             return false;
         }
         if (p.probs != nullptr) {
