@@ -865,13 +865,13 @@ struct Gsilu16 {
 };
 
 // The same gated SiLU fed by 1-D TMA, for contiguous 16-byte-aligned
-// operands: one CTA per SM; warp 0's first lane copies tiles of gate and up
-// (TILE elements each, cp.async.bulk with mbarrier completion, no tensor
-// map, no multicast) into a ring of STAGES shared-memory stages; warps 1-15
-// take 16 bytes of both per tile (8 elements each), compute them with
-// Gsilu16's block, and stream the results to HBM.  STAGES tiles (210 KB) are
-// in flight per SM without holding registers, where the register-fed loop
-// keeps about 64 KB in flight at its two CTAs per SM.
+// operands: two CTAs per SM; in each, warp 0's first lane copies tiles of
+// gate and up (TILE elements each, cp.async.bulk with mbarrier completion,
+// no tensor map, no multicast) into a ring of STAGES shared-memory stages;
+// warps 1-15 take 16 bytes of both per tile (8 elements each), compute them
+// with Gsilu16's block, and stream the results to HBM.  2 * STAGES tiles
+// (210 KB) are in flight per SM without holding registers, where the
+// register-fed loop keeps about 64 KB in flight.
 template <int DT, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
 struct Gsilu16Bulk {
     using Base = Gsilu16<DT, OPSIG, OUTSIG, OPS...>;
@@ -882,8 +882,9 @@ struct Gsilu16Bulk {
     static constexpr int CONSUMERS = THREADS - 32;
     static constexpr int TILE = CONSUMERS * 8;       // elements per tile
     static constexpr int TILE_BYTES = TILE * 2;      // per operand
-    static constexpr int STAGES = 14;
+    static constexpr int STAGES = 7;
     static constexpr int SMEM = STAGES * 2 * TILE_BYTES + STAGES * 16;
+    static constexpr int CTAS_PER_SM = 2;
 
     __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid, Flags &flags)
     {
@@ -1163,6 +1164,7 @@ struct Entry {
     ew_fn bulk;  // the TMA-fed variant (nullptr: none)
     int bulk_smem;
     int bulk_tile;  // elements per TMA tile
+    int bulk_ctas;  // resident CTAs per SM
 };
 
 constexpr int count_of(std::initializer_list<uint64_t> ops)
@@ -1174,13 +1176,14 @@ constexpr int count_of(std::initializer_list<uint64_t> ops)
 // generic kernel's 64-bit addressing.
 #define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS)                                                  \
     {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>, \
-     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll, nullptr, 0, 0},
+     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll, nullptr, 0, 0, 0},
 
 // the dedicated 16-bit gated SiLU programs, matched like the table's own
 #define M3C_GSILU16_ENTRY(DT, OPSIG, OUTSIG, OPS)                                                  \
     {2, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Gsilu16<DT, OPSIG, OUTSIG, OPS>, false>,    \
      Gsilu16<DT, OPSIG, OUTSIG, OPS>::unroll, ew_kernel<Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>, false>,     \
-     Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::SMEM, Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::TILE},
+     Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::SMEM, Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::TILE,                 \
+     Gsilu16Bulk<DT, OPSIG, OUTSIG, OPS>::CTAS_PER_SM},
 
 const Entry PROGRAMS[] = {
     M3C_GSILU16_ENTRY(M3C_F16, (operand_sig({C16, C16})), (output_sig({OUT(0, M3C_F16)})), OPS_GSILU_F16)
@@ -1298,9 +1301,10 @@ extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
     choice->bulk_smem = 0;
     choice->reserved = 0;
     if (entry != nullptr && entry->bulk != nullptr && params->reduce == nullptr) {
-        // at least one whole tile per CTA, one CTA per SM
+        // at least one whole tile per CTA, every resident CTA and no more
+        const uint64_t resident = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(entry->bulk_ctas);
         uint64_t tiles = params->count / static_cast<uint64_t>(entry->bulk_tile);
-        if (tiles > static_cast<uint64_t>(m3c::sm_count())) tiles = static_cast<uint64_t>(m3c::sm_count());
+        if (tiles > resident) tiles = resident;
         if (tiles >= 1u && cudaFuncSetAttribute(entry->bulk, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 entry->bulk_smem) == cudaSuccess) {
             choice->bulk = reinterpret_cast<void *>(entry->bulk);
