@@ -808,6 +808,13 @@ m3_status m3_cuda_exp_self_test(int device, uint32_t *max_ulp,
 m3_status m3_cuda_sin_squared_self_test(int device, float *max_abs_error,
                                         uint32_t *max_ulp, m3_error *error);
 
+/* Diagnostics: the snake's sin^2 runs two arguments per packed F32x2
+ * instruction; this compares that evaluation with the scalar one, bit for
+ * bit, on every F32 argument in [-8192, 8192] and reports the number of
+ * differing results (0 expected). */
+m3_status m3_cuda_sin_squared_packed_self_test(int device, uint64_t *mismatches,
+                                               m3_error *error);
+
 /* ------------------------------------------------------------------------
  * Abs-max without allocation.  No counterpart in the reference: m3.c has no
  * device memory to manage, so it has no allocation-free variant either.

@@ -317,10 +317,18 @@ __device__ __forceinline__ float exp_moderate(float d)
 // measures the error over every F32 argument of the range.
 constexpr float SIN_SQUARED_LIMIT = 8192.0f;
 
+// The quadrant k is the integer nearest the exact t 2/pi: one fused
+// multiply-add of 1.5 * 2^23 (at that magnitude the F32 grid is the
+// integers, and the even shift keeps ties to even; exact while
+// |t 2/pi| < 2^22), with k's parity in the sum's last bit.  The packed
+// sin_squared2 takes the same single rounding.
+constexpr float QUADRANT_SHIFT = 0x1.8p23f;
+
 __device__ __forceinline__ float sin_squared(float t)
 {
-    const int k = __float2int_rn(__fmul_rn(t, 0x1.45f306p-1f));  // 2/pi
-    const float kf = __int2float_rn(k);
+    const float m = __fmaf_rn(t, 0x1.45f306p-1f, QUADRANT_SHIFT);  // 2/pi
+    const float kf = __fsub_rn(m, QUADRANT_SHIFT);
+    const bool odd = (__float_as_uint(m) & 1u) != 0u;
     float r = __fmaf_rn(-kf, 0x1.921fb6p+0f, t);                   // pi/2 in three parts
     r = __fmaf_rn(-kf, -0x1.777a5cp-25f, r);
     r = __fmaf_rn(-kf, -0x1.ee59dap-50f, r);
@@ -333,7 +341,79 @@ __device__ __forceinline__ float sin_squared(float t)
     q = __fmaf_rn(q, u, -0x1.555556p-2f);                          // -2^3 / 4!
     q = __fmaf_rn(q, u, 1.0f);                                     // 2 / 2!
     const float s = __fmul_rn(u, q);
-    return (k & 1) != 0 ? __fsub_rn(1.0f, s) : s;
+    return odd ? __fsub_rn(1.0f, s) : s;
+}
+
+// Two F32 lanes in one instruction (PTX add / mul / fma .rn.f32x2, sm_100):
+// each lane is rounded as the scalar instruction rounds it.  One caution,
+// measured here: a packed multiply whose only use is the addend of a packed
+// add was contracted into one fused operation despite .rn (and despite
+// ptxas --fmad=false), so packed code never feeds a packed product straight
+// into a packed add; products that must round on their own stay scalar.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_splat(float v)
+{
+    return f2_pack(v, v);
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// sin_squared of two arguments, bit for bit: the same quadrant fma, -k c as
+// k (-c), and 1 - s as fma(s, -1, 1).  m3_cuda_sin_squared_packed_self_test
+// compares it with sin_squared on every F32 argument of the range.
+__device__ __forceinline__ void sin_squared2(float t0, float t1, float &s0, float &s1)
+{
+    const uint64_t t = f2_pack(t0, t1);
+    const uint64_t m = f2_fma(t, f2_splat(0x1.45f306p-1f), f2_splat(QUADRANT_SHIFT));
+    const uint64_t kf = f2_add(m, f2_splat(-QUADRANT_SHIFT));
+    uint64_t r = f2_fma(kf, f2_splat(-0x1.921fb6p+0f), t);
+    r = f2_fma(kf, f2_splat(0x1.777a5cp-25f), r);
+    r = f2_fma(kf, f2_splat(0x1.ee59dap-50f), r);
+    const uint64_t u = f2_mul(r, r);
+    uint64_t q = f2_fma(f2_splat(0x1.93974ap-24f), u, f2_splat(-0x1.1eed8ep-18f));
+    q = f2_fma(q, u, f2_splat(0x1.27e4fcp-13f));
+    q = f2_fma(q, u, f2_splat(-0x1.a01a02p-9f));
+    q = f2_fma(q, u, f2_splat(0x1.6c16c2p-5f));
+    q = f2_fma(q, u, f2_splat(-0x1.555556p-2f));
+    q = f2_fma(q, u, f2_splat(1.0f));
+    const uint64_t sq = f2_mul(u, q);
+    const uint64_t alt = f2_fma(sq, f2_splat(-1.0f), f2_splat(1.0f));
+    float a0, a1, m0, m1;
+    f2_unpack(sq, s0, s1);
+    f2_unpack(alt, a0, a1);
+    f2_unpack(m, m0, m1);
+    s0 = (__float_as_uint(m0) & 1u) != 0u ? a0 : s0;
+    s1 = (__float_as_uint(m1) & 1u) != 0u ? a1 : s1;
 }
 
 // a / b within about one ulp for normal a / b and b: the hardware reciprocal

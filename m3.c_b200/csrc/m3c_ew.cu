@@ -374,11 +374,19 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
             const float largest =
                 fmaxf(fmaxf(fabsf(angle[0]), fabsf(angle[1])), fmaxf(fabsf(angle[2]), fabsf(angle[3])));
             if (largest <= SIN_SQUARED_LIMIT) {  // false for NaN
-                // the square of the sine straight from sin_squared: a few
-                // F32 ulps, far inside the activation's 0x1p-19 tolerance
+                // the square of the sine straight from sin_squared (a few F32
+                // ulps, far inside the activation's 0x1p-19 tolerance), two
+                // elements per packed instruction; inverse * sq and x + that
+                // stay scalar, separately rounded as the reference's
+                // statements are
 #pragma unroll
-                for (int j = 0; j < VEC; ++j) {
-                    d[j] = as_bits(__fadd_rn(as_float(a[j]), __fmul_rn(inverse, sin_squared(angle[j]))));
+                for (int j = 0; j < VEC; j += 2) {
+                    float sq[2];
+                    sin_squared2(angle[j], angle[j + 1], sq[0], sq[1]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        d[j + h] = as_bits(__fadd_rn(as_float(a[j + h]), __fmul_rn(inverse, sq[h])));
+                    }
                 }
             } else {
 #pragma unroll
@@ -780,6 +788,31 @@ struct Gsilu16 {
         }
     }
 
+    // g / (1 + e^-g) for two gates, exp_moderate and div_approx with their
+    // F32 statements two lanes per packed instruction (the same bits)
+    __device__ __forceinline__ static void silu_pair(float g0, float g1, float &s0, float &s1)
+    {
+        const uint64_t g = f2_pack(g0, g1);
+        const uint64_t d = f2_mul(g, f2_splat(-1.0f));                    // -g, exact
+        const uint64_t h = f2_mul(d, f2_splat(0x1.715476p+0f));
+        uint64_t c = f2_fma(h, f2_splat(-0x1.62e000p-1f), d);
+        c = f2_fma(h, f2_splat(-0x1.0bfbe8p-15f), c);
+        float h0, h1, r0, r1;
+        f2_unpack(h, h0, h1);
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(h0));
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(h1));
+        const uint64_t r = f2_pack(r0, r1);
+        const uint64_t den = f2_add(f2_splat(1.0f), f2_fma(r, c, r));  // 1 + e^-g
+        float b0, b1, y0, y1;
+        f2_unpack(den, b0, b1);
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(b0));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y1) : "f"(b1));
+        const uint64_t y = f2_pack(y0, y1);
+        const uint64_t q0 = f2_mul(g, y);
+        const uint64_t rem = f2_fma(q0, f2_mul(den, f2_splat(-1.0f)), g);
+        f2_unpack(f2_fma(rem, y, q0), s0, s1);
+    }
+
     // four results (two packed words) from four gates and ups
     __device__ __forceinline__ static uint2 block(const m3c_ew_params &p, uint2 gw, uint2 uw, Flags &flags)
     {
@@ -804,7 +837,7 @@ struct Gsilu16 {
             // product; no NaN or infinity reaches this path)
             float s[VEC];
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) s[j] = div_approx(g[j], __fadd_rn(1.0f, exp_moderate(-g[j])));
+            for (int j = 0; j < VEC; j += 2) silu_pair(g[j], g[j + 1], s[j], s[j + 1]);
             return make_uint2(mul2(narrow2(s[0], s[1]), uw.x), mul2(narrow2(s[2], s[3]), uw.y));
         }
         RegisterFile rf;

@@ -271,6 +271,27 @@ __global__ void sin_squared_check_kernel(unsigned int *worst_abs_bits, unsigned 
     atomicMax(worst_ulps, ulps);
 }
 
+// sin_squared2 against sin_squared, bit for bit, on every F32 argument in
+// [-8192, 8192] (each argument once in each lane).
+__global__ void sin_squared_packed_check_kernel(unsigned long long *mismatches)
+{
+    constexpr uint32_t last = 0x46000000u;  // |8192.0|
+    unsigned long long bad = 0ull;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i <= last; i += stride) {
+        const float t = as_float(i);
+        const float u = as_float(0x80000000u | (last - i));
+        float p0, p1, q0, q1;
+        sin_squared2(t, u, p0, p1);
+        sin_squared2(u, t, q0, q1);
+        const uint32_t want_t = as_bits(sin_squared(t));
+        const uint32_t want_u = as_bits(sin_squared(u));
+        bad += (as_bits(p0) != want_t) + (as_bits(p1) != want_u) + (as_bits(q0) != want_u) +
+               (as_bits(q1) != want_t);
+    }
+    if (bad != 0ull) atomicAdd(mismatches, bad);
+}
+
 }  // namespace
 }  // namespace m3c
 
@@ -501,4 +522,33 @@ extern "C" int m3c_launch_shard_unpack(const m3c_shard_words *words, void *strea
 extern "C" const char *m3c_cuda_error_string(int code)
 {
     return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
+
+extern "C" m3_status m3_cuda_sin_squared_packed_self_test(int device, uint64_t *mismatches, m3_error *error)
+{
+    unsigned long long *counter = nullptr;
+    unsigned long long host = 0;
+    cudaError_t code = cudaSetDevice(device);
+    if (code == cudaSuccess) code = cudaMalloc(&counter, sizeof(*counter));
+    if (code == cudaSuccess) code = cudaMemset(counter, 0, sizeof(*counter));
+    if (code == cudaSuccess) {
+        m3c::sin_squared_packed_check_kernel<<<148 * 16, 256>>>(counter);
+        code = cudaGetLastError();
+    }
+    if (code == cudaSuccess) code = cudaMemcpy(&host, counter, sizeof(host), cudaMemcpyDeviceToHost);
+    if (counter != nullptr) cudaFree(counter);
+    if (code != cudaSuccess) {
+        if (error != nullptr) {
+            error->status = M3_STATUS_INTERNAL;
+            snprintf(error->message, sizeof(error->message), "packed sin^2 self-test failed: %s",
+                     cudaGetErrorString(code));
+        }
+        return M3_STATUS_INTERNAL;
+    }
+    if (mismatches != nullptr) *mismatches = host;
+    if (error != nullptr) {
+        error->status = M3_STATUS_OK;
+        error->message[0] = '\0';
+    }
+    return M3_STATUS_OK;
 }

@@ -369,6 +369,8 @@ _CUDA_SIGNATURES = {
     "m3_cuda_sin_squared_self_test": (ctypes.c_int, [
         ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_uint32),
         ctypes.POINTER(M3Error)]),
+    "m3_cuda_sin_squared_packed_self_test": (ctypes.c_int, [
+        ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(M3Error)]),
     "m3_cuda_exp_self_test": (ctypes.c_int, [
         ctypes.c_int, ctypes.POINTER(ctypes.c_uint32),
         ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(M3Error)]),

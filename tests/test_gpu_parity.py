@@ -131,6 +131,18 @@ def test_sin_squared_error_bound(m3, gpu):
     assert worst.value <= 4
 
 
+def test_sin_squared_packed_matches_scalar(m3, gpu):
+    """The snake's packed (F32x2) sin^2 gives the scalar evaluation's bits on
+    every F32 argument in [-8192, 8192], in either lane."""
+    import ctypes
+
+    mismatches = ctypes.c_uint64(99)
+    err = m3.M3Error()
+    m3.check(m3.load().m3_cuda_sin_squared_packed_self_test(0, ctypes.byref(mismatches),
+                                                            ctypes.byref(err)), err)
+    assert mismatches.value == 0
+
+
 # ------------------------------------------------------------ element-wise
 
 
