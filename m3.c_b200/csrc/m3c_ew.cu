@@ -560,6 +560,14 @@ template <int NOPERANDS, uint64_t OPSIG, uint64_t OUTSIG, uint64_t... OPS>
 struct Fixed {
     static constexpr bool custom_loop = false;
     static constexpr int unroll = 4;  // blocks per thread and pass, loads all in flight
+    // no transcendental op (SNAKE1D's sin^2, TANH, F32 gated SiLU): the
+    // program leaves issue slots to spare for a shared-memory pipeline
+    __host__ __device__ static constexpr bool light()
+    {
+        return ((static_cast<int>(OPS & 0xffu) != M3C_OP_SNAKE && static_cast<int>(OPS & 0xffu) != M3C_OP_TANH &&
+                 static_cast<int>(OPS & 0xffu) != M3C_OP_GSILU) &&
+                ...);
+    }
     static constexpr int operands = NOPERANDS;
     static constexpr uint64_t opsig = OPSIG;
     static constexpr uint64_t outsig = OUTSIG;
@@ -1006,6 +1014,197 @@ struct Gsilu16Bulk {
     }
 };
 
+// Any signature program fed by 1-D TMA: its contiguous (streamed) operands
+// arrive in shared memory by cp.async.bulk (global -> shared, mbarrier
+// completion, no tensor map, no multicast), one tile of TILE elements per
+// operand per stage, issued by one thread of warp 0; warps 1-15 each take
+// BPT blocks of the tile from shared memory, load the cached operands
+// (broadcast rows and elements, immediates) as the register-fed loop does,
+// run the program and store from registers.  Two CTAs per SM, up to about
+// 200 KB of streamed loads in flight per SM without holding registers.
+// (the table also asks programs that keep the register-fed loop for their
+// bulk geometry, leaving members of those instantiations unused)
+#pragma nv_diag_suppress 177
+template <class Prog>
+struct BulkFixed {
+    static constexpr bool custom_loop = true;
+    static constexpr bool cta_pipeline = true;
+    static constexpr int operands = Prog::operands;
+    static constexpr int CONSUMERS = THREADS - 32;
+    static constexpr int BPT = 2;                          // blocks per consumer per tile
+    static constexpr int TILE_BLOCKS = CONSUMERS * BPT;
+    static constexpr int TILE = TILE_BLOCKS * VEC;         // elements per tile
+    static constexpr int CTAS_PER_SM = 2;
+    static constexpr int BUDGET = 104 * 1024;              // stage bytes per CTA
+
+    __host__ __device__ static constexpr uint32_t sig_of(int i)
+    {
+        return static_cast<uint32_t>((Prog::opsig >> (8 * i)) & 0xffu);
+    }
+    __host__ __device__ static constexpr bool streamed_of(int i)
+    {
+        return sig_of(i) != 0xffu && (sig_of(i) & 7u) == M3C_V_CONTIG;
+    }
+    __host__ __device__ static constexpr int eb_of(int i)
+    {
+        return ((sig_of(i) >> 3) & 3u) == M3C_F16 || ((sig_of(i) >> 3) & 3u) == M3C_BF16 ? 2 : 4;
+    }
+    // byte offset of operand i's tile in a stage (streamed operands only)
+    __host__ __device__ static constexpr int offset_of(int i)
+    {
+        int o = 0;
+        for (int j = 0; j < i; ++j) o += streamed_of(j) ? TILE * eb_of(j) : 0;
+        return o;
+    }
+    static constexpr int STAGE_BYTES = offset_of(Prog::operands);
+    __host__ __device__ static constexpr int streamed_count()
+    {
+        int n = 0;
+        for (int j = 0; j < Prog::operands; ++j) n += streamed_of(j) ? 1 : 0;
+        return n;
+    }
+    static constexpr int STREAMED = streamed_count();
+    static constexpr int STAGES = STAGE_BYTES == 0 ? 0
+                                  : BUDGET / STAGE_BYTES > 8 ? 8
+                                  : BUDGET / STAGE_BYTES < 2 ? 2
+                                                             : BUDGET / STAGE_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGES * 16;
+
+    __device__ __forceinline__ static void run(const m3c_ew_params &p, RegisterFile &rf, int valid, Flags &flags)
+    {
+        Prog::run(p, rf, valid, flags);
+    }
+
+    template <int I>
+    __device__ __forceinline__ static void issue(const m3c_ew_params &p, unsigned char *stage, uint64_t e,
+                                                 uint64_t *bar)
+    {
+        if constexpr (streamed_of(I)) {
+            constexpr int EB = eb_of(I);
+            bulk_load(stage + offset_of(I), static_cast<const unsigned char *>(p.operands[I].base) + e * EB,
+                      TILE * EB, bar);
+        }
+    }
+    template <int... I>
+    __device__ __forceinline__ static void issue_all(const m3c_ew_params &p, unsigned char *stage, uint64_t e,
+                                                     uint64_t *bar, std::integer_sequence<int, I...>)
+    {
+        (issue<I>(p, stage, e, bar), ...);
+    }
+
+    template <int I>
+    __device__ __forceinline__ static void take(const unsigned char *stage, int blk, RegisterFile &rf)
+    {
+        if constexpr (streamed_of(I)) {
+            if constexpr (eb_of(I) == 4) {
+                const uint4 v = reinterpret_cast<const uint4 *>(stage + offset_of(I))[blk];
+                rf.w[I][0] = v.x;
+                rf.w[I][1] = v.y;
+                rf.w[I][2] = v.z;
+                rf.w[I][3] = v.w;
+            } else {
+                const uint2 v = reinterpret_cast<const uint2 *>(stage + offset_of(I))[blk];
+                rf.w[I][0] = v.x & 0xffffu;
+                rf.w[I][1] = v.x >> 16;
+                rf.w[I][2] = v.y & 0xffffu;
+                rf.w[I][3] = v.y >> 16;
+            }
+        }
+    }
+    template <int... I>
+    __device__ __forceinline__ static void take_all(const unsigned char *stage, int blk, RegisterFile &rf,
+                                                    std::integer_sequence<int, I...>)
+    {
+        (take<I>(stage, blk, rf), ...);
+    }
+
+    __device__ static void loop(const m3c_ew_params &p, Flags &flags)
+    {
+        extern __shared__ __align__(16) unsigned char bulk_smem[];
+        uint64_t *full = reinterpret_cast<uint64_t *>(bulk_smem + STAGES * STAGE_BYTES);
+        uint64_t *empty = full + STAGES;
+        constexpr auto ops = std::make_integer_sequence<int, Prog::operands>{};
+        const uint32_t command = p.ops[0].command;
+        const uint64_t tiles = p.count / TILE;
+        const uint64_t first = tiles * blockIdx.x / gridDim.x;
+        const int n = static_cast<int>(tiles * (blockIdx.x + 1) / gridDim.x - first);
+        const int warp = static_cast<int>(threadIdx.x) / 32;
+        const int lane = static_cast<int>(threadIdx.x) % 32;
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < STAGES; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], CONSUMERS / 32);
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        if (warp == 0) {
+            if (lane == 0) {
+                int i = 0;
+                for (; i < n; ++i) {
+                    const int s = i % STAGES;
+                    const int use = i / STAGES;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                        bulk_timed_out(p.status, command);
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    issue_all(p, bulk_smem + s * STAGE_BYTES, (first + static_cast<uint64_t>(i)) * TILE, &full[s],
+                              ops);
+                }
+                // every copy issued has landed before the CTA ends
+                for (int r = i - STAGES < 0 ? 0 : i - STAGES; r < i; ++r) {
+                    (void)mbar_wait(&full[r % STAGES], (r / STAGES) & 1);
+                }
+            }
+        } else {
+            // one consumer group takes every tile in order, so a consumer is
+            // never a phase ahead of the producer's copies
+            const int c = static_cast<int>(threadIdx.x) - 32;
+            for (int i = 0; i < n; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+                    bulk_timed_out(p.status, command);
+                    break;
+                }
+                const unsigned char *stage = bulk_smem + s * STAGE_BYTES;
+                RegisterFile rf[BPT];
+#pragma unroll
+                for (int u = 0; u < BPT; ++u) take_all(stage, c + u * CONSUMERS, rf[u], ops);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+                for (int u = 0; u < BPT; ++u) {
+                    const uint64_t f =
+                        ((first + static_cast<uint64_t>(i)) * TILE_BLOCKS + static_cast<uint64_t>(c + u * CONSUMERS)) *
+                        VEC;
+                    load_block_all<Prog, false, LOAD_CACHED>(p, f, rf[u]);
+                    Prog::run(p, rf[u], VEC, flags);
+                    store_block_all<Prog>(p, f, rf[u]);
+                }
+            }
+        }
+        if (blockIdx.x != gridDim.x - 1) return;
+        // the blocks after the last whole tile, then the partial block: the
+        // last CTA, from HBM
+        const uint64_t blocks = p.count / VEC;
+        for (uint64_t b = tiles * TILE_BLOCKS + threadIdx.x; b < blocks; b += THREADS) {
+            RegisterFile rf;
+            load_block_all<Prog, false, LOAD_ALL>(p, b * VEC, rf);
+            Prog::run(p, rf, VEC, flags);
+            store_block_all<Prog>(p, b * VEC, rf);
+        }
+        const int tail = static_cast<int>(p.count - blocks * VEC);
+        if (tail != 0 && threadIdx.x == 0) {
+            RegisterFile rf;
+            load_operands<false, operands>(p, blocks * VEC, tail, rf);
+            Prog::run(p, rf, tail, flags);
+            store_outputs(p, blocks * VEC, tail, rf);
+        }
+    }
+};
+#pragma nv_diag_default 177
+
 // Programs whose threads wait on one another (a shared-memory pipeline)
 // declare cta_pipeline; their CTA decides once whether to skip.
 template <class Prog, class = void>
@@ -1186,6 +1385,47 @@ constexpr uint64_t output_sig(std::initializer_list<uint32_t> bytes)
 
 typedef void (*ew_fn)(m3c_ew_params);
 
+// The TMA-fed kernel of a signature program with a streamed operand, else
+// none.
+// Measured on the benchmark programs (one B200, L2 flushed): the bulk path
+// speeds up light programs with one streamed operand (x * c + b: 16.2 ->
+// 14.9 us) and slows the snake (2.27 -> 2.44 ms: its arithmetic needs the
+// issue slots the stage handoff takes) and the three-operand CFG chain
+// (134 -> 138 us per 30 runs, whose carried runs are mostly L2 hits).
+template <class Prog>
+ew_fn bulk_kernel_of()
+{
+    if constexpr (Prog::opsig != ANY_OPERANDS) {
+        if constexpr (Prog::light() && BulkFixed<Prog>::STAGE_BYTES != 0 &&
+                      BulkFixed<Prog>::STREAMED <= 2) {
+            return ew_kernel<BulkFixed<Prog>, false>;
+        }
+    }
+    return nullptr;
+}
+
+// Its shared memory, tile and CTAs per SM (0 where it has none).
+template <class Prog>
+constexpr int bulk_smem_of()
+{
+    if constexpr (Prog::opsig != ANY_OPERANDS) return BulkFixed<Prog>::SMEM;
+    return 0;
+}
+
+template <class Prog>
+constexpr int bulk_tile_of()
+{
+    if constexpr (Prog::opsig != ANY_OPERANDS) return BulkFixed<Prog>::TILE;
+    return 0;
+}
+
+template <class Prog>
+constexpr int bulk_ctas_of()
+{
+    if constexpr (Prog::opsig != ANY_OPERANDS) return BulkFixed<Prog>::CTAS_PER_SM;
+    return 0;
+}
+
 struct Entry {
     int operands;
     uint64_t opsig;
@@ -1209,7 +1449,9 @@ constexpr int count_of(std::initializer_list<uint64_t> ops)
 // generic kernel's 64-bit addressing.
 #define M3C_ENTRY(NOPERANDS, OPSIG, OUTSIG, OPS)                                                  \
     {NOPERANDS, OPSIG, OUTSIG, count_of({OPS}), {OPS}, ew_kernel<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>, false>, \
-     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll, nullptr, 0, 0, 0},
+     Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>::unroll, bulk_kernel_of<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>>(),       \
+     bulk_smem_of<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>>(), bulk_tile_of<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>>(),     \
+     bulk_ctas_of<Fixed<NOPERANDS, OPSIG, OUTSIG, OPS>>()},
 
 // the dedicated 16-bit gated SiLU programs, matched like the table's own
 #define M3C_GSILU16_ENTRY(DT, OPSIG, OUTSIG, OPS)                                                  \
@@ -1333,7 +1575,7 @@ extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
     choice->bulk_grid = 0;
     choice->bulk_smem = 0;
     choice->reserved = 0;
-    if (entry != nullptr && entry->bulk != nullptr && params->reduce == nullptr) {
+    if (entry != nullptr && entry->bulk != nullptr) {
         // at least one whole tile per CTA, every resident CTA and no more
         const uint64_t resident = static_cast<uint64_t>(m3c::sm_count()) * static_cast<uint64_t>(entry->bulk_ctas);
         uint64_t tiles = params->count / static_cast<uint64_t>(entry->bulk_tile);
@@ -1353,11 +1595,19 @@ extern "C" int m3c_ew_choose(const m3c_ew_params *params, m3c_ew_choice *choice)
 extern "C" int m3c_launch_ew_chosen(const m3c_ew_choice *choice, const m3c_ew_params *params,
                                     void *stream)
 {
-    if (choice->bulk != nullptr && !params->outputs[0].scalar_only) {
-        const uintptr_t bits = reinterpret_cast<uintptr_t>(params->operands[0].base) |
-                               reinterpret_cast<uintptr_t>(params->operands[1].base) |
-                               reinterpret_cast<uintptr_t>(params->outputs[0].base);
-        if ((bits & 15u) == 0u) {
+    if (choice->bulk != nullptr) {
+        // bulk copies of the streamed operands and 16-byte stores need
+        // 16-byte-aligned bases
+        uintptr_t bits = 0u;
+        bool vector_stores = true;
+        for (int i = 0; i < params->n_operands && i < M3C_EW_MAX_OPERANDS; ++i) {
+            if (params->operands[i].vclass == M3C_V_CONTIG) bits |= reinterpret_cast<uintptr_t>(params->operands[i].base);
+        }
+        for (int o = 0; o < params->n_outputs && o < M3C_EW_MAX_OUTPUTS; ++o) {
+            bits |= reinterpret_cast<uintptr_t>(params->outputs[o].base);
+            vector_stores = vector_stores && !params->outputs[o].scalar_only;
+        }
+        if ((bits & 15u) == 0u && vector_stores) {
             const m3c::ew_fn bulk = reinterpret_cast<m3c::ew_fn>(choice->bulk);
             bulk<<<static_cast<unsigned>(choice->bulk_grid), m3c::THREADS, choice->bulk_smem,
                    static_cast<cudaStream_t>(stream)>>>(*params);
