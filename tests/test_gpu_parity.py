@@ -733,6 +733,63 @@ def test_residual_rms_norm_bit_exact(m3, ref, oracle, gpu, dtype, width):
         assert np.array_equal(bits(a), bits(b))
 
 
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+@pytest.mark.parametrize("rows", [1, 23, 25, 97, 148 * 24 + 7])
+@pytest.mark.parametrize("residual", ["none", "temporary", "output"])
+def test_rms_norm_4k_rows_bit_exact(m3, ref, oracle, gpu, dtype, rows, residual):
+    """RMSNorm over the benchmark's 4 KiB rows (2048 16-bit or 1024 F32
+    elements) with the residual sum absent, a temporary, or a graph output,
+    over row counts from one row to many tiles per CTA: bit-exact against the
+    reference, rows holding an infinity or a NaN included."""
+    dt = getattr(m3, dtype)
+    width = 1024 if dtype == "F32" else 2048
+    enc = {"F32": lambda v: v, "F16": oracle.to_f16, "BF16": oracle.to_bf16}[dtype]
+    rng = np.random.default_rng(rows + width)
+    h = rng.standard_normal((rows, width)).astype(np.float32)
+    r = rng.standard_normal((rows, width)).astype(np.float32)
+    if rows > 2:
+        h[1, 7] = np.inf          # an infinite row and a NaN row stay row-local
+        h[2, 9] = np.nan
+        h[rows - 1] *= 300.0      # large squares
+    h, r = enc(h), enc(r)
+    w = enc(rng.normal(1, 0.05, width).astype(np.float32))
+
+    def build(g):
+        vh = g.value(m3.INPUT, dt, h.shape)
+        vw = g.constant(dt, w)
+        handles = {"h": vh}
+        outputs = []
+        x = vh
+        if residual != "none":
+            vr = g.value(m3.INPUT, dt, r.shape)
+            handles["r"] = vr
+            kind = m3.OUTPUT if residual == "output" else m3.TEMPORARY
+            x = g.inferred("ADD", [vh, vr], kind, dt)
+            g.node("ADD", [vh, vr], [x])
+            if residual == "output":
+                outputs.append(x)
+        n = g.inferred("RMS_NORM", [x, vw], m3.OUTPUT, dt, epsilon=1e-6)
+        g.node("RMS_NORM", [x, vw], [n], epsilon=1e-6)
+        return handles, outputs + [n]
+
+    def nan_mask(b):
+        if b.dtype.itemsize == 4:
+            return np.isnan(b.view(np.float32))
+        exponent, mantissa = (0x7c00, 0x03ff) if dtype == "F16" else (0x7f80, 0x007f)
+        return ((b & exponent) == exponent) & ((b & mantissa) != 0)
+
+    mine, theirs = run_both(m3, ref, build, {"h": h, "r": r})
+    for a, b in zip(mine, theirs):
+        ba, bb = bits(a), bits(b)
+        na, nb = nan_mask(ba), nan_mask(bb)
+        # NaNs made by arithmetic carry each platform's default NaN: compare
+        # NaN-ness there and bits everywhere else
+        assert np.array_equal(na, nb)
+        assert np.array_equal(ba[~na], bb[~nb])
+    if rows > 2:
+        assert nan_mask(bits(mine[-1]))[2].all()   # the NaN row of the norm
+
+
 @pytest.mark.parametrize("dtype", ["F32", "F16"])
 @pytest.mark.parametrize("bias", [True, False])
 def test_layer_norm_bit_exact(m3, ref, oracle, gpu, dtype, bias):
