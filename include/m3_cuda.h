@@ -746,6 +746,11 @@ m3_status m3_cuda_backend_read(void *context, const void *data,
                                size_t byte_count, m3_error *error);
 /* Placement table for m3_provider_select_regular (src/m3_provider.c:7-33). */
 bool m3_cuda_backend_supports_kind(m3_op_kind kind);
+/* Kernels the last m3_cuda_backend_execute on this context launched (no
+ * reference counterpart: a measurement hook).  Consecutive element-wise
+ * commands over one output shape, and SOFTMAX / TOP_K / ROW_SUM commands over
+ * one input view, share a launch where that cannot change a result. */
+unsigned m3_cuda_backend_launch_count(const void *context);
 
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (reference src/m3_rng.c:9-110)

@@ -3,8 +3,10 @@
  *
  * The reference's scheduler hands this backend whole command lists
  * (src/m3_backend.c:113-154 validates them first).  Commands run in order on
- * one stream, one launch per command (no liveness information reaches a
- * backend, so nothing is fused here).  Views may be strided: element-wise
+ * one stream.  Consecutive commands merge into one launch where that cannot
+ * change a result (fuse_ew, fuse_rows below): every output is still written,
+ * since no liveness information reaches a backend, but a value a fused
+ * command wrote is not read back.  Views may be strided: element-wise
  * operands are addressed through their strides directly; row operators gather
  * a non-contiguous input into the backend's reusable gather buffer first.
  * Data-checked operators
@@ -34,6 +36,8 @@ typedef struct {
      * copy is consumed before the next command overwrites it) */
     void *gather;
     size_t gather_bytes;
+    /* kernels launched by the last execute */
+    unsigned launches;
 } cuda_backend;
 
 static const m3c_status clean = {UINT32_MAX, 0U, 0U, UINT32_MAX};
@@ -359,6 +363,7 @@ static int launch_unary_ew(cuda_backend *b, uint32_t command, uint8_t code,
                                ? 1
                                : 0;
     }
+    ++b->launches;
     return m3c_launch_ew(&p, b->stream);
 }
 
@@ -421,6 +426,7 @@ static int dense_input(cuda_backend *b, const m3_tensor_view *view,
         p.outputs[0].dtype = (int32_t)view->metadata.dtype;
         p.outputs[0].reg = 1;
         p.outputs[0].raw = 1;
+        ++b->launches;
         result = m3c_launch_ew(&p, b->stream);
     }
     *data = *temporary;
@@ -455,6 +461,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
             const void *data;
             code = dense_input(b, in, index, &data, temporary);
             if (code == 0) {
+                ++b->launches;
                 code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
                                        in->metadata.element_count, 1, index,
                                        b->status, b->stream);
@@ -508,6 +515,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
 
         code = dense_input(b, in, index, &data, temporary);
         if (code == 0) {
+            ++b->launches;
             code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
                                    in->metadata.element_count, 0, index,
                                    b->status, b->stream);
@@ -538,6 +546,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
             p.k = c->descriptor.top_k.k;
             p.topk_command = index;
         }
+        ++b->launches;
         return m3c_launch_softmax(&p, b->stream);
     }
     case (int)M3_OP_ROW_SUM: {
@@ -567,6 +576,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
                                         c->descriptor.copy.output->metadata.byte_count,
                                         b->stream);
         }
+        ++b->launches;
         return m3c_launch_softmax(&p, b->stream);
     }
     case M3_OP_CATEGORICAL: {
@@ -597,6 +607,7 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
          * when no row failed: a failing command writes nothing */
         p.skip_before = index;
         p.check_only = 1;
+        b->launches += 2U;
         code = m3c_launch_categorical(&p, b->stream);
         if (code == 0) {
             p.skip_before = index + 1U;
@@ -646,11 +657,491 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         p.epsilon = layer ? c->descriptor.layer_norm.epsilon
                           : c->descriptor.rms_norm.epsilon;
         p.status = b->status;
+        ++b->launches;
         return m3c_launch_norm(&p, b->stream);
     }
     default:
         return -1;
     }
+}
+
+/* ------------------------------------------------------- fused launches */
+
+static bool same_view(const m3_tensor_view *x, const m3_tensor_view *y)
+{
+    uint8_t d;
+
+    if (x->storage != y->storage || x->byte_offset != y->byte_offset ||
+        x->metadata.dtype != y->metadata.dtype ||
+        x->metadata.rank != y->metadata.rank) {
+        return false;
+    }
+    for (d = 0U; d < x->metadata.rank; ++d) {
+        if (x->metadata.shape[d] != y->metadata.shape[d] ||
+            (x->metadata.shape[d] > 1U &&
+             x->byte_strides[d] != y->byte_strides[d])) {
+            return false;
+        }
+    }
+    return true;
+}
+
+static bool same_shape(const m3_tensor_metadata *x, const m3_tensor_metadata *y)
+{
+    uint8_t d;
+
+    if (x->rank != y->rank) {
+        return false;
+    }
+    for (d = 0U; d < x->rank; ++d) {
+        if (x->shape[d] != y->shape[d]) {
+            return false;
+        }
+    }
+    return true;
+}
+
+/* Do the byte ranges two views can touch intersect? */
+static bool views_overlap(const cuda_backend *b, const m3_tensor_view *x,
+                          const m3_tensor_view *y)
+{
+    const m3_tensor_view *v[2] = {x, y};
+    uintptr_t lo[2];
+    uintptr_t hi[2];
+    int k;
+
+    for (k = 0; k < 2; ++k) {
+        size_t extent = m3c_dtype_size(v[k]->metadata.dtype);
+        uint8_t d;
+
+        lo[k] = (uintptr_t)view_base(b, v[k]) + v[k]->byte_offset;
+        if (v[k]->metadata.element_count == 0U) {
+            hi[k] = lo[k];
+            continue;
+        }
+        for (d = 0U; d < v[k]->metadata.rank; ++d) {
+            extent += (size_t)(v[k]->metadata.shape[d] - 1U) * v[k]->byte_strides[d];
+        }
+        hi[k] = lo[k] + extent;
+    }
+    return lo[0] < hi[1] && lo[1] < hi[0];
+}
+
+/* An element-wise command without a data check, as one micro-op. */
+typedef struct {
+    uint8_t code;
+    int n_in;
+    const m3_tensor_view *in[2];
+    const m3_tensor_view *out;
+    int aux;
+} ew_step;
+
+static bool ew_step_of(const m3_command *c, ew_step *step)
+{
+    memset(step, 0, sizeof(*step));
+    switch ((int)c->kind) {
+    case M3_OP_COPY:
+        step->code = M3C_OP_MOV;
+        step->in[0] = c->descriptor.copy.input;
+        step->out = c->descriptor.copy.output;
+        break;
+    case M3_OP_CAST: {
+        const m3_tensor_view *in = c->descriptor.cast.input;
+        const m3_tensor_view *out = c->descriptor.cast.output;
+
+        if (out->metadata.dtype == M3_DTYPE_I32 &&
+            in->metadata.dtype != M3_DTYPE_I32) {
+            return false;  /* range-checked: runs on its own */
+        }
+        step->code = in->metadata.dtype == out->metadata.dtype ? M3C_OP_MOV
+                     : in->metadata.dtype == M3_DTYPE_I32      ? M3C_OP_I2F
+                                                               : M3C_OP_ROUND;
+        step->in[0] = in;
+        step->out = out;
+        break;
+    }
+    case M3_OP_ADD:
+    case M3_OP_MUL:
+    case M3_OP_GATED_SILU:
+        step->code = c->kind == M3_OP_ADD   ? M3C_OP_ADD
+                     : c->kind == M3_OP_MUL ? M3C_OP_MUL
+                                            : M3C_OP_GSILU;
+        step->in[0] = c->descriptor.add.left;
+        step->in[1] = c->descriptor.add.right;
+        step->out = c->descriptor.add.output;
+        step->aux = (int)c->descriptor.add.left->metadata.dtype;
+        break;
+    case M3_OP_SNAKE1D:
+        step->code = M3C_OP_SNAKE;
+        step->in[0] = c->descriptor.snake1d.input;
+        step->in[1] = c->descriptor.snake1d.alpha;
+        step->out = c->descriptor.snake1d.output;
+        break;
+    case M3_OP_TANH:
+        step->code = M3C_OP_TANH;
+        step->in[0] = c->descriptor.tanh.input;
+        step->out = c->descriptor.tanh.output;
+        break;
+    case (int)M3_OP_CLAMP_UNIT:
+        step->code = M3C_OP_CLAMP;
+        step->in[0] = c->descriptor.copy.input;
+        step->out = c->descriptor.copy.output;
+        break;
+    default:
+        return false;
+    }
+    step->n_in = step->in[1] != NULL ? 2 : 1;
+    return true;
+}
+
+static bool is_16bit(const m3_tensor_view *v)
+{
+    return v->metadata.dtype == M3_DTYPE_F16 || v->metadata.dtype == M3_DTYPE_BF16;
+}
+
+/* Merge commands [first, first + *count) of the list into one element-wise
+ * launch (*count >= 2 on success; 0: nothing merged).  A command joins when
+ * it has no data check, its output has the group's shape, and it cannot race
+ * with the group:
+ *   - an input that is exactly an earlier member's output view is taken from
+ *     that member's register, which holds the value rounded to its stored
+ *     dtype (what the reference reloads); an input that only partly overlaps
+ *     a member's output ends the group;
+ *   - its output, where it overlaps a member's memory input or output (or its
+ *     own memory input), is exactly that view and contiguous, so each element
+ *     is read and written by the thread that owns its index, in command
+ *     order.
+ * Copies move raw words: a copy reads memory only, and only F32 copies feed
+ * later members. */
+static int fuse_ew(cuda_backend *b, const m3_command *commands, size_t first,
+                   size_t available, size_t *count)
+{
+    enum { MAXSTEPS = 8 };
+    ew_step steps[MAXSTEPS];
+    const m3_tensor_view *loaded[M3C_EW_MAX_OPERANDS];
+    int source[MAXSTEPS][2];   /* >= 0: operand index; < 0: -(member + 1) */
+    int reg_of_step[MAXSTEPS];
+    int reg_of_operand[M3C_EW_MAX_OPERANDS];
+    int n_loaded = 0;
+    int n_widen = 0;           /* registers reserved for widened operands */
+    size_t n = 0U;
+    size_t k;
+    int next_reg;
+    int n_out;
+    m3c_ew_params p;
+
+    *count = 0U;
+    while (n < MAXSTEPS && first + n < available) {
+        ew_step st;
+        int in_src[2] = {0, 0};
+        int new_loads = 0;
+        int new_widen = 0;
+        bool ok = true;
+        int i;
+        size_t m;
+
+        if (!ew_step_of(&commands[first + n], &st) ||
+            (n > 0U && !same_shape(&st.out->metadata, &steps[0].out->metadata))) {
+            break;
+        }
+        for (i = 0; i < st.n_in && ok; ++i) {
+            int found = INT32_MIN;
+
+            /* the latest member that wrote exactly this view */
+            for (m = n; m-- > 0U;) {
+                if (same_view(st.in[i], steps[m].out)) {
+                    found = -(int)m - 1;
+                    break;
+                }
+            }
+            if (found != INT32_MIN) {
+                const ew_step *w = &steps[-found - 1];
+
+                if (st.code == M3C_OP_MOV ||
+                    (w->code == M3C_OP_MOV && w->out->metadata.dtype != M3_DTYPE_F32)) {
+                    ok = false;
+                }
+                in_src[i] = found;
+                continue;
+            }
+            for (m = 0U; m < n; ++m) {
+                if (views_overlap(b, st.in[i], steps[m].out)) {
+                    ok = false;  /* part of a member's output */
+                }
+            }
+            for (m = 0U; m < (size_t)n_loaded && found == INT32_MIN; ++m) {
+                if (same_view(st.in[i], loaded[m])) {
+                    found = (int)m;
+                }
+            }
+            if (found == INT32_MIN && i == 1 && in_src[0] >= n_loaded &&
+                same_view(st.in[1], st.in[0])) {
+                found = in_src[0];  /* both inputs one new operand */
+            }
+            if (found == INT32_MIN) {
+                if (n_loaded + new_loads >= M3C_EW_MAX_OPERANDS) {
+                    ok = false;
+                    break;
+                }
+                found = n_loaded + new_loads++;
+                if (is_16bit(st.in[i])) {
+                    ++new_widen;
+                }
+            }
+            in_src[i] = found;
+        }
+        if (ok) {
+            const m3_tensor_view *out = st.out;
+            bool dense = m3c_contiguous(&out->metadata, out->byte_strides);
+
+            for (m = 0U; m < (size_t)n_loaded && ok; ++m) {
+                if (views_overlap(b, out, loaded[m]) && !(dense && same_view(out, loaded[m]))) {
+                    ok = false;
+                }
+            }
+            for (i = 0; i < st.n_in && ok; ++i) {
+                if (in_src[i] >= n_loaded && views_overlap(b, out, st.in[i]) &&
+                    !(dense && same_view(out, st.in[i]))) {
+                    ok = false;
+                }
+            }
+            for (m = 0U; m < n && ok; ++m) {
+                if (views_overlap(b, out, steps[m].out) && !(dense && same_view(out, steps[m].out))) {
+                    ok = false;
+                }
+            }
+        }
+        if (!ok || n_loaded + new_loads + n_widen + new_widen + (int)n + 1 > M3C_EW_MAX_REGS ||
+            n_widen + new_widen + (int)n + 1 > M3C_EW_MAX_OPS) {
+            break;
+        }
+        for (i = 0; i < st.n_in; ++i) {
+            if (in_src[i] >= n_loaded) {
+                loaded[n_loaded] = st.in[i];
+                in_src[i] = n_loaded++;
+            }
+        }
+        n_widen += new_widen;
+        source[n][0] = in_src[0];
+        source[n][1] = st.n_in == 2 ? in_src[1] : in_src[0];
+        steps[n++] = st;
+    }
+    if (n < 2U) {
+        return 0;
+    }
+    /* registers: the loaded operands, their widened copies, one per member */
+    memset(&p, 0, sizeof(p));
+    p.count = steps[0].out->metadata.element_count;
+    p.status = b->status;
+    p.skip_before = (uint32_t)first;
+    p.n_operands = n_loaded;
+    next_reg = n_loaded;
+    for (k = 0U; k < (size_t)n_loaded; ++k) {
+        const m3_tensor_view *v = loaded[k];
+        bool read_as_float = false;
+        size_t s;
+        int i;
+
+        for (s = 0U; s < n; ++s) {
+            for (i = 0; i < steps[s].n_in; ++i) {
+                if (source[s][i] == (int)k && steps[s].code != M3C_OP_MOV) {
+                    read_as_float = true;
+                }
+            }
+        }
+        m3c_operand_setup(&p.operands[k], view_base(b, v), &v->metadata, v->byte_offset,
+                          v->byte_strides, &steps[0].out->metadata,
+                          v->metadata.dtype == M3_DTYPE_I32 ? M3C_LOAD_INT : M3C_LOAD_RAW);
+        reg_of_operand[k] = (int)k;
+        if (read_as_float && is_16bit(v)) {
+            m3c_ew_op *op = &p.ops[p.n_ops++];
+
+            op->code = M3C_OP_WIDEN;
+            op->dst = (uint8_t)next_reg;
+            op->a = (uint8_t)k;
+            op->b = (uint8_t)k;
+            op->rdtype = M3C_F32;
+            op->aux = (int8_t)v->metadata.dtype;
+            op->command = (uint16_t)first;
+            reg_of_operand[k] = next_reg++;
+        }
+    }
+    for (k = 0U; k < n; ++k) {
+        m3c_ew_op *op = &p.ops[p.n_ops++];
+        int r[2];
+        int i;
+
+        for (i = 0; i < 2; ++i) {
+            int src = source[k][i];
+
+            if (src < 0) {
+                r[i] = reg_of_step[-src - 1];
+            } else {
+                r[i] = steps[k].code == M3C_OP_MOV ? src : reg_of_operand[src];
+            }
+        }
+        op->code = steps[k].code;
+        op->a = (uint8_t)r[0];
+        op->b = (uint8_t)r[1];
+        op->dst = (uint8_t)next_reg;
+        op->rdtype = (int8_t)steps[k].out->metadata.dtype;
+        op->aux = (int8_t)steps[k].aux;
+        op->command = (uint16_t)(first + k);
+        reg_of_step[k] = next_reg++;
+    }
+    /* every output view is stored once, from its last writer in the group */
+    n_out = 0;
+    for (k = 0U; k < n; ++k) {
+        const m3_tensor_view *out = steps[k].out;
+        size_t vector_bytes = 4U * m3c_dtype_size(out->metadata.dtype);
+        bool overwritten = false;
+        size_t later;
+        m3c_ew_out *o;
+
+        for (later = k + 1U; later < n; ++later) {
+            if (same_view(out, steps[later].out)) {
+                overwritten = true;
+            }
+        }
+        if (overwritten) {
+            continue;
+        }
+        if (n_out == M3C_EW_MAX_OUTPUTS) {
+            return 0;  /* nothing launched: the commands run one by one */
+        }
+        o = &p.outputs[n_out++];
+        o->base = view_base(b, out) + out->byte_offset;
+        o->dtype = (int32_t)out->metadata.dtype;
+        o->reg = (int16_t)reg_of_step[k];
+        o->scalar_only = ((uintptr_t)o->base % vector_bytes) != 0U ? 1U : 0U;
+        o->raw = (steps[k].code == M3C_OP_MOV && m3c_dtype_size(out->metadata.dtype) == 2U) ? 1 : 0;
+    }
+    p.n_outputs = n_out;
+    *count = n;
+    ++b->launches;
+    return m3c_launch_ew(&p, b->stream);
+}
+
+/* Merge SOFTMAX / TOP_K / ROW_SUM commands [first, first + *count) over one
+ * input view into one NaN scan and one row pass (*count >= 2 on success).
+ * The data-checked commands (SOFTMAX, TOP_K) come first: a ROW_SUM ahead of
+ * a failing check would have been written by the reference, so it runs on
+ * its own.  No member's output may overlap the input or another member's
+ * output. */
+static int fuse_rows(cuda_backend *b, const m3_command *commands, size_t first,
+                     size_t available, size_t *count, void **temporary)
+{
+    const m3_tensor_view *in = NULL;
+    const m3_tensor_view *outs[6];
+    int n_outs = 0;
+    size_t n = 0U;
+    size_t softmax = SIZE_MAX;
+    size_t topk = SIZE_MAX;
+    size_t rowsum = SIZE_MAX;
+    m3c_softmax_params p;
+    const void *data;
+    int code;
+
+    *count = 0U;
+    while (first + n < available) {
+        const m3_command *c = &commands[first + n];
+        const m3_tensor_view *cin;
+        const m3_tensor_view *cout[2] = {NULL, NULL};
+        bool ok = true;
+        int i;
+
+        if (c->kind == M3_OP_SOFTMAX && softmax == SIZE_MAX && rowsum == SIZE_MAX) {
+            cin = c->descriptor.softmax.input;
+            cout[0] = c->descriptor.softmax.output;
+        } else if (c->kind == M3_OP_TOP_K && topk == SIZE_MAX && rowsum == SIZE_MAX) {
+            cin = c->descriptor.top_k.logits;
+            cout[0] = c->descriptor.top_k.values;
+            cout[1] = c->descriptor.top_k.indices;
+        } else if ((int)c->kind == (int)M3_OP_ROW_SUM && rowsum == SIZE_MAX && n > 0U) {
+            cin = c->descriptor.copy.input;
+            cout[0] = c->descriptor.copy.output;
+        } else {
+            break;
+        }
+        if (in != NULL && !same_view(cin, in)) {
+            break;
+        }
+        for (i = 0; i < 2 && cout[i] != NULL && ok; ++i) {
+            int j;
+
+            if (views_overlap(b, cout[i], cin)) {
+                ok = false;
+            }
+            for (j = 0; j < n_outs; ++j) {
+                if (views_overlap(b, cout[i], outs[j])) {
+                    ok = false;
+                }
+            }
+        }
+        if (!ok) {
+            break;
+        }
+        in = cin;
+        for (i = 0; i < 2 && cout[i] != NULL; ++i) {
+            outs[n_outs++] = cout[i];
+        }
+        if (c->kind == M3_OP_SOFTMAX) {
+            softmax = first + n;
+        } else if (c->kind == M3_OP_TOP_K) {
+            topk = first + n;
+        } else {
+            rowsum = first + n;
+        }
+        ++n;
+    }
+    if (n < 2U || in->metadata.shape[in->metadata.rank - 1U] == 0U) {
+        return 0;
+    }
+    code = dense_input(b, in, (uint32_t)first, &data, temporary);
+    if (code != 0) {
+        return code;
+    }
+    /* the NaN check, reported against the group's first (checked) command */
+    ++b->launches;
+    code = m3c_launch_scan(data, (int32_t)in->metadata.dtype, in->metadata.element_count, 0,
+                           (uint32_t)first, b->status, b->stream);
+    if (code != 0) {
+        return code;
+    }
+    memset(&p, 0, sizeof(p));
+    p.input = data;
+    p.in_dtype = (int32_t)in->metadata.dtype;
+    p.width = in->metadata.shape[in->metadata.rank - 1U];
+    p.rows = in->metadata.element_count / p.width;
+    p.status = b->status;
+    p.skip_before = (uint32_t)first + 1U;
+    p.softmax_command = UINT32_MAX;
+    p.topk_command = UINT32_MAX;
+    p.rowsum_command = UINT32_MAX;
+    if (softmax != SIZE_MAX) {
+        const m3_tensor_view *out = commands[softmax].descriptor.softmax.output;
+
+        p.probs = view_base(b, out) + out->byte_offset;
+        p.probs_dtype = (int32_t)out->metadata.dtype;
+        p.softmax_command = (uint32_t)softmax;
+    }
+    if (topk != SIZE_MAX) {
+        const m3_op_top_k *t = &commands[topk].descriptor.top_k;
+
+        p.top_values = (float *)(view_base(b, t->values) + t->values->byte_offset);
+        p.top_indices = (int32_t *)(view_base(b, t->indices) + t->indices->byte_offset);
+        p.k = t->k;
+        p.topk_command = (uint32_t)topk;
+    }
+    if (rowsum != SIZE_MAX) {
+        const m3_tensor_view *out = commands[rowsum].descriptor.copy.output;
+
+        p.row_sums = (float *)(view_base(b, out) + out->byte_offset);
+        p.rowsum_command = (uint32_t)rowsum;
+    }
+    *count = n;
+    ++b->launches;
+    return m3c_launch_softmax(&p, b->stream);
 }
 
 static const char *check_message(m3_op_kind kind, uint32_t detail)
@@ -699,10 +1190,23 @@ m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
                              "cannot allocate execution state");
     }
     (void)cudaSetDevice(b->device);
-    for (i = 0U; i < command_count; ++i) {
-        int result = run_command(b, &commands[i], (uint32_t)i, &temporaries[i]);
+    b->launches = 0U;
+    for (i = 0U; i < command_count;) {
+        size_t merged = 0U;
+        size_t failing = i;
+        int result = fuse_ew(b, commands, i, command_count, &merged);
 
+        if (result == 0 && merged == 0U) {
+            result = fuse_rows(b, commands, i, command_count, &merged,
+                               &temporaries[i]);
+        }
+        if (result == 0 && merged == 0U) {
+            result = run_command(b, &commands[i], (uint32_t)i, &temporaries[i]);
+            merged = 1U;
+        }
+        i += merged;
         if (result != 0) {
+            i = failing;
             status = m3c_error_set(
                 error, result < 0 ? M3_STATUS_UNSUPPORTED : M3_STATUS_INTERNAL,
                 "CUDA execution of %s failed: %s",
@@ -737,4 +1241,11 @@ m3_status m3_cuda_backend_execute(void *context, const m3_command *commands,
         m3_error_reset(error);
     }
     return status;
+}
+
+unsigned m3_cuda_backend_launch_count(const void *context)
+{
+    const cuda_backend *b = context;
+
+    return b == NULL ? 0U : b->launches;
 }

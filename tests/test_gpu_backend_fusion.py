@@ -1,0 +1,291 @@
+"""Fused launches in the backend plug-in (m3_cuda_backend_execute).
+
+The reference's scheduler hands a backend whole command lists
+(src/m3_graph_session.c:116-150, src/m3_backend.c:113-154).  The plug-in
+merges consecutive element-wise commands over one output shape, and
+SOFTMAX / TOP_K / ROW_SUM commands over one input view, into one launch.
+These tests check that merging never changes a result: every output equals
+what the reference's command-by-command order produces (F32 statements for
+ADD / MUL / COPY, which are bit-exact; the unfused plug-in for the row
+operators), including lists whose views alias, overlap in part or broadcast,
+and that a failing data check still leaves the failing command's outputs and
+everything after it untouched."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+class Plugin:
+    """A plug-in context with host-side storage bookkeeping (the reference's
+    backend layer holds it), F32 storages and arbitrary views."""
+
+    def __init__(self, m3):
+        self.m3 = m3
+        self.lib = m3.load()
+        self.storages = {}
+        self.sizes = {}
+        self.err = m3.M3Error()
+
+        @m3.STORAGE_DATA
+        def storage_data(storage):
+            return self.storages[storage]
+
+        self._keep = storage_data
+        options = m3.BackendOptions(0, storage_data, False)
+        self.context = ctypes.c_void_p()
+        m3.check(self.lib.m3_cuda_backend_context_create(
+            ctypes.byref(options), ctypes.byref(self.context), ctypes.byref(self.err)), self.err)
+
+    def tensor(self, array):
+        array = np.ascontiguousarray(array)
+        handle, data = ctypes.c_void_p(), ctypes.c_void_p()
+        self.m3.check(self.lib.m3_cuda_backend_allocate(
+            self.context, max(array.nbytes, 4), 256, ctypes.byref(handle), ctypes.byref(data),
+            ctypes.byref(self.err)), self.err)
+        key = len(self.storages) + 1
+        self.storages[key] = data.value
+        self.sizes[key] = array.nbytes
+        self.write(key, array)
+        return key
+
+    def write(self, key, array):
+        array = np.ascontiguousarray(array)
+        self.m3.check(self.lib.m3_cuda_backend_write(
+            self.context, self.storages[key], 0, array.ctypes.data, array.nbytes,
+            ctypes.byref(self.err)), self.err)
+
+    def read(self, key, dtype=np.float32):
+        host = np.zeros(self.sizes[key] // np.dtype(dtype).itemsize, dtype)
+        self.m3.check(self.lib.m3_cuda_backend_read(
+            self.context, self.storages[key], 0, host.ctypes.data, host.nbytes,
+            ctypes.byref(self.err)), self.err)
+        return host
+
+    def view(self, key, shape, offset=0, strides=None, dtype=None, item=4):
+        """A view of `shape` at element `offset`; `strides` in elements
+        (default: row-major contiguous)."""
+        v = self.m3.TensorView()
+        v.metadata.dtype = self.m3.F32 if dtype is None else dtype
+        v.metadata.rank = len(shape)
+        if strides is None:
+            strides, step = [], 1
+            for n in reversed(shape):
+                strides.insert(0, step)
+                step *= n
+        for i, n in enumerate(shape):
+            v.metadata.shape[i] = n
+            v.byte_strides[i] = strides[i] * item
+        count = int(np.prod(shape))
+        v.metadata.element_count = count
+        v.metadata.byte_count = count * item
+        v.byte_offset = offset * item
+        v.storage = key
+        return v
+
+    def execute(self, commands):
+        """commands: (kind, fields) with fields a dict of descriptor members."""
+        cmd = (self.m3.Command * len(commands))()
+        keep = []
+        for i, (kind, member, fields) in enumerate(commands):
+            cmd[i].kind = self.m3.OPS[kind]
+            desc = getattr(cmd[i].descriptor, member)
+            for name, value in fields.items():
+                if isinstance(value, int):
+                    setattr(desc, name, value)
+                else:
+                    keep.append(value)
+                    setattr(desc, name, ctypes.pointer(value))
+        status = self.lib.m3_cuda_backend_execute(self.context, cmd, len(commands), None,
+                                                  ctypes.byref(self.err))
+        return status, self.err.message.decode() if status != self.m3.OK else ""
+
+    def launches(self):
+        return self.lib.m3_cuda_backend_launch_count(self.context)
+
+    def close(self):
+        for key in list(self.storages):
+            self.lib.m3_cuda_backend_free_storage(self.context, self.storages[key],
+                                                  self.storages[key])
+        self.lib.m3_cuda_backend_destroy_context(self.context)
+
+
+def binary(kind, left, right, out):
+    return (kind, "add", {"left": left, "right": right, "output": out})
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.fixture
+def plugin(m3, gpu):
+    p = Plugin(m3)
+    yield p
+    p.close()
+
+
+def test_c1_chain_is_one_launch(m3, plugin):
+    """y = (x * c) + b as the reference issues it (MUL into a temporary, ADD
+    from it), c and b broadcast over rows: one launch, both outputs written,
+    bit-exact with the F32 statements."""
+    rng = np.random.default_rng(5)
+    rows, width = 64, 4096
+    x = rng.uniform(-1, 1, (rows, width)).astype(np.float32)
+    c = rng.uniform(0.5, 2, width).astype(np.float32)
+    b = rng.standard_normal(width).astype(np.float32)
+    kx, kc, kb = plugin.tensor(x), plugin.tensor(c), plugin.tensor(b)
+    kt, ky = plugin.tensor(np.zeros_like(x)), plugin.tensor(np.zeros_like(x))
+    status, message = plugin.execute([
+        binary("MUL", plugin.view(kx, (rows, width)), plugin.view(kc, (width,)),
+               plugin.view(kt, (rows, width))),
+        binary("ADD", plugin.view(kt, (rows, width)), plugin.view(kb, (1, width)),
+               plugin.view(ky, (rows, width))),
+    ])
+    assert status == m3.OK, message
+    assert plugin.launches() == 1
+    t = x * c
+    assert np.array_equal(bits(plugin.read(kt)), bits(t.ravel()))
+    assert np.array_equal(bits(plugin.read(ky)), bits((t + b).ravel()))
+
+
+def _emulate(buffers, commands):
+    """The reference's order: each command reads memory, then writes it."""
+    import numpy.lib.stride_tricks as st
+
+    for kind, (lk, lshape, loff, lstr), (rk, rshape, roff, rstr), (ok, oshape, ooff) in commands:
+        def read(key, shape, off, strides):
+            base = buffers[key]
+            itemsz = base.itemsize
+            v = st.as_strided(base[off:], shape=shape, strides=[s * itemsz for s in strides])
+            return np.broadcast_to(v.copy(), oshape)
+
+        a = read(lk, lshape, loff, lstr)
+        if kind == "COPY":
+            result = a.copy()
+        else:
+            b = read(rk, rshape, roff, rstr)
+            result = a + b if kind == "ADD" else a * b
+        count = int(np.prod(oshape))
+        buffers[ok][ooff:ooff + count] = result.astype(np.float32).ravel()
+
+
+def test_random_aliasing_lists_match_command_order(m3, plugin):
+    """Random lists of ADD / MUL / COPY over three buffers whose views are
+    windows at row offsets (exact aliases, partial overlaps), row or scalar
+    broadcasts: every buffer equals the command-by-command result bit for
+    bit, whatever the plug-in merged."""
+    rng = np.random.default_rng(11)
+    rows, width, nbuf = 6, 32, 3
+    span = rows * width
+    size = span + 3 * width
+    checked = merged = 0
+    for trial in range(320):
+        init = [rng.standard_normal(size).astype(np.float32) for _ in range(nbuf)]
+        keys = [plugin.tensor(a) for a in init]
+        commands, spec = [], []
+        for _ in range(int(rng.integers(2, 6))):
+            kind = ["ADD", "MUL", "COPY"][int(rng.integers(0, 3))]
+            ins = []
+            for _side in range(2):
+                k = int(rng.integers(0, nbuf))
+                form = int(rng.integers(0, 4))
+                if form <= 1:         # a window at a row offset
+                    off = int(rng.integers(0, 4)) * width
+                    ins.append((k, (rows, width), off, (width, 1)))
+                elif form == 2:       # one row broadcast over the rows
+                    off = int(rng.integers(0, rows)) * width
+                    ins.append((k, (rows, width), off, (0, 1)))
+                else:                 # one element broadcast everywhere
+                    off = int(rng.integers(0, span))
+                    ins.append((k, (rows, width), off, (0, 0)))
+            ko = int(rng.integers(0, nbuf))
+            oo = int(rng.integers(0, 4)) * width
+            spec.append((kind, ins[0], ins[1], (ko, (rows, width), oo)))
+            left = plugin.view(keys[ins[0][0]], ins[0][1], ins[0][2], list(ins[0][3]))
+            right = plugin.view(keys[ins[1][0]], ins[1][1], ins[1][2], list(ins[1][3]))
+            out = plugin.view(keys[ko], (rows, width), oo)
+            if kind == "COPY":
+                commands.append(("COPY", "copy", {"input": left, "output": out}))
+            else:
+                commands.append(binary(kind, left, right, out))
+        status, _ = plugin.execute(commands)
+        if status == m3.OK:
+            expect = [a.copy() for a in init]
+            _emulate(expect, spec)
+            for k, e in zip(keys, expect):
+                assert np.array_equal(bits(plugin.read(k)), bits(e)), (trial, spec)
+            checked += 1
+            merged += plugin.launches() < len(commands)
+        else:
+            # the reference rejects a command whose output overlaps its own
+            # input in part; nothing may have been written
+            for k, a in zip(keys, init):
+                assert np.array_equal(bits(plugin.read(k)), bits(a))
+        for k in keys:
+            plugin.lib.m3_cuda_backend_free_storage(plugin.context, plugin.storages[k],
+                                                    plugin.storages[k])
+            del plugin.storages[k]
+    assert checked >= 50 and merged >= 20, (checked, merged)
+
+
+def _row_commands(plugin, kx, rows, width, kp, kv, ki, ks, order):
+    x = plugin.view(kx, (rows, width))
+    parts = {
+        "SOFTMAX": ("SOFTMAX", "softmax", {"input": x, "output": plugin.view(kp, (rows, width))}),
+        "TOP_K": ("TOP_K", "top_k", {"logits": x, "values": plugin.view(kv, (rows, 1)),
+                                     "indices": plugin.view(ki, (rows, 1), dtype=plugin.m3.I32),
+                                     "k": 1}),
+        "ROW_SUM": ("ROW_SUM", "copy", {"input": x, "output": plugin.view(ks, (rows, 1))}),
+    }
+    return [parts[name] for name in order]
+
+
+@pytest.mark.parametrize("rows,width", [(4096, 1024), (37, 300)])
+def test_softmax_topk_rowsum_share_one_pass(m3, plugin, rows, width):
+    """SOFTMAX, TOP_K and ROW_SUM of one input in one list: one NaN scan and
+    one row pass, every output equal to running the commands one list each."""
+    rng = np.random.default_rng(rows)
+    x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
+    kx = plugin.tensor(x)
+    outs = [plugin.tensor(np.zeros(n, np.float32)) for n in (rows * width, rows, rows, rows)]
+    order = ["SOFTMAX", "TOP_K", "ROW_SUM"]
+    status, message = plugin.execute(_row_commands(plugin, kx, rows, width, *outs, order))
+    assert status == m3.OK, message
+    assert plugin.launches() == 2
+    fused = [plugin.read(k) for k in outs]
+    alone = [plugin.tensor(np.zeros(n, np.float32)) for n in (rows * width, rows, rows, rows)]
+    for name in order:
+        status, message = plugin.execute(_row_commands(plugin, kx, rows, width, *alone, [name]))
+        assert status == m3.OK, message
+    for got, k in zip(fused, alone):
+        assert np.array_equal(bits(got), bits(plugin.read(k)))
+
+
+def test_fused_rows_fail_atomically_and_in_command_order(m3, plugin):
+    """A NaN in the input: SOFTMAX and TOP_K, merged, both stay untouched with
+    the reference's message; a ROW_SUM listed before them is written first,
+    as the reference's command-by-command order does."""
+    rows, width = 64, 1024
+    x = np.ones((rows, width), np.float32)
+    x[40, 3] = np.nan
+    kx = plugin.tensor(x)
+    sentinel = np.float32(-7.0)
+    outs = [plugin.tensor(np.full(n, sentinel, np.float32)) for n in (rows * width, rows, rows, rows)]
+    status, message = plugin.execute(
+        _row_commands(plugin, kx, rows, width, *outs, ["SOFTMAX", "TOP_K", "ROW_SUM"]))
+    assert status == m3.OUT_OF_RANGE and message == "softmax input contains NaN"
+    for k in outs:
+        assert (plugin.read(k) == sentinel).all()
+    status, message = plugin.execute(
+        _row_commands(plugin, kx, rows, width, *outs, ["ROW_SUM", "TOP_K", "SOFTMAX"]))
+    assert status == m3.OUT_OF_RANGE and message == "top-k logits contain NaN"
+    sums = plugin.read(outs[3])
+    assert sums[0] == np.float32(width) and np.isnan(sums[40])
+    for k in outs[:3]:
+        assert (plugin.read(k) == sentinel).all()
