@@ -7,7 +7,10 @@ Headline workload (`--config`, default c5): BASELINE.json's largest
 configuration, the vocoder activation on stereo F32 [2,512,1572864] (snake,
 global abs-max, clamp), 12.9 GB per run.  Every other configuration (c1-c4)
 is measured the same way in the same run and reported under `per_config`,
-each with its own value, roofline, CPU baseline and end-to-end figure.
+each with its own value, roofline, CPU baseline and end-to-end figure.  At
+N=1, `per_config` also holds C1 and C2 through the reference-facing backend
+plug-in (`c1_plugin`, `c2_plugin`: m3_cuda_backend_execute on the command
+lists the reference's scheduler issues).
 
 One step = one session run over one batch (C4: its 30 carried Euler runs).
 With N ranks (torchrun, one process per GPU) every configuration's FIXED
@@ -890,6 +893,108 @@ def measure_cuda(m3, torch, dist, env, config, args, stream, flush, with_baselin
             "elems_per_s": config.elements(args.scale) / (ms_per_step / 1e3)}
 
 
+def measure_plugin(m3, torch, env, stream, flush, args):
+    """C1 and C2 as the reference's scheduler hands them to the backend
+    plug-in (m3_cuda_backend_execute, the vtable call of
+    src/m3_backend.c:113-154): C1's MUL into a temporary then ADD, C2's
+    SOFTMAX then TOP_K, over device storages.  The context runs on the bench
+    stream (m3_cuda_backend_set_stream), so CUDA events time each call; a
+    call returns after its stream is idle, as the vtable requires.  `value`
+    uses the session path's algorithmic bytes, so the two compare directly;
+    the plug-in also writes C1's temporary (no liveness reaches a backend) and
+    scans C2's input for NaN before its row pass."""
+    lib = m3.load()
+    tensors = {}
+    # storages are the tensors' device addresses, resolved by a C accessor
+    # (as the reference's m3_storage_data is C): no Python in the call
+    storage_data = ctypes.cast(lib.m3_cuda_storage_is_address, m3.STORAGE_DATA)
+
+    err = m3.M3Error()
+    context = ctypes.c_void_p()
+    options = m3.BackendOptions(env.local, storage_data, False)
+    m3.check(lib.m3_cuda_backend_context_create(ctypes.byref(options), ctypes.byref(context),
+                                                ctypes.byref(err)), err)
+    m3.check(lib.m3_cuda_backend_set_stream(context, stream.cuda_stream, ctypes.byref(err)), err)
+    views = []
+
+    def view(key, shape, dtype=m3.F32):
+        v = m3.TensorView()
+        v.metadata.dtype = dtype
+        v.metadata.rank = len(shape)
+        step = 4
+        for axis in reversed(range(len(shape))):
+            v.metadata.shape[axis] = shape[axis]
+            v.byte_strides[axis] = step
+            step *= shape[axis]
+        v.metadata.element_count = int(np.prod(shape))
+        v.metadata.byte_count = v.metadata.element_count * 4
+        v.storage = tensors[key].data_ptr()
+        views.append(v)
+        return ctypes.pointer(v)
+
+    results = {}
+    try:
+        for name in ("c1", "c2"):
+            config = CONFIGS[name]
+            rows, width = config.shape(args.scale)
+            x = config.inputs_device(m3, torch, env.device, args.scale)["x"]
+            cmd = (m3.Command * 2)()
+            if name == "c1":
+                rng = ProductRng(m3)
+                c = torch.from_numpy(rng.uniform(0, 1, 0.5, 2.0, width)).to(env.device)
+                b = torch.from_numpy(rng.normal(0, 2, 0.0, 1.0, width)).to(env.device)
+                tensors.clear()
+                tensors.update({1: x, 2: c, 3: b, 4: torch.empty_like(x), 5: torch.empty_like(x)})
+                cmd[0].kind, cmd[1].kind = m3.OPS["MUL"], m3.OPS["ADD"]
+                cmd[0].descriptor.mul.left = view(1, (rows, width))
+                cmd[0].descriptor.mul.right = view(2, (width,))
+                cmd[0].descriptor.mul.output = view(4, (rows, width))
+                cmd[1].descriptor.add.left = view(4, (rows, width))
+                cmd[1].descriptor.add.right = view(3, (1, width))
+                cmd[1].descriptor.add.output = view(5, (rows, width))
+            else:
+                tensors.clear()
+                tensors.update({1: x, 2: torch.empty_like(x),
+                                3: torch.empty(rows, dtype=torch.float32, device=env.device),
+                                4: torch.empty(rows, dtype=torch.int32, device=env.device)})
+                cmd[0].kind, cmd[1].kind = m3.OPS["SOFTMAX"], m3.OPS["TOP_K"]
+                cmd[0].descriptor.softmax.input = view(1, (rows, width))
+                cmd[0].descriptor.softmax.output = view(2, (rows, width))
+                cmd[1].descriptor.top_k.logits = view(1, (rows, width))
+                cmd[1].descriptor.top_k.values = view(3, (rows, 1))
+                cmd[1].descriptor.top_k.indices = view(4, (rows, 1), m3.I32)
+                cmd[1].descriptor.top_k.k = 1
+            torch.cuda.synchronize(env.device)
+
+            def call():
+                m3.check(lib.m3_cuda_backend_execute(context, cmd, 2, None, ctypes.byref(err)), err)
+
+            for _ in range(args.warmup):
+                flush()
+                call()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            for i in range(args.steps):
+                flush()
+                starts[i].record(stream)
+                call()
+                ends[i].record(stream)
+            torch.cuda.synchronize(env.device)
+            ms = sum(a.elapsed_time(e) for a, e in zip(starts, ends)) / args.steps
+            launches = int(lib.m3_cuda_backend_launch_count(context))
+            results[name + "_plugin"] = {
+                "workload": config.workload + " through m3_cuda_backend_execute",
+                "value": config.algorithmic_bytes(args.scale) / (ms / 1e3) / 1e9,
+                "unit": "GB/s", "ms_per_step": ms, "dtype": config.dtype,
+                "launches_per_call": launches, "gpu_launches": launches * args.steps,
+                "timing": "CUDA events on the bench stream around each call; L2 evicted between calls",
+                "bytes": "the session path's algorithmic bytes"}
+    finally:
+        lib.m3_cuda_backend_destroy_context(context)
+        tensors.clear()
+    return results
+
+
 def time_c3_gsilu(m3, torch, env, stream, flush, steps, scale):
     """C3's dominant kernel (the gated-SiLU launch, this rank's rows), timed
     alone."""
@@ -1046,6 +1151,8 @@ def main():
             if name != headline.name:
                 per_config[name] = measure_cuda(m3, torch, dist, env, config, args, stream, flush,
                                                 baseline_here)
+        if env.world == 1:
+            per_config.update(measure_plugin(m3, torch, env, stream, flush, args))
     launches = result["gpu_launches"] + sum(r["gpu_launches"] for r in per_config.values())
     config = config_dict(headline, env.world)
     if args.scale != 1.0:

@@ -751,6 +751,16 @@ bool m3_cuda_backend_supports_kind(m3_op_kind kind);
  * commands over one output shape, and SOFTMAX / TOP_K / ROW_SUM commands over
  * one input view, share a launch where that cannot change a result. */
 unsigned m3_cuda_backend_launch_count(const void *context);
+/* Run this context's executes on a caller's cudaStream_t (NULL: the stream
+ * the context created), e.g. one shared with a framework or timed with
+ * events; no reference counterpart.  Waits for work already queued on the
+ * previous stream.  execute still returns after the stream is idle. */
+m3_status m3_cuda_backend_set_stream(void *context, void *stream, m3_error *error);
+/* A storage accessor for hosts whose storage handles are the device
+ * addresses themselves (pass it as m3_cuda_backend_options.storage_data);
+ * no reference counterpart: the reference's own accessor is
+ * m3_storage_data. */
+void *m3_cuda_storage_is_address(m3_storage *storage);
 
 /* ------------------------------------------------------------------------
  * Seeded synthetic inputs (reference src/m3_rng.c:9-110)

@@ -38,6 +38,8 @@ typedef struct {
     size_t gather_bytes;
     /* kernels launched by the last execute */
     unsigned launches;
+    /* the stream created with the context; `stream` may be a caller's */
+    cudaStream_t own_stream;
 } cuda_backend;
 
 static const m3c_status clean = {UINT32_MAX, 0U, 0U, UINT32_MAX};
@@ -84,7 +86,8 @@ m3_status m3_cuda_backend_context_create(
     b->managed = options->managed_memory;
     code = cudaSetDevice(b->device);
     if (code == cudaSuccess) {
-        code = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+        code = cudaStreamCreateWithFlags(&b->own_stream, cudaStreamNonBlocking);
+        b->stream = b->own_stream;
     }
     if (code == cudaSuccess) {
         code = cudaMalloc((void **)&b->status, sizeof(m3c_status));
@@ -121,7 +124,10 @@ void m3_cuda_backend_destroy_context(void *context)
     (void)cudaSetDevice(b->device);
     if (b->stream != NULL) {
         (void)cudaStreamSynchronize(b->stream);
-        (void)cudaStreamDestroy(b->stream);
+    }
+    if (b->own_stream != NULL) {
+        (void)cudaStreamSynchronize(b->own_stream);
+        (void)cudaStreamDestroy(b->own_stream);
     }
     (void)cudaFree(b->status);
     (void)cudaFree(b->reduce);
@@ -433,6 +439,17 @@ static int dense_input(cuda_backend *b, const m3_tensor_view *view,
     return result;
 }
 
+/* The NaN check of a SOFTMAX / TOP_K input (dense rows), recorded against
+ * `command`, visiting the rows in the reverse of the order the row pass
+ * `p` reads them, so that its first reads hit L2. */
+static int scan_rows(cuda_backend *b, const m3c_softmax_params *p, uint32_t command)
+{
+    ++b->launches;
+    return m3c_launch_row_scan(p->input, p->in_dtype, p->rows, p->width,
+                               m3c_softmax_row_ranges(p), 0, command, b->status,
+                               b->stream);
+}
+
 static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
                        void **temporary)
 {
@@ -514,12 +531,6 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
         const void *data;
 
         code = dense_input(b, in, index, &data, temporary);
-        if (code == 0) {
-            ++b->launches;
-            code = m3c_launch_scan(data, (int32_t)in->metadata.dtype,
-                                   in->metadata.element_count, 0, index,
-                                   b->status, b->stream);
-        }
         if (code != 0) {
             return code;
         }
@@ -545,6 +556,10 @@ static int run_command(cuda_backend *b, const m3_command *c, uint32_t index,
                             c->descriptor.top_k.indices->byte_offset);
             p.k = c->descriptor.top_k.k;
             p.topk_command = index;
+        }
+        code = scan_rows(b, &p, index);
+        if (code != 0) {
+            return code;
         }
         ++b->launches;
         return m3c_launch_softmax(&p, b->stream);
@@ -1101,13 +1116,6 @@ static int fuse_rows(cuda_backend *b, const m3_command *commands, size_t first,
     if (code != 0) {
         return code;
     }
-    /* the NaN check, reported against the group's first (checked) command */
-    ++b->launches;
-    code = m3c_launch_scan(data, (int32_t)in->metadata.dtype, in->metadata.element_count, 0,
-                           (uint32_t)first, b->status, b->stream);
-    if (code != 0) {
-        return code;
-    }
     memset(&p, 0, sizeof(p));
     p.input = data;
     p.in_dtype = (int32_t)in->metadata.dtype;
@@ -1138,6 +1146,11 @@ static int fuse_rows(cuda_backend *b, const m3_command *commands, size_t first,
 
         p.row_sums = (float *)(view_base(b, out) + out->byte_offset);
         p.rowsum_command = (uint32_t)rowsum;
+    }
+    /* the NaN check, reported against the group's first (checked) command */
+    code = scan_rows(b, &p, (uint32_t)first);
+    if (code != 0) {
+        return code;
     }
     *count = n;
     ++b->launches;
@@ -1248,4 +1261,29 @@ unsigned m3_cuda_backend_launch_count(const void *context)
     const cuda_backend *b = context;
 
     return b == NULL ? 0U : b->launches;
+}
+
+m3_status m3_cuda_backend_set_stream(void *context, void *stream, m3_error *error)
+{
+    cuda_backend *b = context;
+    cudaError_t code;
+
+    if (b == NULL) {
+        return m3c_error_set(error, M3_STATUS_INVALID_ARGUMENT,
+                             "backend context is required");
+    }
+    (void)cudaSetDevice(b->device);
+    /* work already queued on the old stream finishes first */
+    code = cudaStreamSynchronize(b->stream);
+    if (code != cudaSuccess) {
+        return fail_cuda(error, code, "cannot switch the backend stream");
+    }
+    b->stream = stream != NULL ? (cudaStream_t)stream : b->own_stream;
+    m3_error_reset(error);
+    return M3_STATUS_OK;
+}
+
+void *m3_cuda_storage_is_address(m3_storage *storage)
+{
+    return (void *)storage;
 }

@@ -1277,6 +1277,8 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(const __grid_constant__ m3c
 
 #define E op_code
 #define OPS_MUL_ADD_F32 E(M3C_OP_MUL, 0, 0, 1, 0, 0), E(M3C_OP_ADD, 0, 0, 2, 0, 0)
+// the same chain merged by the backend plug-in, which keeps the temporary
+#define OPS_MUL_ADD_F32_KEEP E(M3C_OP_MUL, 3, 0, 1, 0, 0), E(M3C_OP_ADD, 4, 3, 2, 0, 0)
 #define OPS_CFG_EULER_BF16                                                           \
     E(M3C_OP_MUL, 1, 0, 1, 0, 0), E(M3C_OP_ADD, 1, 2, 1, 0, 0), E(M3C_OP_MUL, 1, 1, 3, 0, 0), \
         E(M3C_OP_ADD, 0, 0, 1, 0, 0), E(M3C_OP_MUL, 0, 0, 4, 0, 0), E(M3C_OP_ADD, 0, 5, 0, 0, 0), \
@@ -1338,6 +1340,8 @@ constexpr uint64_t output_sig(std::initializer_list<uint32_t> bytes)
 // behind them take any addressing.
 #define M3C_PROGRAMS(X)                                                                 \
     X(3, (operand_sig({C32, V32_1, V32_1})), (output_sig({OUT(0, M3C_F32)})), OPS_MUL_ADD_F32) \
+    X(3, (operand_sig({C32, V32_1, V32_1})), (output_sig({OUT(3, M3C_F32), OUT(4, M3C_F32)})),   \
+      OPS_MUL_ADD_F32_KEEP)                                                             \
     X(6, (operand_sig({C32, I32C, C32, I32C, I32C, C32})),                                \
       (output_sig({OUT(0, M3C_F32), OUT(1, M3C_BF16)})), OPS_CFG_EULER_BF16)             \
     X(2, (operand_sig({C32, C32})), (output_sig({OUT(0, M3C_F32)})), OPS_GSILU_F32)        \

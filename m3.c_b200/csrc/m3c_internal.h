@@ -189,6 +189,14 @@ int m3c_launch_norm(const m3c_norm_params *params, void *stream);
 /* mode 0: NaN check; mode 1: float-to-I32 range check (contiguous data) */
 int m3c_launch_scan(const void *data, int32_t dtype, uint64_t count, int mode,
                     uint32_t command, m3c_status *status, void *stream);
+/* The same checks over `rows` rows of `width` elements, one warp per row,
+ * visiting the rows in the reverse of the order a row kernel reading
+ * `ranges` contiguous row ranges side by side consumes them (so they are
+ * still in L2 when it does); falls back to m3c_launch_scan for rows that are
+ * not whole 16-byte vectors. */
+int m3c_launch_row_scan(const void *data, int32_t dtype, uint64_t rows, uint64_t width,
+                        uint32_t ranges, int mode, uint32_t command, m3c_status *status,
+                        void *stream);
 int m3c_launch_rng_uniform(uint64_t seed, uint64_t sequence, float low,
                            float high, float *out, uint64_t count,
                            void *stream);

@@ -220,6 +220,10 @@ int m3c_launch_categorical(const m3c_categorical_params *params, void *stream);
  * 512 or 1024 elements (m3c_ring.cu); -1 when it does not apply. */
 int m3c_launch_softmax_ring(const m3c_softmax_params *params, void *stream);
 
+/* The number of contiguous row ranges the row pass for `params` reads side
+ * by side (1: ascending order). */
+uint32_t m3c_softmax_row_ranges(const m3c_softmax_params *params);
+
 /* The words a sharded session's ranks agree on after each run: the bit
  * patterns of its global reductions (ABS_MAX outputs) and the complement of
  * the first failing command, all combined by one MAX all-reduce. */

@@ -450,12 +450,33 @@ int launch_ring(const m3c_softmax_params &p, void *stream)
 // F32 rows of 512 or 1024 elements, k <= 1, not both probabilities and row
 // sums (the chain warp sums e for SOFTMAX, x for ROW_SUM alone); -1 when the
 // pipeline does not apply.
+static bool ring_applies(const m3c_softmax_params *p)
+{
+    return p->in_dtype == M3C_F32 && p->k <= 1 && (p->probs == nullptr || p->row_sums == nullptr) &&
+           (p->width == 1024 || p->width == 512) && (reinterpret_cast<uintptr_t>(p->input) & 15u) == 0u &&
+           (p->probs == nullptr || (reinterpret_cast<uintptr_t>(p->probs) & 15u) == 0u);
+}
+
+// The contiguous row ranges the row pass for `p` reads side by side: the
+// pipeline's CTAs (one range each), else 1 (the tile kernels take tiles in
+// ascending order).
+extern "C" uint32_t m3c_softmax_row_ranges(const m3c_softmax_params *p)
+{
+    if (!ring_applies(p) || p->rows == 0) return 1u;
+    int device = 0;
+    int sms = 0;
+    cudaGetDevice(&device);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) {
+        (void)cudaGetLastError();
+        sms = 148;
+    }
+    const uint64_t grid = (p->rows + m3c::CHAIN_LANES - 1) / m3c::CHAIN_LANES;
+    return static_cast<uint32_t>(grid < static_cast<uint64_t>(sms) ? grid : static_cast<uint64_t>(sms));
+}
+
 extern "C" int m3c_launch_softmax_ring(const m3c_softmax_params *p, void *stream)
 {
-    if (p->in_dtype != M3C_F32 || p->k > 1 || (p->probs != nullptr && p->row_sums != nullptr) ||
-        (p->width != 1024 && p->width != 512) ||
-        (reinterpret_cast<uintptr_t>(p->input) & 15u) != 0u ||
-        (p->probs != nullptr && (reinterpret_cast<uintptr_t>(p->probs) & 15u) != 0u)) {
+    if (!ring_applies(p)) {
         return -1;
     }
     const int out = p->probs == nullptr ? M3C_F32 : p->probs_dtype;

@@ -123,6 +123,78 @@ __global__ void scan_kernel(const void *data, int dtype, uint64_t count, int mod
     }
 }
 
+// The data checks of a row operator's input, one warp per row, 16-byte loads.
+// Rows are visited in the reverse of the order in which the row kernel that
+// follows reads them (it reads `ranges` contiguous row ranges side by side,
+// from their starts), so the rows it reads first are the ones still in L2.
+__device__ __forceinline__ bool vector_fails(const uint4 &q, int dtype, int mode)
+{
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (mode == 0) {
+        if (dtype == M3C_F32) {
+            bool nan = false;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) nan |= (w[t] & 0x7fffffffu) > 0x7f800000u;
+            return nan;
+        }
+        // a 16-bit magnitude m is a NaN when m + (0x3ff or 0x7f) carries
+        // into bit 15
+        const uint32_t add = dtype == M3C_F16 ? 0x03ff03ffu : 0x007f007fu;
+        uint32_t acc = 0u;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) acc |= (w[t] & 0x7fff7fffu) + add;
+        return (acc & 0x80008000u) != 0u;
+    }
+    bool bad = false;
+    if (dtype == M3C_F32) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float v = as_float(w[t]);
+            bad |= !(v >= -2147483648.0f && v < 2147483648.0f);
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float v = widen(dtype, (w[t >> 1] >> ((t & 1) * 16)) & 0xffffu);
+            bad |= !(v >= -2147483648.0f && v < 2147483648.0f);
+        }
+    }
+    return bad;
+}
+
+__global__ void row_scan_kernel(const uint4 *data, int dtype, uint64_t rows, uint32_t nvec, uint32_t ranges,
+                                int mode, uint32_t command, m3c_status *status)
+{
+    const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x / 32);
+    const uint64_t first = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const int lane = static_cast<int>(threadIdx.x % 32);
+    const uint64_t longest = (rows + ranges - 1) / ranges;
+    const uint64_t visits = longest * ranges;
+    bool bad = false;
+    for (uint64_t j = first; j < visits; j += warps) {
+        const uint64_t offset = longest - 1 - j / ranges;   // within a range, last first
+        const uint64_t range = j % ranges;
+        const uint64_t begin = rows * range / ranges;
+        const uint64_t end = rows * (range + 1) / ranges;
+        const uint64_t row = begin + offset;
+        if (row >= end) continue;
+        const uint4 *r = data + row * nvec;
+        for (uint32_t v = static_cast<uint32_t>(lane); v < nvec; v += 4u * 32u) {
+            uint4 q[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t e = v + static_cast<uint32_t>(k) * 32u;
+                q[k] = e < nvec ? __ldcg(r + e) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) bad |= vector_fails(q[k], dtype, mode);
+        }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) {
+        record_failure(status, command);
+    }
+}
+
 // Exhaustive agreement of the hardware-assisted codecs with the integer
 // restatement of the reference's encoders: every F32 bit pattern through
 // both F16 and BF16 narrowing, every F16 pattern through widening; and the
@@ -438,6 +510,27 @@ extern "C" int m3c_launch_rng_normal(uint64_t seed, uint64_t sequence, float mea
     const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
     m3c::normal_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(seed, sequence, mean,
                                                                               deviation, out, count);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int m3c_launch_scan(const void *data, int32_t dtype, uint64_t count, int mode,
+                               uint32_t command, m3c_status *status, void *stream);
+
+extern "C" int m3c_launch_row_scan(const void *data, int32_t dtype, uint64_t rows, uint64_t width,
+                                   uint32_t ranges, int mode, uint32_t command, m3c_status *status,
+                                   void *stream)
+{
+    const uint64_t eb = dtype == M3C_F32 || dtype == M3C_I32 ? 4u : 2u;
+    if (rows == 0 || width == 0) return 0;
+    if ((width * eb) % 16u != 0u || (reinterpret_cast<uintptr_t>(data) & 15u) != 0u || ranges == 0 ||
+        width * eb / 16u > 0xffffffffull) {
+        return m3c_launch_scan(data, dtype, rows * width, mode, command, status, stream);
+    }
+    const uint64_t blocks = (rows + 7u) / 8u;
+    const unsigned grid = static_cast<unsigned>(blocks < 148u * 8u ? blocks : 148u * 8u);
+    m3c::row_scan_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4 *>(data), dtype, rows, static_cast<uint32_t>(width * eb / 16u),
+        ranges < rows ? ranges : static_cast<uint32_t>(rows), mode, command, status);
     return static_cast<int>(cudaGetLastError());
 }
 

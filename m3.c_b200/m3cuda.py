@@ -347,6 +347,9 @@ _CUDA_SIGNATURES = {
         ctypes.c_size_t, ctypes.POINTER(M3Error)]),
     "m3_cuda_backend_supports_kind": (ctypes.c_bool, [ctypes.c_int]),
     "m3_cuda_backend_launch_count": (ctypes.c_uint, [ctypes.c_void_p]),
+    "m3_cuda_storage_is_address": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "m3_cuda_backend_set_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.POINTER(M3Error)]),
     "m3_cuda_fill_uniform_host": (ctypes.c_int, [
         ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float,
         ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(M3Error)]),
