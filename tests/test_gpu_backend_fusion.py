@@ -289,3 +289,75 @@ def test_fused_rows_fail_atomically_and_in_command_order(m3, plugin):
     assert sums[0] == np.float32(width) and np.isnan(sums[40])
     for k in outs[:3]:
         assert (plugin.read(k) == sentinel).all()
+
+
+def _reference_outputs(m3, ref, build, inputs):
+    """The reference's CPU provider on `build`'s graph."""
+    g = m3.Graph(lib=ref)
+    handles, outputs = build(g)
+    s = m3.Session(g, allow_metal=False, allow_neural_engine=False, cuda=False)
+    for name, vid in handles.items():
+        s.write(vid, inputs[name])
+    s.run()
+    out = [s.read(v).copy() for v in outputs]
+    s.close()
+    return out
+
+
+def test_vocoder_final_stage_in_command_order(m3, ref, plugin):
+    """The vocoder's final stage in the reference's command order
+    (src/m3_vocoder_decode.c:395-432): SNAKE1D into the activation buffer,
+    CONV1D into the mono waveform, TANH in place on it.  No convolution runs
+    on the GPU here, so the convolution is an opaque producer between two
+    plug-in lists: computed on the host and written into the device storage,
+    as the reference's m3_storage_write would.  The snake and the in-place
+    tanh match the reference's CPU provider on the same inputs (the tanh on
+    the same convolution output) within 2^-19, the bound of every
+    transcendental here."""
+    tol = 2.0 ** -19
+    rng = np.random.default_rng(395)
+    channels, length = 24, 3000
+    hidden = (rng.standard_normal((2, channels, length)) * 0.5).astype(np.float32)
+    alpha = rng.uniform(0.2, 2.0, (1, channels, 1)).astype(np.float32)
+    weight = (rng.standard_normal((channels, 7)) * 0.2).astype(np.float64)
+    kh, ka = plugin.tensor(hidden), plugin.tensor(alpha)
+    kact = plugin.tensor(np.zeros_like(hidden))
+    kmono = plugin.tensor(np.zeros((2, 1, length), np.float32))
+    status, message = plugin.execute([("SNAKE1D", "snake1d", {
+        "input": plugin.view(kh, hidden.shape), "alpha": plugin.view(ka, alpha.shape),
+        "output": plugin.view(kact, hidden.shape)})])
+    assert status == m3.OK, message
+    activated = plugin.read(kact).reshape(hidden.shape)
+
+    # the opaque producer: a 7-tap convolution, padding 3, to one channel
+    padded = np.pad(activated.astype(np.float64), ((0, 0), (0, 0), (3, 3)))
+    mono = np.zeros((2, 1, length))
+    for c in range(channels):
+        for k in range(7):
+            mono[:, 0, :] += weight[c, k] * padded[:, c, k:k + length]
+    mono = (mono * 0.25 + 0.01).astype(np.float32)
+    plugin.write(kmono, mono)
+    status, message = plugin.execute([("TANH", "tanh", {
+        "input": plugin.view(kmono, mono.shape), "output": plugin.view(kmono, mono.shape)})])
+    assert status == m3.OK, message
+    waveform = plugin.read(kmono).reshape(mono.shape)
+
+    def snake(g):
+        vx = g.value(m3.INPUT, m3.F32, hidden.shape)
+        va = g.value(m3.INPUT, m3.F32, alpha.shape)
+        z = g.inferred("SNAKE1D", [vx, va], m3.OUTPUT, m3.F32)
+        g.node("SNAKE1D", [vx, va], [z])
+        return {"x": vx, "a": va}, [z]
+
+    def tanh(g):
+        vx = g.value(m3.INPUT, m3.F32, mono.shape)
+        t = g.inferred("TANH", [vx], m3.OUTPUT, m3.F32)
+        g.node("TANH", [vx], [t])
+        return {"x": vx}, [t]
+
+    (want_act,) = _reference_outputs(m3, ref, snake, {"x": hidden, "a": alpha})
+    (want_wave,) = _reference_outputs(m3, ref, tanh, {"x": mono})
+    for got, want in ((activated, want_act), (waveform, want_wave)):
+        diff = np.abs(got.astype(np.float64) - want)
+        assert ((diff <= tol) | (diff <= tol * np.abs(want))).all(), diff.max()
+    assert np.abs(waveform).max() < 1.0 and np.abs(mono).max() > 0.5   # the tanh did work
