@@ -321,6 +321,11 @@ __device__ __forceinline__ void round_words(int rdtype, float (&f)[VEC], uint32_
 struct Flags {
     uint32_t fail_command;
     uint32_t max_bits;
+    // the snake's 1 / (alpha + eps) for the last alpha this thread saw: a
+    // channel spans many blocks, so the division runs once per channel change
+    uint32_t snake_alpha = 0u;
+    float snake_inverse = 0.0f;
+    bool snake_known = false;
 };
 
 __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, int valid,
@@ -367,7 +372,12 @@ __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, in
             // one channel per block (the common case): the reciprocal of
             // (alpha + eps) is the same statement for all four elements
             const float alpha = as_float(b[0]);
-            const float inverse = __fdiv_rn(1.0f, __fadd_rn(alpha, 0x1.12e0bep-30f));
+            if (!flags.snake_known || b[0] != flags.snake_alpha) {
+                flags.snake_known = true;
+                flags.snake_alpha = b[0];
+                flags.snake_inverse = __fdiv_rn(1.0f, __fadd_rn(alpha, 0x1.12e0bep-30f));
+            }
+            const float inverse = flags.snake_inverse;
             float angle[VEC];
 #pragma unroll
             for (int j = 0; j < VEC; ++j) angle[j] = __fmul_rn(alpha, as_float(a[j]));
