@@ -326,6 +326,12 @@ struct Flags {
     uint32_t snake_alpha = 0u;
     float snake_inverse = 0.0f;
     bool snake_known = false;
+    // the word of the program's first broadcast-per-block operand (a
+    // channel's alpha) and the element range [lo, hi) it covers: blocks in
+    // the range reuse it instead of dividing the index again
+    uint32_t uniform_lo = 0u;
+    uint32_t uniform_hi = 0u;
+    uint32_t uniform_word = 0u;
 };
 
 __device__ __forceinline__ void run_op(const m3c_ew_op &op, RegisterFile &rf, int valid,
@@ -627,14 +633,56 @@ __device__ __forceinline__ void load_operands(const m3c_ew_params &p, uint64_t f
 // flight), or all of them.
 enum LoadPass { LOAD_STREAMED, LOAD_CACHED, LOAD_ALL };
 
+// The index of a signature's first operand broadcast per block through at
+// least two dimensions (a per-channel scalar), or -1.
+__host__ __device__ constexpr int first_uniform(uint64_t opsig, int operands)
+{
+    for (int i = 0; i < operands && i < 8; ++i) {
+        const uint32_t sig = static_cast<uint32_t>((opsig >> (8 * i)) & 0xffu);
+        if (sig != 0xffu && (sig & 7u) == M3C_V_UNIFORM && ((sig >> 5) & 7u) >= 1u) return i;
+    }
+    return -1;
+}
+
+// A per-block broadcast operand through the thread's cache: its word holds
+// for the whole run of elements that share the index of dimension 1 when
+// dimension 0 (innermost) is broadcast (stride 0).
+template <uint32_t SIG>
+__device__ __forceinline__ void load_uniform_cached(const m3c_operand &op, uint64_t f, uint32_t (&out)[VEC],
+                                                    Flags &cache)
+{
+    const uint32_t g = static_cast<uint32_t>(f);
+    if (g - cache.uniform_lo >= cache.uniform_hi - cache.uniform_lo) {
+        load_block_c<SIG>(op, f, out);
+        cache.uniform_word = out[0];
+        if (op.stride[0] == 0) {
+            const uint32_t lo = fastdiv(g, op.fdiv[0]) * static_cast<uint32_t>(op.size[0]);
+            cache.uniform_lo = lo;
+            cache.uniform_hi = lo + static_cast<uint32_t>(op.size[0]);
+        } else {
+            cache.uniform_lo = cache.uniform_hi = 0u;
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) out[j] = cache.uniform_word;
+}
+
 template <class Prog, int I, LoadPass PASS>
-__device__ __forceinline__ void load_operand_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
+__device__ __forceinline__ void load_operand_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf,
+                                                  Flags *cache)
 {
     constexpr uint32_t sig = static_cast<uint32_t>((Prog::opsig >> (8 * I)) & 0xffu);
     constexpr bool streamed = sig != 0xffu && (sig & 7u) == M3C_V_CONTIG;
     if constexpr (PASS == LOAD_ALL || (PASS == LOAD_STREAMED) == streamed) {
         if constexpr (sig == 0xffu) {
             load_block<false>(p.operands[I], f, rf.w[I]);
+        } else if constexpr (I == first_uniform(Prog::opsig, Prog::operands)) {
+            if (cache != nullptr) {
+                load_uniform_cached<sig>(p.operands[I], f, rf.w[I], *cache);
+            } else {
+                load_block_c<sig>(p.operands[I], f, rf.w[I]);
+            }
         } else {
             load_block_c<sig>(p.operands[I], f, rf.w[I]);
         }
@@ -642,20 +690,22 @@ __device__ __forceinline__ void load_operand_full(const m3c_ew_params &p, uint64
 }
 
 template <class Prog, LoadPass PASS, int... I>
-__device__ __forceinline__ void load_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf,
+__device__ __forceinline__ void load_full(const m3c_ew_params &p, uint64_t f, RegisterFile &rf, Flags *cache,
                                           std::integer_sequence<int, I...>)
 {
-    (load_operand_full<Prog, I, PASS>(p, f, rf), ...);
+    (load_operand_full<Prog, I, PASS>(p, f, rf, cache), ...);
 }
 
 // The operands of a full block that a load pass covers: through the
 // program's signature when it has one (narrow index only), else the
-// run-time dispatch (which loads everything in the first pass).
+// run-time dispatch (which loads everything in the first pass).  `cache`
+// (the thread's Flags, or null) keeps the first per-block broadcast operand.
 template <class Prog, bool WIDE, LoadPass PASS>
-__device__ __forceinline__ void load_block_all(const m3c_ew_params &p, uint64_t f, RegisterFile &rf)
+__device__ __forceinline__ void load_block_all(const m3c_ew_params &p, uint64_t f, RegisterFile &rf,
+                                               Flags *cache = nullptr)
 {
     if constexpr (Prog::opsig != ANY_OPERANDS && !WIDE) {
-        load_full<Prog, PASS>(p, f, rf, std::make_integer_sequence<int, Prog::operands>{});
+        load_full<Prog, PASS>(p, f, rf, cache, std::make_integer_sequence<int, Prog::operands>{});
     } else if constexpr (PASS != LOAD_CACHED) {
         load_operands<WIDE, Prog::operands>(p, f, VEC, rf);
     }
@@ -730,7 +780,7 @@ __device__ __forceinline__ void program_loop(const m3c_ew_params &p, Flags &flag
             for (int u = 0; u < U; ++u) {
                 const uint64_t b = v + static_cast<uint64_t>(u) * threads;
                 if (b < blocks) {
-                    load_block_all<Prog, WIDE, LOAD_CACHED>(p, b * VEC, rf[u]);
+                    load_block_all<Prog, WIDE, LOAD_CACHED>(p, b * VEC, rf[u], &flags);
                     Prog::run(p, rf[u], VEC, flags);
                     store_block_all<Prog>(p, b * VEC, rf[u]);
                 }
