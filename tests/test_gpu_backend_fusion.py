@@ -361,3 +361,64 @@ def test_vocoder_final_stage_in_command_order(m3, ref, plugin):
         diff = np.abs(got.astype(np.float64) - want)
         assert ((diff <= tol) | (diff <= tol * np.abs(want))).all(), diff.max()
     assert np.abs(waveform).max() < 1.0 and np.abs(mono).max() > 0.5   # the tanh did work
+
+
+def test_caller_stream_and_address_storages(m3, gpu):
+    """A context on a caller's stream whose storage handles are device
+    addresses (m3_cuda_backend_set_stream, m3_cuda_storage_is_address): the
+    merged C1 chain computes the same bits as on the context's own stream,
+    and the call has finished when it returns."""
+    import torch
+
+    lib = m3.load()
+    err = m3.M3Error()
+    accessor = ctypes.cast(lib.m3_cuda_storage_is_address, m3.STORAGE_DATA)
+    context = ctypes.c_void_p()
+    m3.check(lib.m3_cuda_backend_context_create(
+        ctypes.byref(m3.BackendOptions(0, accessor, False)), ctypes.byref(context),
+        ctypes.byref(err)), err)
+    rows, width = 32, 256
+    rng = np.random.default_rng(8)
+    x = torch.from_numpy(rng.uniform(-1, 1, (rows, width)).astype(np.float32)).cuda()
+    c = torch.from_numpy(rng.uniform(0.5, 2, width).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(width).astype(np.float32)).cuda()
+    outs = {}
+    stream = torch.cuda.Stream()
+    try:
+        for name, handle in (("caller", stream.cuda_stream), ("own", None)):
+            m3.check(lib.m3_cuda_backend_set_stream(context, handle, ctypes.byref(err)), err)
+            t, y = torch.zeros_like(x), torch.zeros_like(x)
+            views = []
+
+            def view(tensor, shape):
+                v = m3.TensorView()
+                v.metadata.dtype = m3.F32
+                v.metadata.rank = len(shape)
+                step = 4
+                for axis in reversed(range(len(shape))):
+                    v.metadata.shape[axis] = shape[axis]
+                    v.byte_strides[axis] = step
+                    step *= shape[axis]
+                v.metadata.element_count = int(np.prod(shape))
+                v.metadata.byte_count = v.metadata.element_count * 4
+                v.storage = tensor.data_ptr()
+                views.append(v)
+                return ctypes.pointer(v)
+
+            cmd = (m3.Command * 2)()
+            cmd[0].kind, cmd[1].kind = m3.OPS["MUL"], m3.OPS["ADD"]
+            cmd[0].descriptor.mul.left = view(x, (rows, width))
+            cmd[0].descriptor.mul.right = view(c, (width,))
+            cmd[0].descriptor.mul.output = view(t, (rows, width))
+            cmd[1].descriptor.add.left = view(t, (rows, width))
+            cmd[1].descriptor.add.right = view(b, (1, width))
+            cmd[1].descriptor.add.output = view(y, (rows, width))
+            torch.cuda.synchronize()
+            m3.check(lib.m3_cuda_backend_execute(context, cmd, 2, None, ctypes.byref(err)), err)
+            assert lib.m3_cuda_backend_launch_count(context) == 1
+            outs[name] = y.cpu().numpy()    # no wait needed: execute has returned
+    finally:
+        lib.m3_cuda_backend_destroy_context(context)
+    want = x.cpu().numpy() * c.cpu().numpy() + b.cpu().numpy()
+    for got in outs.values():
+        assert np.array_equal(bits(got), bits(want))
